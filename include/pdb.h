@@ -1,0 +1,157 @@
+/*
+ * pdb.h -- C ABI of the pdum_dsl_b200 kernel library (sm_100a).
+ *
+ * The reference (pdum.dsl / pdum.tl) lowers the tile regions produced by its
+ * fusion templates through one Python entry point,
+ *     compile_tile(region, launch=(), prune=()) -> run(values)
+ * (conformance/triton_tile.py:662-698), which JIT-generates Triton source per
+ * region.  This library replaces that lowering for the templates on the hot
+ * path with fixed, hand-written CUDA kernels.  Each entry point below stands
+ * for one template row of the reference registry (packages/tensorlib/src/
+ * pdum/tl/fusion.py:762-868) and is what a reference-side binding (ctypes, a
+ * torch custom op, or a C caller) would call.
+ *
+ * Conventions shared by every entry point:
+ *   - all pointers are DEVICE pointers owned by the caller; the library never
+ *     allocates or frees caller memory (workspace, when needed, is sized by a
+ *     *_workspace_size query and passed in);
+ *   - sizes and strides are int64 element counts (not bytes);
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default);
+ *   - launches are asynchronous; the return value reports argument / launch
+ *     errors only.  Device-side bounded waits that expire set a flag that
+ *     pdb_check_error() reads back (PDB_ERR_TIMEOUT);
+ *   - calls are stateless and re-entrant; the only global state is a lazily
+ *     built, mutex-guarded per-device attribute cache.
+ */
+#ifndef PDB_H_
+#define PDB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum pdb_status {
+  PDB_OK = 0,
+  PDB_ERR_SHAPE = 1,        /* sizes / strides the kernel family cannot take   */
+  PDB_ERR_ALIGN = 2,        /* pointer or stride alignment (TMA: 16 B)         */
+  PDB_ERR_TIMEOUT = 3,      /* a bounded device wait expired (see check_error)  */
+  PDB_ERR_CUDA = 4,         /* a CUDA runtime / driver call failed              */
+  PDB_ERR_UNSUPPORTED = 5,  /* dtype / head-dim combination not built           */
+  PDB_ERR_ARG = 6           /* null descriptor or required pointer              */
+};
+
+enum pdb_dtype { PDB_F32 = 0, PDB_BF16 = 1 };
+
+/* ---- row-normalization: softmax over the last dim --------------------------
+ * Replaces the "row-normalization" template (fusion.py:371-400, :818-826) as
+ * lowered by compile_tile (triton_tile.py:662).  y[r, c] = exp(x[r,c] - max_c
+ * x[r,:]) / sum_c exp(...).  f32 in / f32 out. */
+typedef struct {
+  const float* x;
+  float* y;
+  int64_t rows, cols;
+  int64_t x_row_stride, y_row_stride; /* elements; the column stride is 1 */
+} pdb_rowsoftmax_desc;
+int pdb_rowsoftmax_f32(const pdb_rowsoftmax_desc* d, void* stream);
+
+/* ---- row-statistics: two-pass layernorm over the last dim -------------------
+ * Replaces the "row-statistics" template (fusion.py:403-443, :827-843;
+ * zoo_common.py:56-60): y = (x - mean) / sqrt(mean((x - mean)^2) + eps) *
+ * gamma + beta.  gamma / beta may be NULL (identity scale / zero shift). */
+typedef struct {
+  const float* x;
+  const float* gamma;
+  const float* beta;
+  float* y;
+  int64_t rows, cols;
+  int64_t x_row_stride, y_row_stride;
+  double eps;
+} pdb_layernorm_desc;
+int pdb_layernorm_f32(const pdb_layernorm_desc* d, void* stream);
+
+/* ---- flash attention ---------------------------------------------------------
+ * Replaces the "flash" template (fusion.py:480-615) and its widened rows
+ * (batch/head riders, score scale, no mask, GQA).  Logical shapes:
+ *   q [batch, heads_q,  seqlen_q, head_dim]     o [batch, heads_q, seqlen_q, head_dim_v]
+ *   k [batch, heads_kv, seqlen_k, head_dim]     v [batch, heads_kv, seqlen_k, head_dim_v]
+ * with heads_q = heads_kv * group (GQA: query head h reads KV head h / group).
+ * Strides are per (batch, head, row); the innermost (feature) stride is 1.
+ * Scores are scale * q.k; with `causal`, key s is visible to query row t iff
+ * s <= t + q_start (absolute coordinates: the reference's iota mask
+ * `le(iota(s), iota(t))`, dialect.py:1382-1383).  Optional per-row outputs
+ * (float32, [batch, heads_q, seqlen_q] contiguous):
+ *   lse = log(sum_s exp(score)),   m = max_s score,   den = sum_s exp(score - m)
+ * -- m / den are the template's artifact finals (fusion.py:611-613).
+ * dtype PDB_BF16: bf16 q/k/v/o, fp32 accumulate, tcgen05/TMEM tensor cores
+ * (head_dim, head_dim_v in {64, 128}).  dtype PDB_F32: f32 everything, ieee
+ * FMA path (any head_dim <= 128), the precision of the reference's f32
+ * column (triton_tile.py:684-690 refuses tf32). */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse; /* nullable */
+  float* m;   /* nullable */
+  float* den; /* nullable */
+  int64_t batch, heads_q, heads_kv, seqlen_q, seqlen_k, head_dim, head_dim_v;
+  int64_t q_stride[3], k_stride[3], v_stride[3], o_stride[3]; /* (b, h, row) */
+  int64_t q_start;
+  double scale;
+  int32_t causal;
+  int32_t dtype; /* enum pdb_dtype */
+} pdb_flash_desc;
+int pdb_flash_fwd(const pdb_flash_desc* d, void* stream);
+
+/* ---- flash attention backward ----------------------------------------------
+ * The joint forward+backward region that autodiff.grad builds from the naive
+ * attention region (autodiff.py:102-150) and plan_model carves
+ * (partition.py:586-607): given q, k, v, o, dO and the forward's lse,
+ *   P = exp(scale*q.k - lse),  D = rowsum(dO * o)        ("held-back D")
+ *   dV = P^T dO,  dS = P * (dO.V^T - D),  dQ = scale * dS K,  dK = scale * dS^T Q.
+ * dq/dk/dv share the layouts of q/k/v (GQA: dk/dv are summed over the group).
+ * Workspace (float32) holds D and the dQ accumulator; its size in bytes comes
+ * from pdb_flash_bwd_workspace_size.  If lse is NULL the kernel recomputes it
+ * (the "recompute" variant of the template); otherwise it is the forward's
+ * stored lse ("stored" variant). */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dout;
+  const float* lse; /* nullable: recompute */
+  void* dq;
+  void* dk;
+  void* dv;
+  void* workspace;
+  size_t workspace_bytes;
+  int64_t batch, heads_q, heads_kv, seqlen_q, seqlen_k, head_dim, head_dim_v;
+  int64_t q_stride[3], k_stride[3], v_stride[3], o_stride[3], do_stride[3];
+  int64_t dq_stride[3], dk_stride[3], dv_stride[3];
+  int64_t q_start;
+  double scale;
+  int32_t causal;
+  int32_t dtype;
+} pdb_flash_bwd_desc;
+size_t pdb_flash_bwd_workspace_size(const pdb_flash_bwd_desc* d);
+int pdb_flash_bwd(const pdb_flash_bwd_desc* d, void* stream);
+
+/* ---- status --------------------------------------------------------------------
+ * pdb_check_error synchronises `stream`, reads and clears the device error flag
+ * of the current device (set by bounded waits that expired) and returns
+ * PDB_ERR_TIMEOUT if it was set, PDB_ERR_CUDA on a CUDA error, else PDB_OK.
+ * pdb_last_error_string returns a thread-local description of the last non-OK
+ * status returned on this thread.  pdb_version returns a constant string that
+ * keys compiled kernels (the backend fingerprint, registry.py:56-70). */
+int pdb_check_error(void* stream);
+const char* pdb_last_error_string(void);
+const char* pdb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PDB_H_ */

@@ -1,0 +1,187 @@
+"""ctypes binding of the C ABI declared in ``include/pdb.h``.
+
+The library is the in-tree ``libpdb_sm100.so`` built by ``pdum_dsl_b200.build``.
+There is no fallback: if the library is missing or fails to load, every
+entry point raises ``BackendUnavailable``.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libpdb_sm100.so"
+
+PDB_OK, PDB_ERR_SHAPE, PDB_ERR_ALIGN, PDB_ERR_TIMEOUT, PDB_ERR_CUDA, PDB_ERR_UNSUPPORTED, PDB_ERR_ARG = range(7)
+PDB_F32, PDB_BF16 = 0, 1
+
+STATUS_NAMES = {
+    PDB_OK: "PDB_OK",
+    PDB_ERR_SHAPE: "PDB_ERR_SHAPE",
+    PDB_ERR_ALIGN: "PDB_ERR_ALIGN",
+    PDB_ERR_TIMEOUT: "PDB_ERR_TIMEOUT",
+    PDB_ERR_CUDA: "PDB_ERR_CUDA",
+    PDB_ERR_UNSUPPORTED: "PDB_ERR_UNSUPPORTED",
+    PDB_ERR_ARG: "PDB_ERR_ARG",
+}
+
+# every symbol include/pdb.h declares
+EXPORTS = (
+    "pdb_rowsoftmax_f32",
+    "pdb_layernorm_f32",
+    "pdb_flash_fwd",
+    "pdb_flash_bwd",
+    "pdb_flash_bwd_workspace_size",
+    "pdb_check_error",
+    "pdb_last_error_string",
+    "pdb_version",
+)
+
+
+class BackendUnavailable(RuntimeError):
+    """The sm_100a kernel library is not built / not loadable."""
+
+
+class PdbError(RuntimeError):
+    """A non-OK status from the C ABI."""
+
+    def __init__(self, status: int, what: str, detail: str):
+        super().__init__(f"{what}: {STATUS_NAMES.get(status, status)}: {detail}")
+        self.status = status
+
+
+I64x3 = C.c_int64 * 3
+
+
+class RowSoftmaxDesc(C.Structure):
+    _fields_ = [
+        ("x", C.c_void_p),
+        ("y", C.c_void_p),
+        ("rows", C.c_int64),
+        ("cols", C.c_int64),
+        ("x_row_stride", C.c_int64),
+        ("y_row_stride", C.c_int64),
+    ]
+
+
+class LayerNormDesc(C.Structure):
+    _fields_ = [
+        ("x", C.c_void_p),
+        ("gamma", C.c_void_p),
+        ("beta", C.c_void_p),
+        ("y", C.c_void_p),
+        ("rows", C.c_int64),
+        ("cols", C.c_int64),
+        ("x_row_stride", C.c_int64),
+        ("y_row_stride", C.c_int64),
+        ("eps", C.c_double),
+    ]
+
+
+class FlashDesc(C.Structure):
+    _fields_ = [
+        ("q", C.c_void_p),
+        ("k", C.c_void_p),
+        ("v", C.c_void_p),
+        ("o", C.c_void_p),
+        ("lse", C.c_void_p),
+        ("m", C.c_void_p),
+        ("den", C.c_void_p),
+        ("batch", C.c_int64),
+        ("heads_q", C.c_int64),
+        ("heads_kv", C.c_int64),
+        ("seqlen_q", C.c_int64),
+        ("seqlen_k", C.c_int64),
+        ("head_dim", C.c_int64),
+        ("head_dim_v", C.c_int64),
+        ("q_stride", I64x3),
+        ("k_stride", I64x3),
+        ("v_stride", I64x3),
+        ("o_stride", I64x3),
+        ("q_start", C.c_int64),
+        ("scale", C.c_double),
+        ("causal", C.c_int32),
+        ("dtype", C.c_int32),
+    ]
+
+
+class FlashBwdDesc(C.Structure):
+    _fields_ = [
+        ("q", C.c_void_p),
+        ("k", C.c_void_p),
+        ("v", C.c_void_p),
+        ("o", C.c_void_p),
+        ("dout", C.c_void_p),
+        ("lse", C.c_void_p),
+        ("dq", C.c_void_p),
+        ("dk", C.c_void_p),
+        ("dv", C.c_void_p),
+        ("workspace", C.c_void_p),
+        ("workspace_bytes", C.c_size_t),
+        ("batch", C.c_int64),
+        ("heads_q", C.c_int64),
+        ("heads_kv", C.c_int64),
+        ("seqlen_q", C.c_int64),
+        ("seqlen_k", C.c_int64),
+        ("head_dim", C.c_int64),
+        ("head_dim_v", C.c_int64),
+        ("q_stride", I64x3),
+        ("k_stride", I64x3),
+        ("v_stride", I64x3),
+        ("o_stride", I64x3),
+        ("do_stride", I64x3),
+        ("dq_stride", I64x3),
+        ("dk_stride", I64x3),
+        ("dv_stride", I64x3),
+        ("q_start", C.c_int64),
+        ("scale", C.c_double),
+        ("causal", C.c_int32),
+        ("dtype", C.c_int32),
+    ]
+
+
+_LIB = None
+
+
+def load(path: Path | None = None) -> C.CDLL:
+    """Load (once) and type the library; raise BackendUnavailable if absent."""
+    global _LIB
+    if _LIB is not None and path is None:
+        return _LIB
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise BackendUnavailable(
+            f"{p.name} is not built: run `python -m pdum_dsl_b200.build` (nvcc, sm_100a); "
+            "there is no CPU or library fallback"
+        )
+    try:
+        lib = C.CDLL(str(p))
+    except OSError as e:  # pragma: no cover - depends on the host
+        raise BackendUnavailable(f"cannot load {p}: {e}") from e
+    vp = C.c_void_p
+    lib.pdb_rowsoftmax_f32.argtypes = [C.POINTER(RowSoftmaxDesc), vp]
+    lib.pdb_layernorm_f32.argtypes = [C.POINTER(LayerNormDesc), vp]
+    lib.pdb_flash_fwd.argtypes = [C.POINTER(FlashDesc), vp]
+    lib.pdb_flash_bwd.argtypes = [C.POINTER(FlashBwdDesc), vp]
+    lib.pdb_flash_bwd_workspace_size.argtypes = [C.POINTER(FlashBwdDesc)]
+    lib.pdb_flash_bwd_workspace_size.restype = C.c_size_t
+    lib.pdb_check_error.argtypes = [vp]
+    lib.pdb_last_error_string.restype = C.c_char_p
+    lib.pdb_version.restype = C.c_char_p
+    for name in EXPORTS:
+        f = getattr(lib, name)
+        if name not in ("pdb_flash_bwd_workspace_size", "pdb_last_error_string", "pdb_version"):
+            f.restype = C.c_int
+    if path is None:
+        _LIB = lib
+    return lib
+
+
+def check(status: int, what: str) -> None:
+    if status != PDB_OK:
+        detail = load().pdb_last_error_string().decode(errors="replace")
+        raise PdbError(status, what, detail)
+
+
+def version() -> str:
+    return load().pdb_version().decode()

@@ -1,0 +1,404 @@
+// bf16 flash-attention forward for sm_100a: TMA-staged tiles, tcgen05 MMAs
+// with TMEM accumulators, warp-specialised online softmax.
+//
+// What it computes is the reference's flash template (fusion.py:480-615):
+// the online-softmax fold over key tiles of the masked, scaled score
+// contraction, with the flashsm recurrence of zoo/attention.py:40-46, and
+// the causal tile bounds that _prune_flash derives (fusion.py:659-690,
+// hi = 1 + pid for BT = SI): key tiles past the diagonal are never visited.
+//
+// CTA = 256 query rows of one (batch, head), as two 128-row tiles A and B.
+//   warp 0        TMA producer (Q once; K/V tiles through 2-stage rings)
+//   warp 1        MMA issuer (one thread): S = Q K^T into TMEM, O += P V
+//                 with P read from TMEM (the "TS" form)
+//   warp 2        TMEM allocator
+//   warps 4..7    softmax for tile A, one thread per query row (TMEM lane)
+//   warps 8..11   softmax for tile B
+// TMEM (512 columns x 128 lanes x 32 bit): S_A [0,128) S_B [128,256)
+// O_A [256, 256+D) O_B [256+D, 256+2D).  P (bf16, packed in pairs)
+// overwrites the first 64 columns of its S tile.
+// Ping-pong: while softmax A works on S_A(j+1) the tensor core runs
+// PV_B(j) and S_B(j+1), and vice versa.
+//
+// Softmax is in the log2 domain (c = scale * log2 e) with lazy rescaling:
+// the running max used for the exponent only moves when a tile's max exceeds
+// it by more than 8 (a factor 256), so most tiles need no O correction; the
+// true max is tracked on the side for the m / den / lse outputs.
+#include <cfloat>
+
+#include "common.cuh"
+#include "tma.h"
+
+namespace pdb {
+namespace {
+
+constexpr int BM = 128;          // rows per tile (TMEM lanes)
+constexpr int BN = 128;          // keys per tile
+constexpr int kThreads = 384;    // 3 warpgroups
+constexpr int kBoxBytes = 64 * 128 * 2;  // one TMA box: 128 rows x 64 bf16 (128 B, swizzled)
+constexpr float kRescaleThreshold = 8.0f;
+
+struct __align__(8) Barriers {
+  uint64_t q_full;
+  uint64_t k_full[2], k_empty[2];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[2];  // MMA -> softmax (tile A, B)
+  uint64_t p_full[2];  // softmax -> MMA
+  uint64_t o_full[2];  // last PV done -> epilogue
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct FwdParams {
+  void* o;
+  float* lse;
+  float* m;
+  float* den;
+  int64_t o_stride[3];
+  int T, S, H, HKV, B;
+  int q_start;
+  int causal;
+  int num_mblocks;  // 256-row blocks per head
+  float scale_log2;  // scale * log2(e)
+  int* err;
+};
+
+template <int D>
+struct Smem {
+  static constexpr int kTileBytes = BM * D * 2;  // Q / K / V tile
+  static constexpr int kQ0 = 0;
+  static constexpr int kQ1 = kTileBytes;
+  static constexpr int kK = 2 * kTileBytes;  // 2 stages
+  static constexpr int kV = 4 * kTileBytes;  // 2 stages
+  static constexpr int kBar = 6 * kTileBytes;
+  static constexpr int kTotal = kBar + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+};
+
+template <int D>
+__device__ __forceinline__ void mma_qk(uint32_t d_tmem, uint32_t q_saddr, uint32_t k_saddr) {
+  constexpr uint32_t idesc = idesc_bf16(BM, BN, 0, 0);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+    mma_ss(d_tmem, sdesc_sw128(q_saddr + off, 16, 1024), sdesc_sw128(k_saddr + off, 16, 1024), idesc, kk > 0);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void mma_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_saddr, bool acc) {
+  constexpr uint32_t idesc = idesc_bf16(BM, D, 0, 1);
+#pragma unroll
+  for (int kk = 0; kk < BN / 16; ++kk) {
+    mma_ts(o_tmem, p_tmem + kk * 8, sdesc_sw128(v_saddr + kk * 2048, kBoxBytes, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                           const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using L = Smem<D>;
+  Barriers* bar = reinterpret_cast<Barriers*>(smem + L::kBar);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // ---- tile coordinates: head-major, heaviest (last) row block first ----
+  const int bh = blockIdx.x / p.num_mblocks;
+  const int mblk = p.num_mblocks - 1 - (blockIdx.x % p.num_mblocks);
+  const int b = bh / p.H, h = bh % p.H;
+  const int hk = h / (p.H / p.HKV);
+  const int t0 = mblk * 2 * BM;
+  const int n_kv = (p.S + BN - 1) / BN;
+  int n_tile[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    if (p.causal) {
+      int last_row = t0 + x * BM + BM - 1;
+      if (last_row > p.T - 1) last_row = p.T - 1;
+      int n = (last_row + p.q_start) / BN + 1;
+      n_tile[x] = n < n_kv ? n : n_kv;
+    } else {
+      n_tile[x] = n_kv;
+    }
+  }
+  if (n_tile[1] < n_tile[0]) n_tile[1] = n_tile[0];
+  const int nA = n_tile[0], nB = n_tile[1];
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->k_full[i], 1);
+      mbar_init(&bar->k_empty[i], 1);
+      mbar_init(&bar->v_full[i], 1);
+      mbar_init(&bar->v_empty[i], 1);
+      mbar_init(&bar->s_full[i], 1);
+      mbar_init(&bar->p_full[i], BM);
+      mbar_init(&bar->o_full[i], 1);
+    }
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+
+  const uint32_t sQ0 = smem_u32(smem + L::kQ0), sQ1 = smem_u32(smem + L::kQ1);
+  const uint32_t sK = smem_u32(smem + L::kK), sV = smem_u32(smem + L::kV);
+  constexpr int kNB = D / 64;  // boxes per tile
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&tm_q);
+      prefetch_tensormap(&tm_k);
+      prefetch_tensormap(&tm_v);
+      mbar_expect_tx(&bar->q_full, 2 * L::kTileBytes);
+      for (int i = 0; i < kNB; ++i) {
+        tma_load_4d(smem + L::kQ0 + i * kBoxBytes, &tm_q, &bar->q_full, i * 64, t0, h, b);
+        tma_load_4d(smem + L::kQ1 + i * kBoxBytes, &tm_q, &bar->q_full, i * 64, t0 + BM, h, b);
+      }
+      for (int j = 0; j < nB; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&bar->k_empty[st], ph ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->k_full[st], L::kTileBytes);
+        for (int i = 0; i < kNB; ++i)
+          tma_load_4d(smem + L::kK + st * L::kTileBytes + i * kBoxBytes, &tm_k, &bar->k_full[st], i * 64, j * BN,
+                      hk, b);
+        if (!mbar_wait(&bar->v_empty[st], ph ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->v_full[st], L::kTileBytes);
+        for (int i = 0; i < kNB; ++i)
+          tma_load_4d(smem + L::kV + st * L::kTileBytes + i * kBoxBytes, &tm_v, &bar->v_full[st], i * 64, j * BN,
+                      hk, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t tS[2] = {tmem + 0, tmem + 128};
+      const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
+      bool ok = mbar_wait(&bar->q_full, 0, abort, p.err) && mbar_wait(&bar->k_full[0], 0, abort, p.err);
+      if (ok) {
+        tc_fence_after();
+        mma_qk<D>(tS[0], sQ0, sK);
+        tc_commit(&bar->s_full[0]);
+        mma_qk<D>(tS[1], sQ1, sK);
+        tc_commit(&bar->s_full[1]);
+        tc_commit(&bar->k_empty[0]);
+      }
+      for (int j = 0; ok && j < nB; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const int jn = j + 1, stn = jn & 1;
+        const uint32_t phn = (jn >> 1) & 1;
+        if (!(ok = mbar_wait(&bar->v_full[st], ph, abort, p.err))) break;
+        if (j < nA) {
+          if (!(ok = mbar_wait(&bar->p_full[0], j & 1, abort, p.err))) break;
+          tc_fence_after();
+          mma_pv<D>(tO[0], tS[0], sV + st * L::kTileBytes, j > 0);
+          if (jn < nA) {
+            if (!(ok = mbar_wait(&bar->k_full[stn], phn, abort, p.err))) break;
+            tc_fence_after();
+            mma_qk<D>(tS[0], sQ0, sK + stn * L::kTileBytes);
+            tc_commit(&bar->s_full[0]);
+          } else {
+            tc_commit(&bar->o_full[0]);
+          }
+        }
+        if (!(ok = mbar_wait(&bar->p_full[1], j & 1, abort, p.err))) break;
+        tc_fence_after();
+        mma_pv<D>(tO[1], tS[1], sV + st * L::kTileBytes, j > 0);
+        tc_commit(&bar->v_empty[st]);
+        if (jn < nB) {
+          if (!(ok = mbar_wait(&bar->k_full[stn], phn, abort, p.err))) break;
+          tc_fence_after();
+          mma_qk<D>(tS[1], sQ1, sK + stn * L::kTileBytes);
+          tc_commit(&bar->s_full[1]);
+          tc_commit(&bar->k_empty[stn]);
+        } else {
+          tc_commit(&bar->o_full[1]);
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------- softmax
+    const int x = (warp >= 8) ? 1 : 0;  // tile A / B
+    const int q4 = warp & 3;            // TMEM lane quadrant of this warp
+    const int row = q4 * 32 + lane;     // row within the tile (= TMEM lane)
+    const int t = t0 + x * BM + row;    // query row
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tS = tmem + lane_off + x * 128;
+    const uint32_t tO = tmem + lane_off + 256 + x * D;
+    const int n = x ? nB : nA;
+    const float c = p.scale_log2;
+    float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!(ok = mbar_wait(&bar->s_full[x], j & 1, abort, p.err))) break;
+      tc_fence_after();
+      float s[BN];
+      {
+        uint32_t r[BN];
+#pragma unroll
+        for (int ch = 0; ch < BN / 32; ++ch)
+          tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(r + ch * 32));
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < BN; ++i) s[i] = __uint_as_float(r[i]);
+      }
+      // keys at or past `lim` (tile-relative) are masked for this row
+      int lim = p.S - j * BN;
+      if (p.causal) {
+        const int lc = t + p.q_start + 1 - j * BN;
+        lim = lc < lim ? lc : lim;
+      }
+      if (__any_sync(0xffffffffu, lim < BN)) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) s[i] = (i < lim) ? s[i] : -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int i = 1; i < BN; ++i) mx = fmaxf(mx, s[i]);
+      const float mt = mx * c;
+      m_true = fmaxf(m_true, mt);
+      if (j == 0) {
+        m_used = mt;
+      } else if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
+        const float m_new = fmaxf(m_used, mt);
+        const float alpha = ex2(m_used - m_new);
+        m_used = m_new;
+        l *= alpha;
+        // O is quiescent here: the commit that released S(j) also covers PV(j-1)
+        uint32_t r[32];
+#pragma unroll
+        for (int ch = 0; ch < D / 32; ++ch) {
+          tmem_ld32(tO + ch * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(tO + ch * 32, r);
+        }
+      }
+      const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+      float rs = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2(fmaf(s[ch * 32 + 2 * i], c, neg_m));
+          const float p1 = ex2(fmaf(s[ch * 32 + 2 * i + 1], c, neg_m));
+          rs += p0 + p1;
+          pk[i] = pack_bf16(p0, p1);
+        }
+        tmem_st16(tS + ch * 16, pk);
+      }
+      l += rs;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->p_full[x]);
+    }
+    if (ok && mbar_wait(&bar->o_full[x], 0, abort, p.err)) {
+      tc_fence_after();
+      const float inv_l = 1.0f / l;
+      const bool store = t < p.T;
+      const int64_t bhq = (int64_t)b * p.H + h;
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.o) + (int64_t)b * p.o_stride[0] +
+                            (int64_t)h * p.o_stride[1] + (int64_t)t * p.o_stride[2];
+#pragma unroll
+      for (int ch = 0; ch < D / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(tO + ch * 32, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
+        if (store) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+      if (store) {
+        const int64_t idx = bhq * p.T + t;
+        constexpr float kLn2 = 0.6931471805599453f;
+        if (p.lse) p.lse[idx] = (m_used + __log2f(l)) * kLn2;
+        if (p.m) p.m[idx] = m_true * kLn2;
+        if (p.den) p.den[idx] = l * ex2(m_used - m_true);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+int launch(const pdb_flash_desc& d, cudaStream_t stream) {
+  CUtensorMap tq, tk, tv;
+  const uint32_t box[4] = {64, 128, 1, 1};
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)d.seqlen_q, (uint64_t)d.heads_q, (uint64_t)d.batch};
+    const uint64_t str[3] = {(uint64_t)d.q_stride[2] * 2, (uint64_t)d.q_stride[1] * 2, (uint64_t)d.q_stride[0] * 2};
+    if (int st = encode_tma_4d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+  }
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)d.seqlen_k, (uint64_t)d.heads_kv, (uint64_t)d.batch};
+    const uint64_t sk[3] = {(uint64_t)d.k_stride[2] * 2, (uint64_t)d.k_stride[1] * 2, (uint64_t)d.k_stride[0] * 2};
+    const uint64_t sv[3] = {(uint64_t)d.v_stride[2] * 2, (uint64_t)d.v_stride[1] * 2, (uint64_t)d.v_stride[0] * 2};
+    if (int st = encode_tma_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.k, dims, sk, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+    if (int st = encode_tma_4d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.v, dims, sv, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+  }
+  FwdParams p;
+  p.o = d.o;
+  p.lse = d.lse;
+  p.m = d.m;
+  p.den = d.den;
+  for (int i = 0; i < 3; ++i) p.o_stride[i] = d.o_stride[i];
+  p.T = (int)d.seqlen_q;
+  p.S = (int)d.seqlen_k;
+  p.H = (int)d.heads_q;
+  p.HKV = (int)d.heads_kv;
+  p.B = (int)d.batch;
+  p.q_start = (int)d.q_start;
+  p.causal = d.causal ? 1 : 0;
+  p.num_mblocks = (int)((d.seqlen_q + 2 * BM - 1) / (2 * BM));
+  p.scale_log2 = (float)(d.scale * 1.4426950408889634);
+  p.err = device_error_flag();
+  const int64_t nblk = (int64_t)p.num_mblocks * d.heads_q * d.batch;
+  if (nblk > 0x7fffffffLL) return set_error(PDB_ERR_SHAPE, "bf16 flash: grid too large");
+  const int smem = Smem<D>::kTotal;
+  cudaError_t e = cudaFuncSetAttribute(flash_fwd_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_status(e, "bf16 flash: set smem attribute");
+  flash_fwd_sm100_kernel<D><<<(unsigned)nblk, kThreads, smem, stream>>>(tq, tk, tv, p);
+  return cuda_status(cudaGetLastError(), "bf16 flash launch");
+}
+
+}  // namespace
+
+int flash_fwd_bf16_sm100(const pdb_flash_desc& d, cudaStream_t stream) {
+  if (d.head_dim != d.head_dim_v || (d.head_dim != 64 && d.head_dim != 128))
+    return set_error(PDB_ERR_UNSUPPORTED, "bf16 flash: head_dim == head_dim_v in {64, 128} required (got %lld, %lld)",
+                     (long long)d.head_dim, (long long)d.head_dim_v);
+  if (d.seqlen_q > 0x7fffffffLL - 512 || d.seqlen_k > 0x7fffffffLL - 512 || d.q_start > 0x3fffffffLL)
+    return set_error(PDB_ERR_SHAPE, "bf16 flash: sequence too long");
+  if ((reinterpret_cast<uintptr_t>(d.o) & 15u) || (d.o_stride[0] & 7) || (d.o_stride[1] & 7) || (d.o_stride[2] & 7))
+    return set_error(PDB_ERR_ALIGN, "bf16 flash: o must be 16-byte aligned with strides multiple of 8 elements");
+  return d.head_dim == 64 ? launch<64>(d, stream) : launch<128>(d, stream);
+}
+
+}  // namespace pdb

@@ -1,0 +1,170 @@
+"""Device-tensor entry points over the C ABI (the zero-copy fast path).
+
+Each function takes CUDA tensors, fills a descriptor of ``include/pdb.h`` and
+launches on the current torch stream.  Nothing here computes on the host and
+nothing falls back: a CPU tensor, a dtype the library does not build, or a
+missing ``libpdb_sm100.so`` raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import torch
+
+from . import _lib
+from ._lib import FlashBwdDesc, FlashDesc, LayerNormDesc, RowSoftmaxDesc, check, load
+
+_DTYPES = {torch.float32: _lib.PDB_F32, torch.bfloat16: _lib.PDB_BF16}
+
+
+def _stream(t: torch.Tensor) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _need_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("pdum_dsl_b200 kernels take CUDA tensors (no host fallback)")
+
+
+def _rows2d(x: torch.Tensor) -> torch.Tensor:
+    if x.dim() < 1 or x.stride(-1) != 1:
+        x = x.contiguous()
+    x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
+    if x2.dim() == 2 and x2.shape[0] > 0 and x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    return x2
+
+
+def row_softmax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax over the last dim of an f32 CUDA tensor (row-normalization)."""
+    _need_cuda(x)
+    if x.dtype != torch.float32:
+        raise TypeError("row_softmax: float32 only")
+    x2 = _rows2d(x)
+    y = torch.empty_like(x2) if out is None else out.view(x2.shape)
+    d = RowSoftmaxDesc(x2.data_ptr(), y.data_ptr(), x2.shape[0], x2.shape[1], x2.stride(0) if x2.shape[0] else
+                       x2.shape[1], y.stride(0) if y.shape[0] else y.shape[1])
+    check(load().pdb_rowsoftmax_f32(C.byref(d), _stream(x)), "pdb_rowsoftmax_f32")
+    return y.view(x.shape)
+
+
+def layernorm(x: torch.Tensor, gamma: torch.Tensor | None = None, beta: torch.Tensor | None = None,
+              eps: float = 1e-5, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Two-pass layernorm over the last dim (row-statistics), f32."""
+    _need_cuda(x)
+    if x.dtype != torch.float32:
+        raise TypeError("layernorm: float32 only")
+    x2 = _rows2d(x)
+    C_ = x2.shape[1]
+    for nm, t in (("gamma", gamma), ("beta", beta)):
+        if t is not None and (t.dtype != torch.float32 or t.numel() != C_ or not t.is_cuda):
+            raise ValueError(f"layernorm: {nm} must be a CUDA f32 vector of length {C_}")
+    g = gamma.contiguous() if gamma is not None else None
+    b = beta.contiguous() if beta is not None else None
+    y = torch.empty_like(x2) if out is None else out.view(x2.shape)
+    d = LayerNormDesc(x2.data_ptr(), g.data_ptr() if g is not None else None, b.data_ptr() if b is not None else None,
+                      y.data_ptr(), x2.shape[0], C_, x2.stride(0) if x2.shape[0] else C_,
+                      y.stride(0) if y.shape[0] else C_, float(eps))
+    check(load().pdb_layernorm_f32(C.byref(d), _stream(x)), "pdb_layernorm_f32")
+    return y.view(x.shape)
+
+
+def _as4d(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dim() == 2:
+        t = t[None, None]
+    elif t.dim() == 3:
+        t = t[None]
+    elif t.dim() != 4:
+        raise ValueError(f"{name}: expected (T, D), (H, T, D) or (B, H, T, D), got {tuple(t.shape)}")
+    if t.stride(-1) != 1:
+        t = t.contiguous()
+    return t
+
+
+def _s3(t: torch.Tensor):
+    return _lib.I64x3(t.stride(0), t.stride(1), t.stride(2))
+
+
+def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float | None = None,
+                    causal: bool = False, q_start: int = 0, out: torch.Tensor | None = None,
+                    return_lse: bool = False, return_artifacts: bool = False):
+    """softmax(scale * q k^T [causal: s <= t + q_start]) v.
+
+    q (B, Hq, T, D), k/v (B, Hkv, S, D|Dv) with Hq a multiple of Hkv (GQA);
+    2-D and 3-D inputs drop the leading dims.  bf16 runs the tcgen05 kernel
+    (D = Dv in {64, 128}); f32 runs the IEEE CUDA-core kernel.  Returns o, or
+    (o, lse) / (o, m, den) with the per-row float32 statistics."""
+    _need_cuda(q, k, v)
+    if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError(f"flash_attention: q/k/v must share dtype float32 or bfloat16, got {q.dtype}/{k.dtype}/{v.dtype}")
+    shape_in = q.shape
+    q4, k4, v4 = _as4d(q, "q"), _as4d(k, "k"), _as4d(v, "v")
+    B, H, T, D = q4.shape
+    Bk, HKV, S, Dk = k4.shape
+    if Bk != B or Dk != D or v4.shape[:3] != (B, HKV, S):
+        raise ValueError(f"flash_attention: incompatible q {tuple(q4.shape)} k {tuple(k4.shape)} v {tuple(v4.shape)}")
+    DV = v4.shape[3]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    o = torch.empty((B, H, T, DV), dtype=q.dtype, device=q.device) if out is None else _as4d(out, "out")
+    stats = {}
+    want = ("lse",) if return_lse else ()
+    want += ("m", "den") if return_artifacts else ()
+    for nm in want:
+        stats[nm] = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
+    d = FlashDesc()
+    d.q, d.k, d.v, d.o = q4.data_ptr(), k4.data_ptr(), v4.data_ptr(), o.data_ptr()
+    d.lse = stats["lse"].data_ptr() if "lse" in stats else None
+    d.m = stats["m"].data_ptr() if "m" in stats else None
+    d.den = stats["den"].data_ptr() if "den" in stats else None
+    d.batch, d.heads_q, d.heads_kv, d.seqlen_q, d.seqlen_k, d.head_dim, d.head_dim_v = B, H, HKV, T, S, D, DV
+    d.q_stride, d.k_stride, d.v_stride, d.o_stride = _s3(q4), _s3(k4), _s3(v4), _s3(o)
+    d.q_start, d.scale, d.causal, d.dtype = int(q_start), float(scale), int(bool(causal)), _DTYPES[q.dtype]
+    check(load().pdb_flash_fwd(C.byref(d), _stream(q)), "pdb_flash_fwd")
+    o_ret = o.view(*shape_in[:-1], DV) if out is None else out
+    lead = shape_in[:-1]
+    if return_artifacts:
+        extra = (stats["lse"].view(lead),) if return_lse else ()
+        return (o_ret, *extra, stats["m"].view(lead), stats["den"].view(lead))
+    if return_lse:
+        return o_ret, stats["lse"].view(lead)
+    return o_ret
+
+
+def flash_attention_backward(q, k, v, o, dout, lse=None, *, scale=None, causal=False, q_start=0):
+    """(dq, dk, dv) of flash_attention; ``lse`` None recomputes it."""
+    _need_cuda(q, k, v, o, dout)
+    if q.dtype not in _DTYPES:
+        raise TypeError("flash_attention_backward: float32 or bfloat16")
+    shape_q, shape_k, shape_v = q.shape, k.shape, v.shape
+    q4, k4, v4, o4, do4 = (_as4d(t, n) for t, n in ((q, "q"), (k, "k"), (v, "v"), (o, "o"), (dout, "dout")))
+    B, H, T, D = q4.shape
+    _, HKV, S, _ = k4.shape
+    DV = v4.shape[3]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dq, dk, dv = torch.empty_like(q4), torch.empty_like(k4), torch.empty_like(v4)
+    d = FlashBwdDesc()
+    d.q, d.k, d.v, d.o, d.dout = q4.data_ptr(), k4.data_ptr(), v4.data_ptr(), o4.data_ptr(), do4.data_ptr()
+    lse_c = lse.contiguous().view(B, H, T) if lse is not None else None
+    d.lse = lse_c.data_ptr() if lse_c is not None else None
+    d.dq, d.dk, d.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    d.batch, d.heads_q, d.heads_kv, d.seqlen_q, d.seqlen_k, d.head_dim, d.head_dim_v = B, H, HKV, T, S, D, DV
+    d.q_stride, d.k_stride, d.v_stride, d.o_stride, d.do_stride = _s3(q4), _s3(k4), _s3(v4), _s3(o4), _s3(do4)
+    d.dq_stride, d.dk_stride, d.dv_stride = _s3(dq), _s3(dk), _s3(dv)
+    d.q_start, d.scale, d.causal, d.dtype = int(q_start), float(scale), int(bool(causal)), _DTYPES[q.dtype]
+    lib = load()
+    nbytes = lib.pdb_flash_bwd_workspace_size(C.byref(d))
+    ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=q.device)
+    d.workspace, d.workspace_bytes = ws.data_ptr(), int(nbytes)
+    check(lib.pdb_flash_bwd(C.byref(d), _stream(q)), "pdb_flash_bwd")
+    return dq.view(shape_q), dk.view(shape_k), dv.view(shape_v)
+
+
+def check_device_errors() -> None:
+    """Synchronise the current stream and raise if a bounded device wait expired."""
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    check(load().pdb_check_error(s), "pdb_check_error")

@@ -1,0 +1,77 @@
+"""The C-ABI library: builds, loads, exports every declared symbol, validates descriptors (no GPU needed)."""
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from pdum_dsl_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "pdb.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(pdb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_exports():
+    assert declared_symbols() == sorted(_lib.EXPORTS)
+
+
+def test_library_loads_and_exports_everything():
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert _lib.version().startswith("pdb-sm100a")
+
+
+def test_descriptor_layouts_match_the_header():
+    # pointer-sized fields first, then int64 sizes; the offsets the C side expects
+    assert C.sizeof(_lib.RowSoftmaxDesc) == 6 * 8
+    assert C.sizeof(_lib.LayerNormDesc) == 9 * 8
+    assert C.sizeof(_lib.FlashDesc) == 7 * 8 + 7 * 8 + 12 * 8 + 8 + 8 + 4 + 4
+    assert C.sizeof(_lib.FlashBwdDesc) == 11 * 8 + 7 * 8 + 24 * 8 + 8 + 8 + 4 + 4
+
+
+def test_null_descriptors_are_refused():
+    lib = _lib.load()
+    assert lib.pdb_rowsoftmax_f32(None, None) == _lib.PDB_ERR_ARG
+    assert lib.pdb_layernorm_f32(None, None) == _lib.PDB_ERR_ARG
+    assert lib.pdb_flash_fwd(None, None) == _lib.PDB_ERR_ARG
+    assert b"null descriptor" in lib.pdb_last_error_string()
+
+
+def test_shape_validation_happens_before_any_launch():
+    lib = _lib.load()
+    d = _lib.RowSoftmaxDesc(None, None, -1, 4, 4, 4)
+    assert lib.pdb_rowsoftmax_f32(C.byref(d), None) == _lib.PDB_ERR_SHAPE
+    d = _lib.RowSoftmaxDesc(None, None, 0, 4, 4, 4)  # empty: nothing to do
+    assert lib.pdb_rowsoftmax_f32(C.byref(d), None) == _lib.PDB_OK
+    f = _lib.FlashDesc()
+    f.q = f.k = f.v = f.o = 16
+    f.batch, f.heads_q, f.heads_kv, f.seqlen_q, f.seqlen_k, f.head_dim, f.head_dim_v = 1, 3, 2, 8, 8, 64, 64
+    assert lib.pdb_flash_fwd(C.byref(f), None) == _lib.PDB_ERR_SHAPE  # 3 q heads over 2 kv heads
+    f.heads_q, f.q_start = 4, -1
+    assert lib.pdb_flash_fwd(C.byref(f), None) == _lib.PDB_ERR_SHAPE
+    f.q_start, f.dtype, f.head_dim, f.head_dim_v = 0, _lib.PDB_BF16, 96, 96
+    assert lib.pdb_flash_fwd(C.byref(f), None) == _lib.PDB_ERR_UNSUPPORTED
+    f.dtype = 7
+    assert lib.pdb_flash_fwd(C.byref(f), None) == _lib.PDB_ERR_UNSUPPORTED
+
+
+def test_python_layer_raises_on_host_tensors():
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    with pytest.raises(ValueError, match="CUDA"):
+        kernels.row_softmax(torch.zeros(2, 2))
+    with pytest.raises(ValueError, match="CUDA"):
+        kernels.flash_attention(torch.zeros(4, 8), torch.zeros(4, 8), torch.zeros(4, 8))
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(_lib.BackendUnavailable):
+        _lib.load(tmp_path / "nope.so")

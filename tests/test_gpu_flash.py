@@ -1,0 +1,147 @@
+"""Flash-attention forward kernels vs the reference's run_region fixtures and the oracle."""
+
+import math
+
+import numpy as np
+import pytest
+
+from oracle import attention as OA
+from tests.golden import HERE, load
+from tests.tolerances import assert_bf16, assert_f32
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev, dtype):
+    import torch
+
+    return torch.as_tensor(np.ascontiguousarray(a, dtype=np.float32), device=dev).to(dtype)
+
+
+def _np(t):
+    return t.float().cpu().numpy().astype(np.float64)
+
+
+def _flat_gqa(a, names):
+    if "r" in names:
+        return a.reshape(a.shape[0], a.shape[1] * a.shape[2], *a.shape[3:])
+    return a
+
+
+def test_flash_tile_flagship_f32(cuda):
+    """The reference's own tile flagship (zoo/tiles.py:143), f32 column."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    z = np.load(HERE / "flash_tile_default.npz")
+    o = kernels.flash_attention(_t(z["q"], cuda, torch.float32), _t(z["k"], cuda, torch.float32),
+                                _t(z["v"], cuda, torch.float32), scale=1.0, causal=True)
+    assert_f32(_np(o), z["naive"])
+
+
+@pytest.mark.parametrize("case", ["cfg1_flash_f32", "causal_f32_small"])
+def test_f32_flash_matches_reference(cuda, case):
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    spec, (q, k, v), (want, *_) = load(case)
+    kw = spec["region"]
+    o = kernels.flash_attention(_t(q, cuda, torch.float32), _t(k, cuda, torch.float32),
+                                _t(v, cuda, torch.float32), scale=kw.get("scale") or 1.0, causal=kw["causal"])
+    assert_f32(_np(o), want, what=case)
+
+
+@pytest.mark.parametrize("case", ["causal_bf16_ragged", "causal_bf16_d128", "noncausal_bf16_kv_ragged", "gqa_bf16"])
+def test_bf16_flash_matches_reference(cuda, case):
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    spec, (q, k, v), outs = load(case)
+    kw = spec["region"]
+    qn = spec["inputs"][0]["names"]
+    q4 = _flat_gqa(q, qn)
+    res = kernels.flash_attention(_t(q4, cuda, torch.bfloat16), _t(k, cuda, torch.bfloat16),
+                                  _t(v, cuda, torch.bfloat16), scale=kw["scale"], causal=kw["causal"],
+                                  return_artifacts=bool(kw.get("artifacts")))
+    o = res[0] if isinstance(res, tuple) else res
+    assert_bf16(_np(o).reshape(outs[0].shape), outs[0], what=case)
+    if kw.get("artifacts"):
+        m, den = _np(res[1]), _np(res[2])
+        np.testing.assert_allclose(m.reshape(outs[1].shape), outs[1], rtol=1e-3, atol=1e-3)
+        np.testing.assert_allclose(den.reshape(outs[2].shape), outs[2], rtol=1e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("B,H,HKV,T,S,D,causal", [
+    (1, 1, 1, 128, 128, 64, True), (1, 1, 1, 256, 256, 128, True), (2, 3, 3, 300, 300, 64, True),
+    (1, 4, 1, 513, 513, 128, True), (1, 2, 2, 64, 1000, 128, False), (1, 1, 1, 1, 1, 64, False),
+    (1, 2, 2, 1, 77, 64, True), (3, 2, 1, 257, 129, 64, False)])
+def test_bf16_shapes_vs_oracle(cuda, B, H, HKV, T, S, D, causal):
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device="cpu").manual_seed(B * 1000 + T + S)
+    q = torch.randn(B, H, T, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, HKV, S, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, HKV, S, D, generator=g).to(torch.bfloat16)
+    scale = 1 / math.sqrt(D)
+    o, lse = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), scale=scale, causal=causal,
+                                     return_lse=True)
+    ro, _, _, rlse = OA.attention_fwd(q.double().numpy(), k.double().numpy(), v.double().numpy(), scale=scale,
+                                      causal=causal)
+    assert_bf16(_np(o), ro)
+    np.testing.assert_allclose(_np(lse), rlse, atol=2e-3, rtol=1e-4)
+
+
+def test_bf16_large_scores_rescale(cuda):
+    """Wide scores (x8, the reference's adversarial family) and a dominant key row (x40)."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device="cpu").manual_seed(11)
+    q = (8 * torch.randn(1, 2, 512, 64, generator=g)).to(torch.bfloat16)
+    k = torch.randn(1, 2, 512, 64, generator=g)
+    k[:, :, 300] *= 40
+    k = k.to(torch.bfloat16)
+    v = torch.randn(1, 2, 512, 64, generator=g).to(torch.bfloat16)
+    for causal in (True, False):
+        o = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), scale=0.125, causal=causal)
+        ro, *_ = OA.attention_fwd(q.double().numpy(), k.double().numpy(), v.double().numpy(), scale=0.125,
+                                  causal=causal)
+        assert_bf16(_np(o), ro)
+
+
+def test_bf16_strided_inputs(cuda):
+    """(B, T, H, D) storage read through strides, the layout torch's projections produce."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device="cpu").manual_seed(5)
+    qkv = torch.randn(2, 200, 3, 4, 128, generator=g).to(torch.bfloat16).to(cuda)
+    q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))  # (B, H, T, D) views
+    o = kernels.flash_attention(q, k, v, causal=True)
+    ro, *_ = OA.attention_fwd(*(x.double().cpu().numpy() for x in (q, k, v)), scale=1 / math.sqrt(128), causal=True)
+    assert_bf16(_np(o), ro)
+
+
+def test_bf16_config3_slices(cuda):
+    """Config 3 (B8 H32 S4096 D128 causal): full-size launch, sampled heads vs the oracle."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device=cuda).manual_seed(3)
+    shape = (8, 32, 4096, 128)
+    q, k, v = (torch.randn(shape, device=cuda, generator=g).to(torch.bfloat16) for _ in range(3))
+    o = kernels.flash_attention(q, k, v, causal=True)
+    kernels.check_device_errors()
+    assert torch.isfinite(o).all()
+    for b, h in ((0, 0), (7, 31), (3, 17)):
+        ro, *_ = OA.attention_fwd(*(x[b, h].double().cpu().numpy() for x in (q, k, v)), scale=1 / math.sqrt(128),
+                                  causal=True)
+        assert_bf16(_np(o[b, h]), ro, what=f"head ({b},{h})")
