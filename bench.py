@@ -230,6 +230,11 @@ def run_ours(args):
     launch_ms = sum(per) / len(per)
     achieved = flop_rank / (launch_ms * 1e-3) / 1e12
 
+    if args.kernel_only:
+        if rank == 0:
+            print(json.dumps({"workload": [B, H, S, D], "value": value, "unit": "TFLOP/s", "launch_ms": launch_ms,
+                              "achieved": achieved, "clocks": sampler.summary()}), flush=True)
+        return
     # ---- e2e: the same step through the public API with pinned host buffers
     qh, kh, vh = (x.cpu().pin_memory() for x in (q, k, v))
     oh = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
@@ -338,7 +343,17 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--shape", default=None,
+                    help="B,H,S,D override of the flash workload (profiling a smaller case); implies --kernel-only")
+    ap.add_argument("--kernel-only", action="store_true", help="time only the flash forward (no e2e/extra/cpu)")
     args = ap.parse_args()
+    if args.shape:
+        global B, H, S, D, FLOP_FULL
+        B, H, S, D = (int(x) for x in args.shape.split(","))
+        FLOP_FULL = 4.0 * B * H * S * S * D / 2
+        args.kernel_only = True
+    if args.kernel_only:
+        args.no_extra = args.no_cpu = True
     args.warmup = max(args.warmup, 3)
     args.steps_ref = max(1, min(args.steps, 5))
     args.warmup_ref = 1

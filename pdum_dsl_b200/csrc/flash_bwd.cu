@@ -1,12 +1,623 @@
-// Flash-attention backward (placeholder until the kernels land).
+// bf16 flash-attention backward for sm_100a (tcgen05 / TMEM / TMA).
+//
+// The reference obtains the backward by autodiff of the naive attention
+// region (autodiff.py:102-150) and carves the joint with plan_model
+// (partition.py:586-607) into: the flash forward with its (m, den)
+// artifacts, a held-back D = rowsum(dO * O) row statistic, and contraction
+// carves that re-derive P inside their sweep (partition.py:354-455).  This
+// file executes that plan as three kernels:
+//
+//   bwd_prep     D[t] = sum_o dO[t,o] O[t,o] and lse2[t] = lse[t] * log2 e
+//                (rows padded to a multiple of 128 with lse2 = +inf, D = 0,
+//                so padded query rows carry P = 0 without masks)
+//   bwd_dkdv     one CTA per (batch, KV head, 128-key block): for every query
+//                tile of every query head of the group it forms
+//                S^T = K Q^T and dP^T = V dO^T in TMEM, P^T = exp2(S^T c - lse2),
+//                dS^T = P^T (dP^T - D) (one thread per key row), writes both
+//                back to TMEM as bf16 and accumulates dV += P^T dO,
+//                dK += dS^T Q in TMEM; GQA sums over the group in place.
+//   bwd_dq       one CTA per (batch, head, 128-row block): S = Q K^T,
+//                dP = dO V^T, dS = P (dP - D), dQ += dS K over the key tiles.
+// dQ = scale dS K, dK = scale dS^T Q; everything accumulates in fp32 (TMEM)
+// and is rounded to bf16 once.  No atomics: the result is deterministic.
+#include <cfloat>
+
 #include "common.cuh"
+#include "tma.h"
+
+namespace pdb {
+int flash_fwd_bf16_sm100(const pdb_flash_desc& d, cudaStream_t stream);
+int validate_common(int64_t batch, int64_t hq, int64_t hkv, int64_t T, int64_t S, int64_t E, int64_t O,
+                    int64_t q_start, const void* q, const void* k, const void* v);
+
+namespace {
+
+constexpr int BT = 128;  // query rows per tile
+constexpr int BS = 128;  // keys per tile
+constexpr int kBox = 64 * 128 * 2;
+constexpr int kThreads = 256;  // warp0 TMA, warp1 MMA, warp2 TMEM, warps 4..7 compute
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct BwdParams {
+  const float* lse2;  // [B*H*Tpad]
+  const float* dsum;  // [B*H*Tpad]
+  void* out0;         // dkdv: dk ; dq: dq
+  void* out1;         // dkdv: dv
+  int64_t s0[3], s1[3];
+  int T, S, H, HKV, Tpad;
+  int q_start, causal;
+  float scale, scale_log2;
+  int n_blocks;  // key blocks (dkdv) or query blocks (dq) per head
+  int* err;
+};
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+template <int D>
+__device__ __forceinline__ void mma_kmajor(uint32_t d_tmem, uint32_t a_saddr, uint32_t b_saddr) {
+  constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+    mma_ss(d_tmem, sdesc_sw128(a_saddr + off, 16, 1024), sdesc_sw128(b_saddr + off, 16, 1024), idesc, kk > 0);
+  }
+}
+
+// D (128 x D) (+)= A_tmem (128 x 128, bf16 packed) * B_smem (128 rows x D, MN-major)
+template <int D>
+__device__ __forceinline__ void mma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_saddr, bool acc) {
+  constexpr uint32_t idesc = idesc_bf16(128, D, 0, 1);
+#pragma unroll
+  for (int kk = 0; kk < 128 / 16; ++kk)
+    mma_ts(d_tmem, a_tmem + kk * 8, sdesc_sw128(b_saddr + kk * 2048, kBox, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
+}
+
+template <int D>
+__device__ __forceinline__ void store_rows_bf16(uint32_t t_src, float mul, __nv_bfloat16* row, bool store) {
+#pragma unroll
+  for (int ch = 0; ch < D / 32; ++ch) {
+    uint32_t r[32];
+    tmem_ld32(t_src + ch * 32, r);
+    tmem_wait_ld();
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * mul, __uint_as_float(r[2 * i + 1]) * mul);
+    if (store) {
+      uint4* dst = reinterpret_cast<uint4*>(row + ch * 32);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+    }
+  }
+}
+
+struct __align__(8) BarsKV {
+  uint64_t kv_full;
+  uint64_t q_full[2], q_empty[2];
+  uint64_t s_full, p_full, o_full;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// ------------------------------------------------------------------ dK / dV
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                    const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kTile = 128 * D * 2;
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + kTile;
+  uint8_t* sQ = smem + 2 * kTile;   // 2 stages
+  uint8_t* sDO = smem + 4 * kTile;  // 2 stages
+  float* sVec = reinterpret_cast<float*>(smem + 6 * kTile);  // 2 stages x (lse2[128], dsum[128])
+  BarsKV* bar = reinterpret_cast<BarsKV*>(smem + 6 * kTile + 2 * 2 * 128 * 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int bhk = blockIdx.x / p.n_blocks;
+  const int nblk = blockIdx.x % p.n_blocks;
+  const int b = bhk / p.HKV, hk = bhk % p.HKV;
+  const int group = p.H / p.HKV;
+  const int s0 = nblk * BS;
+  const int n_qt = p.Tpad / BT;
+  int qt0 = 0;
+  if (p.causal) {
+    const int first = s0 - p.q_start;  // first query row that can see key s0
+    qt0 = first > 0 ? first / BT : 0;
+  }
+  const int per_head = n_qt - qt0 > 0 ? n_qt - qt0 : 0;
+  const int n_items = per_head * group;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->q_full[i], 1);
+      mbar_init(&bar->q_empty[i], 1);
+    }
+    mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->p_full, 128);
+    mbar_init(&bar->o_full, 1);
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+  constexpr int kNB = D / 64;
+  // TMEM: S^T [0,128) (P^T in [0,64)), dP^T [128,256) (dS^T in [128,192)), dV [256,256+D), dK [256+D, 256+2D)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(&bar->kv_full, 2 * kTile);
+      for (int i = 0; i < kNB; ++i) {
+        tma_load_4d(sK + i * kBox, &tm_k, &bar->kv_full, i * 64, s0, hk, b);
+        tma_load_4d(sV + i * kBox, &tm_v, &bar->kv_full, i * 64, s0, hk, b);
+      }
+      for (int it = 0; it < n_items; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        const int h = hk * group + it / per_head;
+        const int t0 = (qt0 + it % per_head) * BT;
+        if (!mbar_wait(&bar->q_empty[st], ph ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->q_full[st], 2 * kTile + 2 * 128 * 4);
+        for (int i = 0; i < kNB; ++i) {
+          tma_load_4d(sQ + st * kTile + i * kBox, &tm_q, &bar->q_full[st], i * 64, t0, h, b);
+          tma_load_4d(sDO + st * kTile + i * kBox, &tm_do, &bar->q_full[st], i * 64, t0, h, b);
+        }
+        const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
+        bulk_load(sVec + st * 256, p.lse2 + vrow, 512, &bar->q_full[st]);
+        bulk_load(sVec + st * 256 + 128, p.dsum + vrow, 512, &bar->q_full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar->kv_full, 0, abort, p.err);
+      for (int it = 0; ok && it < n_items; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        if (!(ok = mbar_wait(&bar->q_full[st], ph, abort, p.err))) break;
+        tc_fence_after();
+        mma_kmajor<D>(tmem + 0, smem_u32(sK), smem_u32(sQ + st * kTile));      // S^T = K Q^T
+        mma_kmajor<D>(tmem + 128, smem_u32(sV), smem_u32(sDO + st * kTile));  // dP^T = V dO^T
+        tc_commit(&bar->s_full);
+        if (!(ok = mbar_wait(&bar->p_full, it & 1, abort, p.err))) break;
+        tc_fence_after();
+        mma_tmem_a<D>(tmem + 256, tmem + 0, smem_u32(sDO + st * kTile), it > 0);    // dV += P^T dO
+        mma_tmem_a<D>(tmem + 256 + D, tmem + 128, smem_u32(sQ + st * kTile), it > 0);  // dK += dS^T Q
+        tc_commit(&bar->q_empty[st]);
+      }
+      if (ok) tc_commit(&bar->o_full);
+    }
+  } else if (warp >= 4) {
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;  // key row within the block
+    const int s = s0 + row;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const float c = p.scale_log2;
+    bool ok = true;
+    for (int it = 0; it < n_items; ++it) {
+      const int st = it & 1;
+      const uint32_t ph = (it >> 1) & 1;
+      const int t0 = (qt0 + it % per_head) * BT;
+      if (!(ok = mbar_wait(&bar->q_full[st], ph, abort, p.err))) break;
+      if (!(ok = mbar_wait(&bar->s_full, it & 1, abort, p.err))) break;
+      tc_fence_after();
+      const float* lse2 = sVec + st * 256;
+      const float* dsum = lse2 + 128;
+      // query columns below `lo` are masked for this key (causal: t + q_start >= s)
+      const int lo = p.causal ? s - p.q_start - t0 : -1;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tmem + lane_off + ch * 32, sr);
+        tmem_ld32(tmem + lane_off + 128 + ch * 32, dr);
+        tmem_wait_ld();
+        uint32_t pp[16], ds[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = ch * 32 + 2 * i + u;
+            float pr = ex2(fmaf(__uint_as_float(sr[2 * i + u]), c, -lse2[col]));
+            pr = (col < lo) ? 0.f : pr;
+            pv[u] = pr;
+            dv[u] = pr * (__uint_as_float(dr[2 * i + u]) - dsum[col]);
+          }
+          pp[i] = pack_bf16(pv[0], pv[1]);
+          ds[i] = pack_bf16(dv[0], dv[1]);
+        }
+        tmem_st16(tmem + lane_off + ch * 16, pp);
+        tmem_st16(tmem + lane_off + 128 + ch * 16, ds);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->p_full);
+    }
+    if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
+      tc_fence_after();
+      const bool store = s < p.S;
+      __nv_bfloat16* dk = static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] +
+                          (int64_t)s * p.s0[2];
+      __nv_bfloat16* dv = static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] +
+                          (int64_t)s * p.s1[2];
+      // with no query tile at all (a key block past every row) dK = dV = 0
+      if (n_items == 0) {
+        if (store) {
+          for (int i = 0; i < D; i += 8) {
+            *reinterpret_cast<uint4*>(dk + i) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(dv + i) = make_uint4(0, 0, 0, 0);
+          }
+        }
+      } else {
+        store_rows_bf16<D>(tmem + lane_off + 256, 1.0f, dv, store);
+        store_rows_bf16<D>(tmem + lane_off + 256 + D, p.scale, dk, store);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+struct __align__(8) BarsQ {
+  uint64_t qo_full;
+  uint64_t kv_full[2], kv_empty[2];
+  uint64_t s_full, p_full, o_full;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// --------------------------------------------------------------------- dQ
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                  const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kTile = 128 * D * 2;
+  uint8_t* sQ = smem;
+  uint8_t* sDO = smem + kTile;
+  uint8_t* sK = smem + 2 * kTile;  // 2 stages
+  uint8_t* sV = smem + 4 * kTile;  // 2 stages
+  BarsQ* bar = reinterpret_cast<BarsQ*>(smem + 6 * kTile);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int bh = blockIdx.x / p.n_blocks;
+  const int mblk = p.n_blocks - 1 - (blockIdx.x % p.n_blocks);  // heaviest first
+  const int b = bh / p.H, h = bh % p.H;
+  const int hk = h / (p.H / p.HKV);
+  const int t0 = mblk * BT;
+  const int n_kv_all = (p.S + BS - 1) / BS;
+  int n_kv = n_kv_all;
+  if (p.causal) {
+    int last = t0 + BT - 1;
+    if (last > p.T - 1) last = p.T - 1;
+    const int n = (last + p.q_start) / BS + 1;
+    n_kv = n < n_kv_all ? n : n_kv_all;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->qo_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->kv_full[i], 1);
+      mbar_init(&bar->kv_empty[i], 1);
+    }
+    mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->p_full, 128);
+    mbar_init(&bar->o_full, 1);
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+  constexpr int kNB = D / 64;
+  // TMEM: S [0,128) (dS in [0,64)), dP [128,256), dQ [256, 256+D)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(&bar->qo_full, 2 * kTile);
+      for (int i = 0; i < kNB; ++i) {
+        tma_load_4d(sQ + i * kBox, &tm_q, &bar->qo_full, i * 64, t0, h, b);
+        tma_load_4d(sDO + i * kBox, &tm_do, &bar->qo_full, i * 64, t0, h, b);
+      }
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&bar->kv_empty[st], ph ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->kv_full[st], 2 * kTile);
+        for (int i = 0; i < kNB; ++i) {
+          tma_load_4d(sK + st * kTile + i * kBox, &tm_k, &bar->kv_full[st], i * 64, j * BS, hk, b);
+          tma_load_4d(sV + st * kTile + i * kBox, &tm_v, &bar->kv_full[st], i * 64, j * BS, hk, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar->qo_full, 0, abort, p.err);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!(ok = mbar_wait(&bar->kv_full[st], ph, abort, p.err))) break;
+        tc_fence_after();
+        mma_kmajor<D>(tmem + 0, smem_u32(sQ), smem_u32(sK + st * kTile));     // S = Q K^T
+        mma_kmajor<D>(tmem + 128, smem_u32(sDO), smem_u32(sV + st * kTile));  // dP = dO V^T
+        tc_commit(&bar->s_full);
+        if (!(ok = mbar_wait(&bar->p_full, j & 1, abort, p.err))) break;
+        tc_fence_after();
+        mma_tmem_a<D>(tmem + 256, tmem + 0, smem_u32(sK + st * kTile), j > 0);  // dQ += dS K
+        tc_commit(&bar->kv_empty[st]);
+      }
+      if (ok) tc_commit(&bar->o_full);
+    }
+  } else if (warp >= 4) {
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int t = t0 + row;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const float c = p.scale_log2;
+    const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t;
+    const float neg_l = -p.lse2[vrow];  // +inf on padded rows -> P = 0
+    const float dsum = p.dsum[vrow];
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!(ok = mbar_wait(&bar->s_full, j & 1, abort, p.err))) break;
+      tc_fence_after();
+      const int lim = p.causal ? t + p.q_start + 1 - j * BS : 1 << 30;  // keys >= lim masked
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tmem + lane_off + ch * 32, sr);
+        tmem_ld32(tmem + lane_off + 128 + ch * 32, dr);
+        tmem_wait_ld();
+        uint32_t ds[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float dv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = ch * 32 + 2 * i + u;
+            float pr = ex2(fmaf(__uint_as_float(sr[2 * i + u]), c, neg_l));
+            pr = (col < lim) ? pr : 0.f;
+            dv[u] = pr * (__uint_as_float(dr[2 * i + u]) - dsum);
+          }
+          ds[i] = pack_bf16(dv[0], dv[1]);
+        }
+        tmem_st16(tmem + lane_off + ch * 16, ds);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->p_full);
+    }
+    if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
+      tc_fence_after();
+      __nv_bfloat16* dq = static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)h * p.s0[1] +
+                          (int64_t)t * p.s0[2];
+      store_rows_bf16<D>(tmem + lane_off + 256, p.scale, dq, t < p.T);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------- prologue
+// One warp per (b, h, padded row): D = sum(dO * O), lse2 = lse * log2(e).
+__global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                const float* __restrict__ lse, float* __restrict__ lse2, float* __restrict__ dsum,
+                                int64_t so0, int64_t so1, int64_t so2, int64_t sd0, int64_t sd1, int64_t sd2, int H,
+                                int T, int Tpad, int DV, int64_t rows) {
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const int t = (int)(r % Tpad);
+  const int64_t bh = r / Tpad;
+  const int b = (int)(bh / H), h = (int)(bh % H);
+  if (t >= T) {
+    if (lane == 0) {
+      lse2[r] = INFINITY;
+      dsum[r] = 0.f;
+    }
+    return;
+  }
+  const __nv_bfloat16* orow = o + b * so0 + h * so1 + t * so2;
+  const __nv_bfloat16* drow = dout + b * sd0 + h * sd1 + t * sd2;
+  float acc = 0.f;
+  for (int i = lane; i < DV; i += 32) acc += __bfloat162float(orow[i]) * __bfloat162float(drow[i]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    dsum[r] = acc;
+    lse2[r] = lse[bh * T + t] * kLog2e;
+  }
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct WsLayout {
+  size_t lse2, dsum, lse, o_scratch, total;
+};
+
+WsLayout ws_layout(const pdb_flash_bwd_desc& d) {
+  const int64_t tpad = (d.seqlen_q + BT - 1) / BT * BT;
+  const size_t rows = (size_t)(d.batch * d.heads_q * tpad);
+  WsLayout w{};
+  size_t off = 0;
+  w.lse2 = off;
+  off = align256(off + rows * 4);
+  w.dsum = off;
+  off = align256(off + rows * 4);
+  if (d.lse == nullptr) {  // recompute variant: the forward's lse and a scratch output
+    w.lse = off;
+    off = align256(off + (size_t)(d.batch * d.heads_q * d.seqlen_q) * 4);
+    w.o_scratch = off;
+    off = align256(off + (size_t)(d.batch * d.heads_q * d.seqlen_q * d.head_dim_v) * 2);
+  }
+  w.total = off;
+  return w;
+}
+
+int map_bf16(CUtensorMap* m, const void* base, int D, int64_t rows, int64_t heads, int64_t batch,
+             const int64_t st[3]) {
+  const uint64_t dims[4] = {(uint64_t)D, (uint64_t)rows, (uint64_t)heads, (uint64_t)batch};
+  const uint64_t str[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
+  const uint32_t box[4] = {64, 128, 1, 1};
+  return encode_tma_4d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int D>
+int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w, cudaStream_t stream) {
+  uint8_t* ws = static_cast<uint8_t*>(d.workspace);
+  const int64_t tpad = (d.seqlen_q + BT - 1) / BT * BT;
+  float* lse2 = reinterpret_cast<float*>(ws + w.lse2);
+  float* dsum = reinterpret_cast<float*>(ws + w.dsum);
+  {
+    const int64_t rows = d.batch * d.heads_q * tpad;
+    const int wpb = 8;
+    bwd_prep_kernel<<<(unsigned)((rows + wpb - 1) / wpb), 32 * wpb, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(d.o), static_cast<const __nv_bfloat16*>(d.dout), lse, lse2, dsum,
+        d.o_stride[0], d.o_stride[1], d.o_stride[2], d.do_stride[0], d.do_stride[1], d.do_stride[2],
+        (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (int)d.head_dim_v, rows);
+    if (int st = cuda_status(cudaGetLastError(), "bwd prep launch")) return st;
+  }
+  CUtensorMap tq, tk, tv, tdo;
+  if (int st = map_bf16(&tq, d.q, D, d.seqlen_q, d.heads_q, d.batch, d.q_stride)) return st;
+  if (int st = map_bf16(&tk, d.k, D, d.seqlen_k, d.heads_kv, d.batch, d.k_stride)) return st;
+  if (int st = map_bf16(&tv, d.v, D, d.seqlen_k, d.heads_kv, d.batch, d.v_stride)) return st;
+  if (int st = map_bf16(&tdo, d.dout, D, d.seqlen_q, d.heads_q, d.batch, d.do_stride)) return st;
+  BwdParams p{};
+  p.lse2 = lse2;
+  p.dsum = dsum;
+  p.T = (int)d.seqlen_q;
+  p.S = (int)d.seqlen_k;
+  p.H = (int)d.heads_q;
+  p.HKV = (int)d.heads_kv;
+  p.Tpad = (int)tpad;
+  p.q_start = (int)d.q_start;
+  p.causal = d.causal ? 1 : 0;
+  p.scale = (float)d.scale;
+  p.scale_log2 = (float)(d.scale * 1.4426950408889634);
+  p.err = device_error_flag();
+  constexpr int kTile = 128 * D * 2;
+  // >= 120 KB keeps one CTA per SM, so the 512-column TMEM allocation never waits
+  const int smem_kv = (6 * kTile + 2048 + 1024) > 120 * 1024 ? (6 * kTile + 2048 + 1024) : 120 * 1024;
+  const int smem_q = smem_kv;
+  {  // dK, dV
+    p.out0 = d.dk;
+    p.out1 = d.dv;
+    for (int i = 0; i < 3; ++i) {
+      p.s0[i] = d.dk_stride[i];
+      p.s1[i] = d.dv_stride[i];
+    }
+    p.n_blocks = (int)((d.seqlen_k + BS - 1) / BS);
+    const int64_t grid = (int64_t)p.n_blocks * d.heads_kv * d.batch;
+    cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
+    if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
+    bwd_dkdv_kernel<D><<<(unsigned)grid, kThreads, smem_kv, stream>>>(tq, tk, tv, tdo, p);
+    if (int st = cuda_status(cudaGetLastError(), "bwd dkdv launch")) return st;
+  }
+  {  // dQ
+    p.out0 = d.dq;
+    p.out1 = nullptr;
+    for (int i = 0; i < 3; ++i) p.s0[i] = d.dq_stride[i];
+    p.n_blocks = (int)(tpad / BT);
+    const int64_t grid = (int64_t)p.n_blocks * d.heads_q * d.batch;
+    cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
+    if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
+    bwd_dq_kernel<D><<<(unsigned)grid, kThreads, smem_q, stream>>>(tq, tk, tv, tdo, p);
+    if (int st = cuda_status(cudaGetLastError(), "bwd dq launch")) return st;
+  }
+  return PDB_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace pdb
 
 using namespace pdb;
 
-extern "C" size_t pdb_flash_bwd_workspace_size(const pdb_flash_bwd_desc* d) { return d ? 0 : 0; }
+extern "C" size_t pdb_flash_bwd_workspace_size(const pdb_flash_bwd_desc* d) {
+  if (!d || d->batch <= 0 || d->heads_q <= 0 || d->seqlen_q <= 0) return 0;
+  return ws_layout(*d).total;
+}
 
 extern "C" int pdb_flash_bwd(const pdb_flash_bwd_desc* d, void* stream) {
-  (void)d;
-  (void)stream;
-  return set_error(PDB_ERR_UNSUPPORTED, "flash backward not built yet");
+  if (!d) return set_error(PDB_ERR_ARG, "null descriptor");
+  if (int st = validate_common(d->batch, d->heads_q, d->heads_kv, d->seqlen_q, d->seqlen_k, d->head_dim,
+                               d->head_dim_v, d->q_start, d->q, d->k, d->v))
+    return st;
+  if (!d->o || !d->dout || !d->dq || !d->dk || !d->dv) return set_error(PDB_ERR_ARG, "null o / dout / dq / dk / dv");
+  if (d->dtype != PDB_BF16)
+    return set_error(PDB_ERR_UNSUPPORTED, "flash backward: bf16 only (dtype %d)", d->dtype);
+  if (d->head_dim != d->head_dim_v || (d->head_dim != 64 && d->head_dim != 128))
+    return set_error(PDB_ERR_UNSUPPORTED, "flash backward: head_dim == head_dim_v in {64, 128} required");
+  if (d->seqlen_q > (1 << 30) || d->seqlen_k > (1 << 30)) return set_error(PDB_ERR_SHAPE, "sequence too long");
+  const WsLayout w = ws_layout(*d);
+  if (!d->workspace || d->workspace_bytes < w.total)
+    return set_error(PDB_ERR_ARG, "workspace too small: need %zu bytes", w.total);
+  if (!aligned16(d->workspace)) return set_error(PDB_ERR_ALIGN, "workspace must be 16-byte aligned");
+  for (const void* ptr : {d->dq, d->dk, d->dv})
+    if (!aligned16(ptr)) return set_error(PDB_ERR_ALIGN, "dq / dk / dv must be 16-byte aligned");
+  for (const int64_t* s : {d->dq_stride, d->dk_stride, d->dv_stride})
+    if ((s[0] | s[1] | s[2]) & 7) return set_error(PDB_ERR_ALIGN, "dq / dk / dv strides must be multiples of 8");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float* lse = d->lse;
+  if (lse == nullptr) {  // recompute the forward's logsumexp
+    uint8_t* ws = static_cast<uint8_t*>(d->workspace);
+    pdb_flash_desc f{};
+    f.q = d->q;
+    f.k = d->k;
+    f.v = d->v;
+    f.o = ws + w.o_scratch;
+    f.lse = reinterpret_cast<float*>(ws + w.lse);
+    f.batch = d->batch;
+    f.heads_q = d->heads_q;
+    f.heads_kv = d->heads_kv;
+    f.seqlen_q = d->seqlen_q;
+    f.seqlen_k = d->seqlen_k;
+    f.head_dim = d->head_dim;
+    f.head_dim_v = d->head_dim_v;
+    for (int i = 0; i < 3; ++i) {
+      f.q_stride[i] = d->q_stride[i];
+      f.k_stride[i] = d->k_stride[i];
+      f.v_stride[i] = d->v_stride[i];
+    }
+    f.o_stride[2] = d->head_dim_v;
+    f.o_stride[1] = d->seqlen_q * d->head_dim_v;
+    f.o_stride[0] = d->heads_q * f.o_stride[1];
+    f.q_start = d->q_start;
+    f.scale = d->scale;
+    f.causal = d->causal;
+    f.dtype = PDB_BF16;
+    if (int st = flash_fwd_bf16_sm100(f, s)) return st;
+    lse = f.lse;
+  }
+  return d->head_dim == 64 ? launch_bwd<64>(*d, lse, w, s) : launch_bwd<128>(*d, lse, w, s);
 }

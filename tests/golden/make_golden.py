@@ -120,10 +120,13 @@ def joint_case(case, T, E, OD, seed):
     names[id(out)] = "out"
     rg = grad(f.naive, "out", seed="dO", names=names)
     shapes, pnames = _param_shapes(rg.region), _param_names(rg.region)
-    arrays = [draw(seed + i, shp, "bf16") for i, shp in enumerate(shapes)]
+    # q is drawn at 1/sqrt(E) so the unscaled region's scores have unit variance (the regime of the
+    # scaled configs); the region itself is the reference's, unchanged
+    scales = [1.0 / np.sqrt(E) if i == 0 else 1.0 for i in range(len(shapes))]
+    arrays = [draw(seed + i, shp, "bf16", scale=sc) for i, (shp, sc) in enumerate(zip(shapes, scales))]
     outs, onames = _run(rg.region, arrays, pnames)
-    spec = [{"seed": seed + i, "shape": list(shp), "names": list(n), "dtype": "bf16", "scale": 1.0,
-             "checksum": input_checksum(a)} for i, (shp, n, a) in enumerate(zip(shapes, pnames, arrays))]
+    spec = [{"seed": seed + i, "shape": list(shp), "names": list(n), "dtype": "bf16", "scale": sc,
+             "checksum": input_checksum(a)} for i, (shp, n, a, sc) in enumerate(zip(shapes, pnames, arrays, scales))]
     save(case, region_kw={"T": T, "E": E, "OD": OD, "causal": True, "scale": None}, inputs_spec=spec,
          outputs=outs, out_names=[list(n) for n in onames], meta={"outputs": list(rg.outputs)})
 
@@ -149,6 +152,7 @@ def main():
     row_case("layernorm_16x4096", "layernorm", 16, 4096, "f32", (411, 412, 413))
     row_case("layernorm_37x1001", "layernorm", 37, 1001, "f32", (414, 415, 416))
     joint_case("flash_joint_bwd", T=64, E=16, OD=16, seed=501)
+    joint_case("flash_joint_bwd_d64", T=200, E=64, OD=64, seed=511)
 
 
 if __name__ == "__main__":

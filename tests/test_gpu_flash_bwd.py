@@ -1,0 +1,83 @@
+"""Flash-attention backward (tcgen05) vs the reference's autodiff joint and the oracle."""
+
+import math
+
+import numpy as np
+import pytest
+
+from oracle import attention as OA
+from tests.golden import load
+from tests.tolerances import assert_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def _np(t):
+    return t.float().cpu().numpy().astype(np.float64)
+
+
+def _bf(a, dev):
+    import torch
+
+    return torch.as_tensor(np.ascontiguousarray(a, dtype=np.float32), device=dev).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("stored_lse", [True, False])
+def test_bwd_matches_autodiff_joint(cuda, stored_lse):
+    """The joint region autodiff.grad builds from the naive causal flash region
+    (the reference's test_partition.py:124-193 subject), evaluated by run_region."""
+    from pdum_dsl_b200 import kernels
+
+    _, (q, k, v, dout), (out, dq, dk, dv) = load("flash_joint_bwd_d64")
+    tq, tk, tv, tdo = (_bf(x, cuda) for x in (q, k, v, dout))
+    o, lse = kernels.flash_attention(tq, tk, tv, scale=1.0, causal=True, return_lse=True)
+    assert_bf16(_np(o), out, what="out")
+    gq, gk, gv = kernels.flash_attention_backward(tq, tk, tv, o, tdo, lse if stored_lse else None, scale=1.0,
+                                                  causal=True)
+    kernels.check_device_errors()
+    assert_bf16(_np(gq), dq, what="dq")
+    assert_bf16(_np(gk), dk, what="dk")
+    assert_bf16(_np(gv).T, dv, what="dv (joint yields (o, s))")
+
+
+@pytest.mark.parametrize("B,H,HKV,T,D,causal", [
+    (1, 1, 1, 128, 64, True), (2, 2, 2, 300, 64, True), (1, 4, 2, 257, 64, True), (1, 2, 1, 200, 128, True),
+    (1, 2, 2, 129, 64, False), (1, 1, 1, 64, 128, False)])
+def test_bwd_shapes_vs_oracle(cuda, B, H, HKV, T, D, causal):
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device="cpu").manual_seed(T * 7 + H)
+    q = torch.randn(B, H, T, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, HKV, T, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, HKV, T, D, generator=g).to(torch.bfloat16)
+    do = torch.randn(B, H, T, D, generator=g).to(torch.bfloat16)
+    scale = 1 / math.sqrt(D)
+    o, lse = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), scale=scale, causal=causal,
+                                     return_lse=True)
+    gq, gk, gv = kernels.flash_attention_backward(q.to(cuda), k.to(cuda), v.to(cuda), o, do.to(cuda), lse,
+                                                  scale=scale, causal=causal)
+    rq, rk, rv = OA.attention_bwd(*(x.double().numpy() for x in (q, k, v, do)), scale=scale, causal=causal)
+    assert_bf16(_np(gq), rq, what="dq")
+    assert_bf16(_np(gk), rk, what="dk")
+    assert_bf16(_np(gv), rv, what="dv")
+
+
+def test_bwd_config5_slices(cuda):
+    """Config 5 (B4 H16 S2048 D64 causal): full-size launch, sampled heads vs the oracle."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device=cuda).manual_seed(5)
+    q, k, v, do = (torch.randn(4, 16, 2048, 64, device=cuda, generator=g).to(torch.bfloat16) for _ in range(4))
+    o, lse = kernels.flash_attention(q, k, v, causal=True, return_lse=True)
+    gq, gk, gv = kernels.flash_attention_backward(q, k, v, o, do, lse, causal=True)
+    kernels.check_device_errors()
+    for b, h in ((0, 0), (3, 15), (2, 7)):
+        rq, rk, rv = OA.attention_bwd(*(x[b, h].double().cpu().numpy() for x in (q, k, v, do)),
+                                      scale=1 / 8, causal=True)
+        assert_bf16(_np(gq[b, h]), rq, what=f"dq ({b},{h})")
+        assert_bf16(_np(gk[b, h]), rk, what=f"dk ({b},{h})")
+        assert_bf16(_np(gv[b, h]), rv, what=f"dv ({b},{h})")

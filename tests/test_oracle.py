@@ -48,8 +48,9 @@ def test_flash_tile_flagship():
     np.testing.assert_allclose(o, z["oracle"], rtol=1e-12, atol=1e-14)
 
 
-def test_backward_oracle_matches_autodiff_joint():
-    spec, (q, k, v, dout), (out, dq, dk, dv) = load("flash_joint_bwd")
+@pytest.mark.parametrize("case", ["flash_joint_bwd", "flash_joint_bwd_d64"])
+def test_backward_oracle_matches_autodiff_joint(case):
+    spec, (q, k, v, dout), (out, dq, dk, dv) = load(case)
     assert spec["outputs"][0] == "out"
     o, *_ = OA.attention_fwd(q, k, v, causal=True)
     gq, gk, gv = OA.attention_bwd(q, k, v, dout, causal=True)
