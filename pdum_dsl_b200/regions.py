@@ -71,11 +71,14 @@ def attention_shapes(B, H, T, S, D, DV, group=None):
 
 
 def attention_region(B=None, H=None, T=6, S=None, D=3, DV=None, *, causal=True, scale=None,
-                     group=None, artifacts=False):
+                     group=None, artifacts=False, all_true_mask=False):
     """The naive (materialised-softmax) attention region; returns the Region.
 
     ``artifacts=True`` yields the tuple ``(out, m, den)`` -- the flash
-    template's artifact variant (``pdum/tl/fusion.py:480-497``)."""
+    template's artifact variant (``pdum/tl/fusion.py:480-497``).
+    ``all_true_mask=True`` (non-causal only) spells "no mask" as a closed
+    always-true mask ``where(iota(s) <= iota(s), sc, -1e9)``, the form the
+    reference's strict flash matcher requires (``fusion.py:468-477``)."""
     Builder, Region, OPS, f64, _, _ = _dsl()
     S = T if S is None else S
     DV = D if DV is None else DV
@@ -87,8 +90,9 @@ def attention_region(B=None, H=None, T=6, S=None, D=3, DV=None, *, causal=True, 
     sc = _contract(b, pq, pk, "e")
     if scale is not None:
         sc = b.emit("tl.pointwise", sc, b.emit("core.const", type=f64, value=float(scale)), f="mul")
-    if causal:
-        mask = b.emit("tl.pointwise", b.emit("tl.iota", sc, name="s"), b.emit("tl.iota", sc, name="t"), f="le")
+    if causal or all_true_mask:
+        other = "t" if causal else "s"
+        mask = b.emit("tl.pointwise", b.emit("tl.iota", sc, name="s"), b.emit("tl.iota", sc, name=other), f="le")
         sc = b.emit("tl.pointwise", mask, sc, b.emit("core.const", type=f64, value=-1e9), f="where")
     pr, mx, den = _softmax(b, sc, "s")
     out = _contract(b, pr, pv, "s")

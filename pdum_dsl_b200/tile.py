@@ -1,0 +1,220 @@
+"""``compile_tile``: the reference lowering's call convention, on sm_100a kernels.
+
+Mirrors ``conformance/triton_tile.py:662-698``:
+
+    run = compile_tile(region, launch=(), prune=())
+    out = run(values)            # values: numpy arrays, positional per region param,
+                                 # each in its param's type-dim order
+    run.source, run.grid         # what runs, and how many programs (CTAs) it launches
+
+``region`` is a plan group's ``kernel`` (the tile region the reference's
+fusion templates emit) or the naive region itself; ``recognize`` decides
+which fixed kernel of ``libpdb_sm100.so`` executes it.  Outputs are
+allocated by the runner (destination passing), returned as float32 numpy
+arrays in the yield's dim order -- a tuple ``(out, m, den)`` for the flash
+artifact variant, as the reference returns.  ``run`` synchronises.
+
+Differences from the Triton column, by design:
+* nothing is generated or JIT-compiled -- the kernels are prebuilt sm_100a;
+* ``dtype="bf16"`` runs the tcgen05 tensor-core path (bf16 operands, fp32
+  accumulate); the default ``"f32"`` is the IEEE CUDA-core path, matching the
+  reference column's refusal of tf32 (triton_tile.py:684-690);
+* ``run_t(*tensors)`` is the zero-copy device-tensor path (no host copies);
+* unsupported regions raise ``Untranslatable`` at compile time -- there is no
+  fallback to the reference evaluator or to any other backend.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from .recognize import AttentionSpec, RowSpec, Untranslatable, recognize
+
+# the executor fingerprint (the reference's Pair seat is keyed the same way, triton_tile.py:54)
+B200_FP = ("tile_sm100a", "pdb")
+
+
+def _check_launch(spec, launch, prune, region):
+    """launch: (output dim, tile) pairs (launch.py:95); prune: (scan dim, lo, hi) affine
+    bounds (fusion.py:659-690).  The kernels tile internally (128/256-row programs) and
+    visit only live key tiles, so these artifacts are validated and recorded, not obeyed."""
+    out_dims = spec.out_dims
+    carried = {spec.s, spec.e} if isinstance(spec, AttentionSpec) else {spec.dim}
+    for name, tile in launch:
+        if name not in out_dims:
+            raise Untranslatable(f"launch dim {name!r} is not an output dim")
+        if name in carried:
+            raise Untranslatable(f"launch dim {name!r} is carried/reduced -- not griddable")
+        if int(tile) <= 0:
+            raise Untranslatable(f"launch tile for {name!r} must be positive")
+    for entry in prune:
+        if not isinstance(spec, AttentionSpec) or not spec.causal:
+            raise Untranslatable("prune bounds only apply to the causal flash template")
+        if entry[0] != "so":
+            raise Untranslatable(f"prune dim {entry[0]!r} is not the flash scan dim")
+
+
+def _extent(region, i, name):
+    d = next(d for d in region.params[i].type.dims if d.name == name)
+    return d.stop - d.start
+
+
+class _Runner:
+    def __init__(self, region, spec, dtype, launch, prune):
+        self.region, self.spec, self.dtype = region, spec, dtype
+        self.launch, self.prune = tuple(launch), tuple(prune)
+        self.checked = False
+        if isinstance(spec, AttentionSpec):
+            T = _extent(region, spec.q, spec.t)
+            heads = 1
+            for n in spec.riders:
+                heads *= _extent(region, spec.k, n)
+            if spec.group:
+                heads *= _extent(region, spec.q, spec.group)
+            rows = 256 if dtype == "bf16" else 64
+            self.grid = heads * -(-T // rows)
+            self.source = (f"pdb_flash_fwd dtype={dtype} causal={spec.causal} scale={spec.scale} "
+                           f"riders={spec.riders} group={spec.group} artifacts={spec.artifacts} "
+                           f"kernel={'flash_fwd_sm100_kernel (tcgen05/TMEM, TMA)' if dtype == 'bf16' else 'flash_f32_kernel (IEEE FMA)'}")
+        else:
+            R = 1
+            for d in region.params[spec.x].type.dims:
+                if d.name != spec.dim:
+                    R *= d.stop - d.start
+            self.grid = R
+            self.source = f"pdb_{'rowsoftmax' if spec.kind == 'softmax' else 'layernorm'}_f32 dim={spec.dim}"
+
+    # ---------------------------------------------------------------- device path
+    def run_t(self, *tensors, out=None):
+        """Device tensors (CUDA, in param type-dim order) -> device tensor(s), no copies."""
+        from . import kernels
+
+        spec = self.spec
+        if isinstance(spec, RowSpec):
+            x = tensors[spec.x]
+            perm = [spec.x_dims.index(n) for n in spec.x_dims if n != spec.dim] + [spec.x_dims.index(spec.dim)]
+            xv = x.permute(*perm)
+            lead = xv.shape[:-1]
+            x2 = xv.reshape(-1, xv.shape[-1])
+            if spec.kind == "softmax":
+                y = kernels.row_softmax(x2)
+            else:
+                g = tensors[spec.gamma] if spec.gamma is not None else None
+                b = tensors[spec.beta] if spec.beta is not None else None
+                y = kernels.layernorm(x2, g, b, eps=spec.eps)
+            ynames = tuple(n for n in spec.x_dims if n != spec.dim) + (spec.dim,)
+            y = y.view(*lead, y.shape[-1])
+            return y.permute(*[ynames.index(n) for n in spec.out_dims])
+        return self._attention(tensors)
+
+    def _attention(self, tensors):
+        import torch
+
+        from . import kernels
+
+        spec = self.spec
+        q, k, v = tensors[spec.q], tensors[spec.k], tensors[spec.v]
+        rid = list(spec.riders)
+        qg = [spec.group] if spec.group else []
+        qv = q.permute(*[spec.q_dims.index(n) for n in rid + qg + [spec.t, spec.e]])
+        kv = k.permute(*[spec.k_dims.index(n) for n in rid + [spec.s, spec.e]])
+        vv = v.permute(*[spec.v_dims.index(n) for n in rid + [spec.s, spec.o]])
+        lead = list(kv.shape[:-2])
+        while len(lead) < 2:  # (batch, heads) with missing riders as 1
+            lead.insert(0, 1)
+        Bn, HK = lead[0], lead[1]
+        G = qv.shape[len(rid)] if spec.group else 1
+        T, D = qv.shape[-2], qv.shape[-1]
+        S, DV = vv.shape[-2], vv.shape[-1]
+        q4 = qv.reshape(Bn, HK * G, T, D)
+        k4 = kv.reshape(Bn, HK, S, D)
+        v4 = vv.reshape(Bn, HK, S, DV)
+        dt = torch.bfloat16 if self.dtype == "bf16" else torch.float32
+        q4, k4, v4 = (x if x.dtype == dt else x.to(dt) for x in (q4, k4, v4))
+        scale = 1.0 if spec.scale is None else spec.scale
+        res = kernels.flash_attention(q4, k4, v4, scale=scale, causal=spec.causal, q_start=spec.t_start,
+                                      return_artifacts=spec.artifacts)
+        o = res[0] if spec.artifacts else res
+        # back to the yield's dim order: (riders..., [group], t, o)
+        onames = tuple(rid + qg + [spec.t, spec.o])
+        o = o.reshape(*qv.shape[:-2], T, DV)
+        o = o.permute(*[onames.index(n) for n in spec.out_dims])
+        if not spec.artifacts:
+            return o
+        snames = tuple(rid + qg + [spec.t])
+        stats = []
+        for st in res[1:3]:
+            st = st.reshape(*qv.shape[:-2], T)
+            stats.append(st.permute(*[snames.index(n) for n in spec.stat_dims]))
+        return (o, *stats)
+
+    # ------------------------------------------------------------------ host path
+    def __call__(self, values):
+        import torch
+
+        if not torch.cuda.is_available():
+            raise RuntimeError("compile_tile runners execute on a CUDA device (sm_100a); none is available")
+        dt = torch.bfloat16 if self.dtype == "bf16" else torch.float32
+        ins = []
+        for i, v in enumerate(values):
+            t = torch.as_tensor(np.ascontiguousarray(v), dtype=torch.float32).cuda()
+            if isinstance(self.spec, AttentionSpec) and i in (self.spec.q, self.spec.k, self.spec.v):
+                t = t.to(dt)
+            ins.append(t)
+        out = self.run_t(*ins)
+        torch.cuda.synchronize()
+        if not self.checked:  # bounded device waits report through the error flag
+            from .kernels import check_device_errors
+
+            check_device_errors()
+            self.checked = True
+        if isinstance(out, tuple):
+            return tuple(o.float().cpu().numpy() for o in out)
+        return out.float().cpu().numpy()
+
+
+def compile_tile(region, launch: tuple = (), prune: tuple = (), *, dtype: str = "f32"):
+    """Region -> runner over the prebuilt sm_100a kernels (see the module docstring)."""
+    if dtype not in ("f32", "bf16"):
+        raise ValueError("dtype must be 'f32' or 'bf16'")
+    spec = recognize(region)
+    if isinstance(spec, RowSpec) and dtype != "f32":
+        raise Untranslatable("row-reduction kernels are f32")
+    if isinstance(spec, AttentionSpec) and dtype == "bf16":
+        D = _extent(region, spec.q, spec.e)
+        DV = _extent(region, spec.v, spec.o)
+        if D != DV or D not in (64, 128):
+            raise Untranslatable(f"bf16 flash needs head dims e == o in (64, 128), got {D}, {DV}")
+    if isinstance(spec, AttentionSpec) and (_extent(region, spec.q, spec.e) > 128 or
+                                            _extent(region, spec.v, spec.o) > 128):
+        raise Untranslatable("flash head dims above 128 are not built")
+    _check_launch(spec, launch, prune, region)
+    runner = _Runner(region, spec, dtype, launch, prune)
+
+    def run(values):
+        return runner(values)
+
+    run.run_t = runner.run_t
+    run.source = runner.source
+    run.grid = runner.grid
+    run.spec = spec
+    run.checked = False
+    return run
+
+
+def flops(region) -> float:
+    """Algorithmic FLOPs of an attention region (causal counted as half)."""
+    spec = recognize(region)
+    if not isinstance(spec, AttentionSpec):
+        return 0.0
+    T = _extent(region, spec.q, spec.t)
+    S = _extent(region, spec.k, spec.s)
+    D = _extent(region, spec.q, spec.e)
+    DV = _extent(region, spec.v, spec.o)
+    heads = math.prod(_extent(region, spec.k, n) for n in spec.riders)
+    if spec.group:
+        heads *= _extent(region, spec.q, spec.group)
+    f = 2.0 * heads * T * S * (D + DV)
+    return f / 2 if spec.causal else f

@@ -22,3 +22,15 @@ def cuda():
     if (major, minor) != (10, 0):
         pytest.fail(f"sm_100a kernels need a B200-class device, got sm_{major}{minor}")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="session")
+def dsl():
+    """The reference DSL (pdum.dsl / pdum.tl) from the shimmed copy in baseline/_ref."""
+    from oracle.make_ref_shim import ensure_importable
+
+    if not ensure_importable():
+        pytest.skip("reference DSL copy not present (python oracle/make_ref_shim.py)")
+    import pdum.tl  # noqa: F401
+
+    return True

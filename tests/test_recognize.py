@@ -1,0 +1,113 @@
+"""Host logic: the recogniser, compile-time refusals and the widened plan_region (CPU)."""
+
+import numpy as np
+import pytest
+
+from pdum_dsl_b200.recognize import AttentionSpec, RowSpec, Untranslatable, recognize
+
+
+def test_flash_tile_naive_and_planned_kernel(dsl):
+    from pdum.tl.fusion import plan_region
+    from pdum.tl.zoo.tiles import flash_tile
+
+    f = flash_tile()
+    spec = recognize(f.naive)
+    assert isinstance(spec, AttentionSpec) and spec.causal and spec.scale is None and spec.riders == ()
+    (g,) = plan_region(f.naive).groups
+    tspec = recognize(g.kernel)  # the generated online-softmax fold (fusion.py:542-615)
+    assert tspec.source == "tile" and tspec.causal and (tspec.t, tspec.s, tspec.e, tspec.o) == ("t", "s", "e", "o")
+    assert recognize(f.region).source == "tile"  # the hand-written tile flagship
+
+
+@pytest.mark.parametrize("kw,expect", [
+    (dict(B=2, H=3, T=8, D=4, causal=True, scale=0.5), dict(riders=("b", "h"), causal=True, scale=0.5)),
+    (dict(B=1, H=4, T=8, D=4, causal=False, scale=0.125), dict(riders=("b", "h"), causal=False, scale=0.125)),
+    (dict(B=1, H=2, T=8, D=4, causal=True, scale=0.125, group=2), dict(riders=("b", "g"), group="r")),
+    (dict(H=2, T=8, S=12, D=4, causal=False), dict(riders=("h",), causal=False, scale=None)),
+    (dict(T=8, D=4, causal=True, artifacts=True), dict(artifacts=True, stat_dims=("t",))),
+])
+def test_widened_attention_spellings(dsl, kw, expect):
+    from pdum_dsl_b200.regions import attention_region
+
+    spec = recognize(attention_region(**kw))
+    for k, v in expect.items():
+        assert getattr(spec, k) == v, (k, getattr(spec, k), v)
+
+
+def test_rows_and_rowstat_carve(dsl):
+    from pdum.tl.fusion import plan_region
+    from pdum.tl.partition import plan_model
+    from pdum.tl.zoo.gpt2 import gpt2
+
+    from pdum_dsl_b200.regions import layernorm_region, row_softmax_region
+
+    s = recognize(row_softmax_region(4, 7))
+    assert isinstance(s, RowSpec) and s.kind == "softmax" and s.dim == "c"
+    (g,) = plan_region(row_softmax_region(4, 7)).groups
+    assert g.template == "row-normalization" and recognize(g.kernel).kind == "softmax"  # staged rows
+    ln = recognize(layernorm_region(4, 7, eps=1e-5))
+    assert ln.kind == "layernorm" and ln.gamma == 1 and ln.beta == 2 and ln.eps == 1e-5
+    pm = plan_model(gpt2().region)  # the reference's device test subject (test_fusion_triton.py:223)
+    carve = next(c for c in pm.carves if c.group.template == "row-statistics")
+    rs = recognize(carve.group.kernel)
+    assert rs.kind == "layernorm"
+
+
+def test_refusals_name_the_reason(dsl):
+    from pdum.dsl.ir import Builder, Region
+    from pdum.dsl.ops import CORE_OPS
+    from pdum.tl.dialect import TL_OPS, tensor_type_of_layout
+    from pdum.tl.tensor import Tensor
+
+    b = Builder({**CORE_OPS, **TL_OPS})
+    x = Tensor.from_numpy(np.zeros((4, 5)), ("m", "k"))
+    px = b.param(0, tensor_type_of_layout(x.layout))
+    y = b.emit("tl.pointwise", px, f="exp")
+    region = Region(params=(px,), body=(b.emit("core.yield", y),))
+    with pytest.raises(Untranslatable, match="no sm_100a template"):
+        recognize(region)
+
+
+def test_sliding_window_mask_is_refused(dsl):
+    from pdum.tl.zoo.attention import sliding_attention
+
+    with pytest.raises(Untranslatable):
+        recognize(sliding_attention().region)
+
+
+def test_compile_tile_checks_launch_and_dtype(dsl):
+    from pdum.tl.fusion import plan_region
+    from pdum.tl.launch import TileLevel, TileMachine
+    from pdum.tl.zoo.tiles import flash_tile
+
+    from pdum_dsl_b200.regions import attention_region
+    from pdum_dsl_b200.tile import compile_tile
+
+    machine = TileMachine((TileLevel("shared", 128, 101376),))
+    f = flash_tile(T=128, E=32, OD=32, SI=2)
+    (g,) = plan_region(f.naive, machine=machine).groups
+    run = compile_tile(g.kernel, g.launch, g.prune)  # the reference's own launch / prune artifacts
+    assert run.grid == 2 and "flash_f32_kernel" in run.source
+    with pytest.raises(Untranslatable, match="not an output dim"):
+        compile_tile(f.naive, (("s", 32),))
+    with pytest.raises(Untranslatable, match="head dims"):
+        compile_tile(f.naive, dtype="bf16")  # E=32 has no tcgen05 build
+    assert compile_tile(attention_region(T=300, D=64, causal=True), dtype="bf16").grid == 2
+
+
+def test_widened_plan_region(dsl):
+    from pdum_dsl_b200.plan import plan_region
+    from pdum_dsl_b200.regions import attention_region
+
+    for kw in (dict(B=1, H=2, T=200, D=64, causal=True, scale=0.125),
+               dict(B=1, H=2, T=64, D=16, causal=False, scale=0.25),
+               dict(B=1, H=2, T=64, D=16, causal=True, scale=0.25, group=2)):
+        (g,) = plan_region(attention_region(**kw)).groups
+        assert g.template == "flash" and g.confidence == "yellow"
+        assert g.certificate.verdict == "licensed-differential"
+        assert "flash.online-softmax" in g.certificate.licenses
+        assert dict(g.params)["causal"] == kw["causal"]
+    from pdum_dsl_b200.regions import row_softmax_region
+
+    (g,) = plan_region(row_softmax_region(4, 8)).groups  # untouched rows stay the reference's
+    assert g.template == "row-normalization"
