@@ -37,6 +37,7 @@ constexpr int BN = 128;          // keys per tile
 constexpr int kThreads = 384;    // 3 warpgroups
 constexpr int kBoxBytes = 64 * 128 * 2;  // one TMA box: 128 rows x 64 bf16 (128 B, swizzled)
 constexpr float kRescaleThreshold = 8.0f;
+constexpr int kPolyPair = 3;  // pairs i with i % 4 == 3 use exp2_poly3 (25 % of the exponentials)
 
 struct __align__(8) Barriers {
   uint64_t q_full;
@@ -243,29 +244,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < n; ++j) {
       if (!(ok = mbar_wait(&bar->s_full[x], j & 1, abort, p.err))) break;
       tc_fence_after();
-      float s[BN];
-      {
-        uint32_t r[BN];
-#pragma unroll
-        for (int ch = 0; ch < BN / 32; ++ch)
-          tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(r + ch * 32));
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < BN; ++i) s[i] = __uint_as_float(r[i]);
-      }
       // keys at or past `lim` (tile-relative) are masked for this row
       int lim = p.S - j * BN;
       if (p.causal) {
         const int lc = t + p.q_start + 1 - j * BN;
         lim = lc < lim ? lc : lim;
       }
-      if (__any_sync(0xffffffffu, lim < BN)) {
+      const bool need_mask = __any_sync(0xffffffffu, lim < BN);
+      // pass 1: row max, two 32-column chunks in flight
+      float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < BN; ++i) s[i] = (i < lim) ? s[i] : -INFINITY;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tS + half * 64, r0);
+        tmem_ld32(tS + half * 64 + 32, r1);
+        tmem_wait_ld();
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (half * 64 + i >= lim) r0[i] = __float_as_uint(-INFINITY);
+            if (half * 64 + 32 + i >= lim) r1[i] = __float_as_uint(-INFINITY);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          mx = max3(mx, __uint_as_float(r0[i]), __uint_as_float(r0[i + 1]));
+          mx = max3(mx, __uint_as_float(r1[i]), __uint_as_float(r1[i + 1]));
+        }
       }
-      float mx = s[0];
-#pragma unroll
-      for (int i = 1; i < BN; ++i) mx = fmaxf(mx, s[i]);
       const float mt = mx * c;
       m_true = fmaxf(m_true, mt);
       if (j == 0) {
@@ -287,14 +293,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+      // pass 2: P = exp2(s c - m) as bf16 pairs over the first 64 columns of S
+      // (P chunk ch lands on columns already read: 16 ch < 32 (ch + 1))
       float rs = 0.f;
 #pragma unroll
       for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(tS + ch * 32, r);
+        tmem_wait_ld();
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (ch * 32 + i >= lim) r[i] = __float_as_uint(-INFINITY);
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2(fmaf(s[ch * 32 + 2 * i], c, neg_m));
-          const float p1 = ex2(fmaf(s[ch * 32 + 2 * i + 1], c, neg_m));
+          // one pair in four goes through the FMA-pipe polynomial, the rest through MUFU
+          const float x0 = fmaf(__uint_as_float(r[2 * i]), c, neg_m);
+          const float x1 = fmaf(__uint_as_float(r[2 * i + 1]), c, neg_m);
+          const bool poly = (i & 3) == kPolyPair;
+          const float p0 = poly ? exp2_poly3(x0) : ex2(x0);
+          const float p1 = poly ? exp2_poly3(x1) : ex2(x1);
           rs += p0 + p1;
           pk[i] = pack_bf16(p0, p1);
         }
