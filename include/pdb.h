@@ -140,6 +140,20 @@ typedef struct {
 size_t pdb_flash_bwd_workspace_size(const pdb_flash_bwd_desc* d);
 int pdb_flash_bwd(const pdb_flash_bwd_desc* d, void* stream);
 
+/* ---- flash attention backward without caller workspace ----------------------
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory when they call (a pool or arena owns the device, or a plain C
+ * caller has no allocator): same descriptor and results as pdb_flash_bwd, but
+ * `workspace` / `workspace_bytes` are ignored and the scratch comes from a
+ * fixed 16 MiB array inside the library, held on every device that loads it.
+ * Problems whose scratch (pdb_flash_bwd_workspace_size) exceeds
+ * pdb_flash_bwd_noalloc_max_scratch() are refused with PDB_ERR_SHAPE.  The
+ * first call on a device looks up the array's address (make it before any
+ * stream capture); calls that may overlap on the GPU share the array and
+ * race, so the caller must order them.  Nothing is allocated or freed. */
+int pdb_flash_bwd_noalloc(const pdb_flash_bwd_desc* d, void* stream);
+size_t pdb_flash_bwd_noalloc_max_scratch(void);
+
 /* ---- status --------------------------------------------------------------------
  * pdb_check_error synchronises `stream`, reads and clears the device error flag
  * of the current device (set by bounded waits that expired) and returns

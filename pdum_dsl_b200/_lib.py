@@ -32,6 +32,8 @@ EXPORTS = (
     "pdb_flash_fwd",
     "pdb_flash_bwd",
     "pdb_flash_bwd_workspace_size",
+    "pdb_flash_bwd_noalloc",
+    "pdb_flash_bwd_noalloc_max_scratch",
     "pdb_check_error",
     "pdb_last_error_string",
     "pdb_version",
@@ -165,12 +167,16 @@ def load(path: Path | None = None) -> C.CDLL:
     lib.pdb_flash_bwd.argtypes = [C.POINTER(FlashBwdDesc), vp]
     lib.pdb_flash_bwd_workspace_size.argtypes = [C.POINTER(FlashBwdDesc)]
     lib.pdb_flash_bwd_workspace_size.restype = C.c_size_t
+    lib.pdb_flash_bwd_noalloc.argtypes = [C.POINTER(FlashBwdDesc), vp]
+    lib.pdb_flash_bwd_noalloc_max_scratch.argtypes = []
+    lib.pdb_flash_bwd_noalloc_max_scratch.restype = C.c_size_t
     lib.pdb_check_error.argtypes = [vp]
     lib.pdb_last_error_string.restype = C.c_char_p
     lib.pdb_version.restype = C.c_char_p
     for name in EXPORTS:
         f = getattr(lib, name)
-        if name not in ("pdb_flash_bwd_workspace_size", "pdb_last_error_string", "pdb_version"):
+        if name not in ("pdb_flash_bwd_workspace_size", "pdb_flash_bwd_noalloc_max_scratch",
+                        "pdb_last_error_string", "pdb_version"):
             f.restype = C.c_int
     if path is None:
         _LIB = lib

@@ -21,6 +21,7 @@
 // dQ = scale dS K, dK = scale dS^T Q; everything accumulates in fp32 (TMEM)
 // and is rounded to bf16 once.  No atomics: the result is deterministic.
 #include <cfloat>
+#include <mutex>
 
 #include "common.cuh"
 #include "tma.h"
@@ -620,4 +621,63 @@ extern "C" int pdb_flash_bwd(const pdb_flash_bwd_desc* d, void* stream) {
     lse = f.lse;
   }
   return d->head_dim == 64 ? launch_bwd<64>(*d, lse, w, s) : launch_bwd<128>(*d, lse, w, s);
+}
+
+// ---------------------------------------------------------------------------
+// pdb_flash_bwd_noalloc: the same backward with its scratch in a fixed,
+// library-owned device array instead of a caller-supplied workspace.
+//
+// Who needs it: callers that may not allocate device memory at call time --
+// code running inside a memory pool or arena that owns every byte of the
+// device, hosts whose allocator is locked while a step is in flight, or C
+// callers with no allocator binding at all.  They pass inputs and outputs
+// only.  The scratch (D and lse2 rows, plus the recomputed lse and a scratch
+// forward output when lse is NULL) lives in g_bwd_scratch below; its address
+// is looked up once per device, on the first call made with that device
+// current (so make that first call before any stream capture).  The prologue
+// kernel rewrites every scratch word it later reads on each call, so nothing
+// has to be cleared between calls.  Every call on a device shares the one
+// array: calls that can overlap on the GPU (different streams without
+// ordering) race on it and must be serialised by the caller.
+namespace pdb {
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB per device
+static __device__ __align__(256) uint8_t g_bwd_scratch[kNoAllocScratchBytes];
+constexpr int kMaxDev = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxDev];
+}  // namespace
+}  // namespace pdb
+
+extern "C" size_t pdb_flash_bwd_noalloc_max_scratch(void) { return pdb::kNoAllocScratchBytes; }
+
+extern "C" int pdb_flash_bwd_noalloc(const pdb_flash_bwd_desc* d, void* stream) {
+  using namespace pdb;
+  if (!d) return set_error(PDB_ERR_ARG, "null descriptor");
+  if (d->batch <= 0 || d->heads_q <= 0 || d->seqlen_q <= 0)
+    return set_error(PDB_ERR_SHAPE, "all sizes must be positive");
+  const WsLayout w = ws_layout(*d);
+  if (w.total > kNoAllocScratchBytes)
+    return set_error(PDB_ERR_SHAPE,
+                     "pdb_flash_bwd_noalloc: problem needs %zu scratch bytes, the fixed scratch holds %zu "
+                     "(use pdb_flash_bwd with a caller workspace)",
+                     w.total, kNoAllocScratchBytes);
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev)) return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDev) return set_error(PDB_ERR_CUDA, "device index out of range");
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (g_scratch_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_bwd_scratch);
+      if (e != cudaSuccess || p == nullptr) return cuda_status(e, "cudaGetSymbolAddress(g_bwd_scratch)");
+      g_scratch_ptr[dev] = p;
+    }
+    ptr = g_scratch_ptr[dev];
+  }
+  pdb_flash_bwd_desc local = *d;
+  local.workspace = ptr;
+  local.workspace_bytes = kNoAllocScratchBytes;
+  return pdb_flash_bwd(&local, stream);
 }
