@@ -154,6 +154,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sK = smem_u32(smem + L::kK), sV = smem_u32(smem + L::kV);
   constexpr int kNB = D / 64;  // boxes per tile
 
+  // Register split (per warpgroup): the control warpgroup hands registers to
+  // the two softmax warpgroups.  Launch budget 384 x 168 = 64512
+  // = 128 x 56 + 256 x 224.
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -228,7 +233,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
     // ------------------------------------------------------------- softmax
     const int x = (warp >= 8) ? 1 : 0;  // tile A / B
     const int q4 = warp & 3;            // TMEM lane quadrant of this warp
@@ -251,28 +258,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         lim = lc < lim ? lc : lim;
       }
       const bool need_mask = __any_sync(0xffffffffu, lim < BN);
-      // pass 1: row max, two 32-column chunks in flight
-      float mx = -INFINITY;
+      // all 128 scores of the row in registers: one TMEM round trip
+      uint32_t sr[BN];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(tS + half * 64, r0);
-        tmem_ld32(tS + half * 64 + 32, r1);
-        tmem_wait_ld();
-        if (need_mask) {
+      for (int ch = 0; ch < BN / 32; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
+      tmem_wait_ld();
+      if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (half * 64 + i >= lim) r0[i] = __float_as_uint(-INFINITY);
-            if (half * 64 + 32 + i >= lim) r1[i] = __float_as_uint(-INFINITY);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          mx = max3(mx, __uint_as_float(r0[i]), __uint_as_float(r0[i + 1]));
-          mx = max3(mx, __uint_as_float(r1[i]), __uint_as_float(r1[i + 1]));
-        }
+        for (int i = 0; i < BN; ++i)
+          if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
       }
-      const float mt = mx * c;
+      float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;  // 4 independent chains
+#pragma unroll
+      for (int i = 0; i < BN; i += 8) {
+        mxa = max3(mxa, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+        mxb = max3(mxb, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
+        mxc = max3(mxc, __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
+        mxd = max3(mxd, __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
+      }
+      const float mt = fmaxf(max3(mxa, mxb, mxc), mxd) * c;
       m_true = fmaxf(m_true, mt);
       if (j == 0) {
         m_used = mt;
@@ -295,32 +299,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
       // pass 2: P = exp2(s c - m) as bf16 pairs over the first 64 columns of S
       // (P chunk ch lands on columns already read: 16 ch < 32 (ch + 1))
-      float rs = 0.f;
+      float rsa = 0.f, rsb = 0.f;  // two independent sum chains
 #pragma unroll
       for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t r[32];
-        tmem_ld32(tS + ch * 32, r);
-        tmem_wait_ld();
-        if (need_mask) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (ch * 32 + i >= lim) r[i] = __float_as_uint(-INFINITY);
-        }
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           // one pair in four goes through the FMA-pipe polynomial, the rest through MUFU
-          const float x0 = fmaf(__uint_as_float(r[2 * i]), c, neg_m);
-          const float x1 = fmaf(__uint_as_float(r[2 * i + 1]), c, neg_m);
+          const float x0 = fmaf(__uint_as_float(sr[ch * 32 + 2 * i]), c, neg_m);
+          const float x1 = fmaf(__uint_as_float(sr[ch * 32 + 2 * i + 1]), c, neg_m);
           const bool poly = (i & 3) == kPolyPair;
           const float p0 = poly ? exp2_poly3(x0) : ex2(x0);
           const float p1 = poly ? exp2_poly3(x1) : ex2(x1);
-          rs += p0 + p1;
+          if (i & 1) rsb += p0 + p1; else rsa += p0 + p1;
           pk[i] = pack_bf16(p0, p1);
         }
         tmem_st16(tS + ch * 16, pk);
       }
-      l += rs;
+      l += rsa + rsb;
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar->p_full[x]);
