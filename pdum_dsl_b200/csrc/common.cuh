@@ -207,22 +207,24 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, for x in [-126, 126]: Cody-Waite split x = n + f with
-// n = rint(x) (the 1.5 * 2^23 shifter) and f in [-1/2, 1/2], a degree-3
-// polynomial for 2^f (coefficients fitted for minimum relative error on
-// [-1/2, 1/2] by iteratively reweighted least squares; max rel. error
-// 7.6e-5, far below bf16's 2^-9), and n added straight into the exponent
-// field.  Used for a fraction of the softmax exponentials so that the MUFU
-// unit and the FMA pipe share the work.
-__device__ __forceinline__ float exp2_poly3(float x) {
-  x = fmaxf(x, -126.0f);
-  const float t = x + 12582912.0f;
-  const float n = t - 12582912.0f;
-  const float f = x - n;
-  float p = fmaf(0.055174145847558975f, f, 0.24261757731437683f);
-  p = fmaf(p, f, 0.6932610869407654f);
-  p = fmaf(p, f, 0.9999275803565979f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// Packed f32x2 arithmetic (sm_100): one instruction for two fp32 lanes.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
 }
 
 __device__ __forceinline__ float max3(float a, float b, float c) {

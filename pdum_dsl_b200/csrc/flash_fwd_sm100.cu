@@ -37,7 +37,6 @@ constexpr int BN = 128;          // keys per tile
 constexpr int kThreads = 384;    // 3 warpgroups
 constexpr int kBoxBytes = 64 * 128 * 2;  // one TMA box: 128 rows x 64 bf16 (128 B, swizzled)
 constexpr float kRescaleThreshold = 8.0f;
-constexpr int kPolyPair = 3;  // pairs i with i % 4 == 3 use exp2_poly3 (25 % of the exponentials)
 
 struct __align__(8) Barriers {
   uint64_t q_full;
@@ -299,23 +298,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
       // pass 2: P = exp2(s c - m) as bf16 pairs over the first 64 columns of S
       // (P chunk ch lands on columns already read: 16 ch < 32 (ch + 1))
-      float rsa = 0.f, rsb = 0.f;  // two independent sum chains
+      // P = exp2(s c - m): packed f32x2 FMA for the argument, MUFU ex2 per
+      // element, packed f32x2 adds for the row sum (two independent chains)
+      const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(neg_m, neg_m);
+      uint64_t sum_a = 0, sum_b = 0;
 #pragma unroll
       for (int ch = 0; ch < BN / 32; ++ch) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          // one pair in four goes through the FMA-pipe polynomial, the rest through MUFU
-          const float x0 = fmaf(__uint_as_float(sr[ch * 32 + 2 * i]), c, neg_m);
-          const float x1 = fmaf(__uint_as_float(sr[ch * 32 + 2 * i + 1]), c, neg_m);
-          const bool poly = (i & 3) == kPolyPair;
-          const float p0 = poly ? exp2_poly3(x0) : ex2(x0);
-          const float p1 = poly ? exp2_poly3(x1) : ex2(x1);
-          if (i & 1) rsb += p0 + p1; else rsa += p0 + p1;
+          const uint64_t sv = (uint64_t)sr[ch * 32 + 2 * i] | ((uint64_t)sr[ch * 32 + 2 * i + 1] << 32);
+          float x0, x1;
+          f2_unpack(f2_fma(sv, c2, nm2), x0, x1);
+          const float p0 = ex2(x0), p1 = ex2(x1);
+          const uint64_t pv = f2_pack(p0, p1);
+          if (i & 1) sum_b = f2_add(sum_b, pv); else sum_a = f2_add(sum_a, pv);
           pk[i] = pack_bf16(p0, p1);
         }
         tmem_st16(tS + ch * 16, pk);
       }
+      float sa0, sa1, sb0, sb1;
+      f2_unpack(sum_a, sa0, sa1);
+      f2_unpack(sum_b, sb0, sb1);
+      const float rsa = sa0 + sa1, rsb = sb0 + sb1;
       l += rsa + rsb;
       tmem_wait_st();
       tc_fence_before();
