@@ -110,9 +110,10 @@ def _dist():
 
 
 def _shard(world, rank):
-    units = B * H
-    lo, hi = units * rank // world, units * (rank + 1) // world
-    return lo, hi
+    from pdum_dsl_b200.partition import shard_units
+
+    sh = shard_units(B * H, world, rank)
+    return sh.lo, sh.hi
 
 
 def _timed(fn, steps, warmup, stream, world):
@@ -230,9 +231,19 @@ def run_ours(args):
     launch_ms = sum(per) / len(per)
     achieved = flop_rank / (launch_ms * 1e-3) / 1e12
 
+    gather = None
+    if world > 1 and (B * H) % world == 0:
+        # the north star's final NCCL gather of the output shards, timed on its own
+        full = torch.empty((world * units, S, D), dtype=o.dtype, device=dev)
+        g_ms, _ = _timed(lambda: dist.all_gather_into_tensor(full, o.reshape(units, S, D)), 5, 2, stream, world)
+        nbytes = o.numel() * o.element_size()
+        gather = {"ms": g_ms / 5, "bytes_in_per_rank": nbytes * (world - 1),
+                  "GB/s_in_per_rank": nbytes * (world - 1) / (g_ms / 5 * 1e-3) / 1e9,
+                  "note": "all_gather_into_tensor of o shards over NCCL; outside `value`"}
+        del full
     if args.kernel_only:
         if rank == 0:
-            print(json.dumps({"workload": [B, H, S, D], "value": value, "unit": "TFLOP/s", "launch_ms": launch_ms,
+            print(json.dumps({"workload": [B, H, S, D], "n_gpus": world, "gather": gather, "value": value, "unit": "TFLOP/s", "launch_ms": launch_ms,
                               "achieved": achieved, "clocks": sampler.summary()}), flush=True)
         return
     # ---- e2e: the same step through the public API with pinned host buffers
@@ -284,6 +295,7 @@ def run_ours(args):
             "gpu_launches": args.steps,
             "cpu_baseline": cpu_base,
             "extra": extra,
+            "gather": gather,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
