@@ -36,7 +36,7 @@ namespace {
 constexpr int BT = 128;  // query rows per tile
 constexpr int BS = 128;  // keys per tile
 constexpr int kBox = 64 * 128 * 2;
-constexpr int kThreads = 256;  // warp0 TMA, warp1 MMA, warp2 TMEM, warps 4..7 compute
+constexpr int kThreads = 384;  // warp0 TMA, warp1 MMA, warp2 TMEM, warps 4..11 two compute warpgroups
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdParams {
@@ -59,29 +59,35 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+// ---- MMA helpers.  Operand tiles are TMA boxes of 64 features x `rows` rows
+// (128-byte swizzle), so a feature-chunk of 64 sits `rows * 128` bytes after
+// the previous one.
+// D (M x N) (+)= A (M x K=D, K-major smem) * B (N x K=D, K-major smem)^T
 template <int D>
-__device__ __forceinline__ void mma_kmajor(uint32_t d_tmem, uint32_t a_saddr, uint32_t b_saddr) {
-  constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
+__device__ __forceinline__ void mma_kmajor(uint32_t d_tmem, uint32_t a_saddr, uint32_t a_box, uint32_t b_saddr,
+                                           uint32_t b_box, uint32_t idesc) {
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-    mma_ss(d_tmem, sdesc_sw128(a_saddr + off, 16, 1024), sdesc_sw128(b_saddr + off, 16, 1024), idesc, kk > 0);
+    const uint32_t o = (kk & 3) * 32;
+    mma_ss(d_tmem, sdesc_sw128(a_saddr + (kk >> 2) * a_box + o, 16, 1024),
+           sdesc_sw128(b_saddr + (kk >> 2) * b_box + o, 16, 1024), idesc, kk > 0);
   }
 }
 
-// D (128 x D) (+)= A_tmem (128 x 128, bf16 packed) * B_smem (128 rows x D, MN-major)
-template <int D>
-__device__ __forceinline__ void mma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_saddr, bool acc) {
-  constexpr uint32_t idesc = idesc_bf16(128, D, 0, 1);
+// D (128 x D) (+)= A_tmem (128 x K, bf16 packed pairs) * B_smem (K rows x D, MN-major, box `b_box` bytes)
+template <int K>
+__device__ __forceinline__ void mma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_saddr, uint32_t b_box,
+                                           uint32_t idesc, bool acc) {
 #pragma unroll
-  for (int kk = 0; kk < 128 / 16; ++kk)
-    mma_ts(d_tmem, a_tmem + kk * 8, sdesc_sw128(b_saddr + kk * 2048, kBox, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
+  for (int kk = 0; kk < K / 16; ++kk)
+    mma_ts(d_tmem, a_tmem + kk * 8, sdesc_sw128(b_saddr + kk * 2048, b_box, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
 }
 
-template <int D>
-__device__ __forceinline__ void store_rows_bf16(uint32_t t_src, float mul, __nv_bfloat16* row, bool store) {
+// rows of a TMEM accumulator (columns [c0, c0 + NC)) -> bf16 global, scaled
+template <int NC>
+__device__ __forceinline__ void store_cols_bf16(uint32_t t_src, float mul, __nv_bfloat16* row, bool store) {
 #pragma unroll
-  for (int ch = 0; ch < D / 32; ++ch) {
+  for (int ch = 0; ch < NC / 32; ++ch) {
     uint32_t r[32];
     tmem_ld32(t_src + ch * 32, r);
     tmem_wait_ld();
@@ -96,15 +102,47 @@ __device__ __forceinline__ void store_rows_bf16(uint32_t t_src, float mul, __nv_
   }
 }
 
+// P, dS for 64 score columns held by one thread: p = exp2(s c - l2), ds = p (dp - dsum).
+// `valid(col)` masks causal positions; l2 / dsum per column (dK/dV) or per row (dQ).
+template <class ColL2, class ColDs, class Valid>
+__device__ __forceinline__ void p_ds_64(const uint32_t (&sr)[64], const uint32_t (&dr)[64], float c, ColL2 l2,
+                                        ColDs ds_of, Valid valid, uint32_t (&pp)[32], uint32_t (&dd)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float pv[2], dv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int col = 2 * i + u;
+      float pr = ex2(fmaf(__uint_as_float(sr[col]), c, -l2(col)));
+      pr = valid(col) ? pr : 0.f;
+      pv[u] = pr;
+      dv[u] = pr * (__uint_as_float(dr[col]) - ds_of(col));
+    }
+    pp[i] = pack_bf16(pv[0], pv[1]);
+    dd[i] = pack_bf16(dv[0], dv[1]);
+  }
+}
+
+constexpr int QT = 64;   // query rows per dK/dV work item
+constexpr int KT = 64;   // keys per dQ work item
+constexpr int kStages = 3;
+
 struct __align__(8) BarsKV {
   uint64_t kv_full;
-  uint64_t q_full[2], q_empty[2];
-  uint64_t s_full, p_full, o_full;
+  uint64_t q_full[kStages], q_empty[kStages];
+  uint64_t s_full[2], p_full[2];
+  uint64_t o_full;
   uint32_t tmem_base;
   int abort;
 };
 
 // ------------------------------------------------------------------ dK / dV
+// CTA = 128 keys of one (batch, KV head).  Work items: (query head of the
+// group, 64-row query tile).  TMEM buffer x in {0, 1}: S^T [128x, 128x+64),
+// dP^T [128x+64, 128x+128) (P^T / dS^T written back as bf16 into their first
+// 32 columns); dV [256, 256+D), dK [256+D, 256+2D).  Compute warpgroup x
+// handles the items i = x mod 2, so one warpgroup computes while the tensor
+// core runs the other's MMAs.
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -112,37 +150,41 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kTile = 128 * D * 2;
+  constexpr int kKV = 128 * D * 2;  // K or V tile
+  constexpr int kQ = QT * D * 2;    // Q or dO tile
+  constexpr uint32_t kBoxKV = 128 * 128, kBoxQ = QT * 128;
   uint8_t* sK = smem;
-  uint8_t* sV = smem + kTile;
-  uint8_t* sQ = smem + 2 * kTile;   // 2 stages
-  uint8_t* sDO = smem + 4 * kTile;  // 2 stages
-  float* sVec = reinterpret_cast<float*>(smem + 6 * kTile);  // 2 stages x (lse2[128], dsum[128])
-  BarsKV* bar = reinterpret_cast<BarsKV*>(smem + 6 * kTile + 2 * 2 * 128 * 4);
+  uint8_t* sV = smem + kKV;
+  uint8_t* sQ = smem + 2 * kKV;                 // kStages
+  uint8_t* sDO = sQ + kStages * kQ;             // kStages
+  float* sVec = reinterpret_cast<float*>(sDO + kStages * kQ);  // kStages x (lse2[64], dsum[64])
+  BarsKV* bar = reinterpret_cast<BarsKV*>(reinterpret_cast<uint8_t*>(sVec) + kStages * 2 * QT * 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   const int bhk = blockIdx.x / p.n_blocks;
   const int nblk = blockIdx.x % p.n_blocks;
   const int b = bhk / p.HKV, hk = bhk % p.HKV;
   const int group = p.H / p.HKV;
-  const int s0 = nblk * BS;
-  const int n_qt = p.Tpad / BT;
+  const int s0 = nblk * 128;
+  const int n_qt = p.Tpad / QT;
   int qt0 = 0;
   if (p.causal) {
     const int first = s0 - p.q_start;  // first query row that can see key s0
-    qt0 = first > 0 ? first / BT : 0;
+    qt0 = first > 0 ? first / QT : 0;
   }
   const int per_head = n_qt - qt0 > 0 ? n_qt - qt0 : 0;
   const int n_items = per_head * group;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&bar->q_full[i], 1);
       mbar_init(&bar->q_empty[i], 1);
     }
-    mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->p_full, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->s_full[i], 1);
+      mbar_init(&bar->p_full[i], 128);
+    }
     mbar_init(&bar->o_full, 1);
     bar->abort = 0;
     fence_barrier_init();
@@ -157,114 +199,102 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bar->tmem_base;
   volatile int* abort = &bar->abort;
   constexpr int kNB = D / 64;
-  // TMEM: S^T [0,128) (P^T in [0,64)), dP^T [128,256) (dS^T in [128,192)), dV [256,256+D), dK [256+D, 256+2D)
+  constexpr uint32_t idS = idesc_bf16(128, QT, 0, 0);  // S^T, dP^T: M = 128 keys, N = 64 queries
+  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);   // dV, dK: M = 128 keys, N = D, B MN-major
 
-  if (warp == 0) {
-    if (lane == 0) {
-      mbar_expect_tx(&bar->kv_full, 2 * kTile);
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+    if (warp == 0 && lane == 0) {
+      mbar_expect_tx(&bar->kv_full, 2 * kKV);
       for (int i = 0; i < kNB; ++i) {
-        tma_load_4d(sK + i * kBox, &tm_k, &bar->kv_full, i * 64, s0, hk, b);
-        tma_load_4d(sV + i * kBox, &tm_v, &bar->kv_full, i * 64, s0, hk, b);
+        tma_load_4d(sK + i * kBoxKV, &tm_k, &bar->kv_full, i * 64, s0, hk, b);
+        tma_load_4d(sV + i * kBoxKV, &tm_v, &bar->kv_full, i * 64, s0, hk, b);
       }
       for (int it = 0; it < n_items; ++it) {
-        const int st = it & 1;
-        const uint32_t ph = (it >> 1) & 1;
+        const int st = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
         const int h = hk * group + it / per_head;
-        const int t0 = (qt0 + it % per_head) * BT;
+        const int t0 = (qt0 + it % per_head) * QT;
         if (!mbar_wait(&bar->q_empty[st], ph ^ 1, abort, p.err)) break;
-        mbar_expect_tx(&bar->q_full[st], 2 * kTile + 2 * 128 * 4);
+        mbar_expect_tx(&bar->q_full[st], 2 * kQ + 2 * QT * 4);
         for (int i = 0; i < kNB; ++i) {
-          tma_load_4d(sQ + st * kTile + i * kBox, &tm_q, &bar->q_full[st], i * 64, t0, h, b);
-          tma_load_4d(sDO + st * kTile + i * kBox, &tm_do, &bar->q_full[st], i * 64, t0, h, b);
+          tma_load_4d(sQ + st * kQ + i * kBoxQ, &tm_q, &bar->q_full[st], i * 64, t0, h, b);
+          tma_load_4d(sDO + st * kQ + i * kBoxQ, &tm_do, &bar->q_full[st], i * 64, t0, h, b);
         }
         const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
-        bulk_load(sVec + st * 256, p.lse2 + vrow, 512, &bar->q_full[st]);
-        bulk_load(sVec + st * 256 + 128, p.dsum + vrow, 512, &bar->q_full[st]);
+        bulk_load(sVec + st * 2 * QT, p.lse2 + vrow, QT * 4, &bar->q_full[st]);
+        bulk_load(sVec + st * 2 * QT + QT, p.dsum + vrow, QT * 4, &bar->q_full[st]);
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
+      auto issue_s = [&](int it) -> bool {
+        const int st = it % kStages, x = it & 1;
+        if (!mbar_wait(&bar->q_full[st], (it / kStages) & 1, abort, p.err)) return false;
+        tc_fence_after();
+        mma_kmajor<D>(tmem + x * 128, smem_u32(sK), kBoxKV, smem_u32(sQ + st * kQ), kBoxQ, idS);        // S^T
+        mma_kmajor<D>(tmem + x * 128 + 64, smem_u32(sV), kBoxKV, smem_u32(sDO + st * kQ), kBoxQ, idS);  // dP^T
+        tc_commit(&bar->s_full[x]);
+        return true;
+      };
       bool ok = mbar_wait(&bar->kv_full, 0, abort, p.err);
+      if (ok && n_items > 0) ok = issue_s(0);
+      if (ok && n_items > 1) ok = issue_s(1);
       for (int it = 0; ok && it < n_items; ++it) {
-        const int st = it & 1;
-        const uint32_t ph = (it >> 1) & 1;
-        if (!(ok = mbar_wait(&bar->q_full[st], ph, abort, p.err))) break;
+        const int st = it % kStages, x = it & 1;
+        if (!(ok = mbar_wait(&bar->p_full[x], (it >> 1) & 1, abort, p.err))) break;
         tc_fence_after();
-        mma_kmajor<D>(tmem + 0, smem_u32(sK), smem_u32(sQ + st * kTile));      // S^T = K Q^T
-        mma_kmajor<D>(tmem + 128, smem_u32(sV), smem_u32(sDO + st * kTile));  // dP^T = V dO^T
-        tc_commit(&bar->s_full);
-        if (!(ok = mbar_wait(&bar->p_full, it & 1, abort, p.err))) break;
-        tc_fence_after();
-        mma_tmem_a<D>(tmem + 256, tmem + 0, smem_u32(sDO + st * kTile), it > 0);    // dV += P^T dO
-        mma_tmem_a<D>(tmem + 256 + D, tmem + 128, smem_u32(sQ + st * kTile), it > 0);  // dK += dS^T Q
+        mma_tmem_a<QT>(tmem + 256, tmem + x * 128, smem_u32(sDO + st * kQ), kBoxQ, idG, it > 0);      // dV += P^T dO
+        mma_tmem_a<QT>(tmem + 256 + D, tmem + x * 128 + 64, smem_u32(sQ + st * kQ), kBoxQ, idG, it > 0);  // dK += dS^T Q
         tc_commit(&bar->q_empty[st]);
+        if (it + 2 < n_items) ok = issue_s(it + 2);
       }
       if (ok) tc_commit(&bar->o_full);
     }
-  } else if (warp >= 4) {
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+    const int x = warp >= 8 ? 1 : 0;
     const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;  // key row within the block
+    const int row = q4 * 32 + lane;  // key row within the block (TMEM lane)
     const int s = s0 + row;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tb = tmem + lane_off + x * 128;
     const float c = p.scale_log2;
     bool ok = true;
-    for (int it = 0; it < n_items; ++it) {
-      const int st = it & 1;
-      const uint32_t ph = (it >> 1) & 1;
-      const int t0 = (qt0 + it % per_head) * BT;
-      if (!(ok = mbar_wait(&bar->q_full[st], ph, abort, p.err))) break;
-      if (!(ok = mbar_wait(&bar->s_full, it & 1, abort, p.err))) break;
+    for (int it = x; it < n_items; it += 2) {
+      const int st = it % kStages;
+      const int t0 = (qt0 + it % per_head) * QT;
+      if (!(ok = mbar_wait(&bar->q_full[st], (it / kStages) & 1, abort, p.err))) break;
+      if (!(ok = mbar_wait(&bar->s_full[x], (it >> 1) & 1, abort, p.err))) break;
       tc_fence_after();
-      const float* lse2 = sVec + st * 256;
-      const float* dsum = lse2 + 128;
-      // query columns below `lo` are masked for this key (causal: t + q_start >= s)
-      const int lo = p.causal ? s - p.q_start - t0 : -1;
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tmem + lane_off + ch * 32, sr);
-        tmem_ld32(tmem + lane_off + 128 + ch * 32, dr);
-        tmem_wait_ld();
-        uint32_t pp[16], ds[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = ch * 32 + 2 * i + u;
-            float pr = ex2(fmaf(__uint_as_float(sr[2 * i + u]), c, -lse2[col]));
-            pr = (col < lo) ? 0.f : pr;
-            pv[u] = pr;
-            dv[u] = pr * (__uint_as_float(dr[2 * i + u]) - dsum[col]);
-          }
-          pp[i] = pack_bf16(pv[0], pv[1]);
-          ds[i] = pack_bf16(dv[0], dv[1]);
-        }
-        tmem_st16(tmem + lane_off + ch * 16, pp);
-        tmem_st16(tmem + lane_off + 128 + ch * 16, ds);
-      }
+      const float* lse2 = sVec + st * 2 * QT;
+      const float* dsum = lse2 + QT;
+      const int lo = p.causal ? s - p.q_start - t0 : -1;  // query columns below lo cannot see key s
+      uint32_t sr[64], dr[64];
+      tmem_ld32(tb, *reinterpret_cast<uint32_t(*)[32]>(sr));
+      tmem_ld32(tb + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+      tmem_ld32(tb + 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
+      tmem_ld32(tb + 96, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
+      tmem_wait_ld();
+      uint32_t pp[32], dd[32];
+      p_ds_64(sr, dr, c, [&](int col) { return lse2[col]; }, [&](int col) { return dsum[col]; },
+              [&](int col) { return col >= lo; }, pp, dd);
+      tmem_st32(tb, pp);
+      tmem_st32(tb + 64, dd);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar->p_full);
+      mbar_arrive(&bar->p_full[x]);
     }
     if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
       tc_fence_after();
       const bool store = s < p.S;
-      __nv_bfloat16* dk = static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] +
-                          (int64_t)s * p.s0[2];
-      __nv_bfloat16* dv = static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] +
-                          (int64_t)s * p.s1[2];
-      // with no query tile at all (a key block past every row) dK = dV = 0
-      if (n_items == 0) {
-        if (store) {
-          for (int i = 0; i < D; i += 8) {
-            *reinterpret_cast<uint4*>(dk + i) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4*>(dv + i) = make_uint4(0, 0, 0, 0);
-          }
-        }
+      // warpgroup 0 writes dV, warpgroup 1 writes dK
+      __nv_bfloat16* dst = x == 0
+          ? static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] + (int64_t)s * p.s1[2]
+          : static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] + (int64_t)s * p.s0[2];
+      if (n_items == 0) {  // a key block past every query row: dK = dV = 0
+        if (store)
+          for (int i = 0; i < D; i += 8) *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
       } else {
-        store_rows_bf16<D>(tmem + lane_off + 256, 1.0f, dv, store);
-        store_rows_bf16<D>(tmem + lane_off + 256 + D, p.scale, dk, store);
+        store_cols_bf16<D>(tmem + lane_off + 256 + x * D, x == 0 ? 1.0f : p.scale, dst, store);
       }
     }
   }
@@ -278,13 +308,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 struct __align__(8) BarsQ {
   uint64_t qo_full;
-  uint64_t kv_full[2], kv_empty[2];
-  uint64_t s_full, p_full, o_full;
+  uint64_t kv_full[kStages], kv_empty[kStages];
+  uint64_t s_full[2], p_full[2];
+  uint64_t o_full;
   uint32_t tmem_base;
   int abort;
 };
 
 // --------------------------------------------------------------------- dQ
+// CTA = 128 query rows of one (batch, head); work items = 64-key tiles.
+// TMEM buffer x: S [128x, 128x+64), dP [128x+64, 128x+128) (dS as bf16 in the
+// first 32 columns of S); dQ [256, 256+D).  Compute warpgroup x handles the
+// key tiles j = x mod 2 (both warpgroups see every query row: lane = row).
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -292,36 +327,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kTile = 128 * D * 2;
+  constexpr int kQ = 128 * D * 2;
+  constexpr int kKV = KT * D * 2;
+  constexpr uint32_t kBoxQ = 128 * 128, kBoxKV = KT * 128;
   uint8_t* sQ = smem;
-  uint8_t* sDO = smem + kTile;
-  uint8_t* sK = smem + 2 * kTile;  // 2 stages
-  uint8_t* sV = smem + 4 * kTile;  // 2 stages
-  BarsQ* bar = reinterpret_cast<BarsQ*>(smem + 6 * kTile);
+  uint8_t* sDO = smem + kQ;
+  uint8_t* sK = smem + 2 * kQ;          // kStages
+  uint8_t* sV = sK + kStages * kKV;     // kStages
+  BarsQ* bar = reinterpret_cast<BarsQ*>(sV + kStages * kKV);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   const int bh = blockIdx.x / p.n_blocks;
   const int mblk = p.n_blocks - 1 - (blockIdx.x % p.n_blocks);  // heaviest first
   const int b = bh / p.H, h = bh % p.H;
   const int hk = h / (p.H / p.HKV);
-  const int t0 = mblk * BT;
-  const int n_kv_all = (p.S + BS - 1) / BS;
-  int n_kv = n_kv_all;
+  const int t0 = mblk * 128;
+  const int n_all = (p.S + KT - 1) / KT;
+  int n_kv = n_all;
   if (p.causal) {
-    int last = t0 + BT - 1;
+    int last = t0 + 127;
     if (last > p.T - 1) last = p.T - 1;
-    const int n = (last + p.q_start) / BS + 1;
-    n_kv = n < n_kv_all ? n : n_kv_all;
+    const int n = (last + p.q_start) / KT + 1;
+    n_kv = n < n_all ? n : n_all;
   }
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->qo_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&bar->kv_full[i], 1);
       mbar_init(&bar->kv_empty[i], 1);
     }
-    mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->p_full, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->s_full[i], 1);
+      mbar_init(&bar->p_full[i], 128);
+    }
     mbar_init(&bar->o_full, 1);
     bar->abort = 0;
     fence_barrier_init();
@@ -336,88 +375,86 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bar->tmem_base;
   volatile int* abort = &bar->abort;
   constexpr int kNB = D / 64;
-  // TMEM: S [0,128) (dS in [0,64)), dP [128,256), dQ [256, 256+D)
+  constexpr uint32_t idS = idesc_bf16(128, KT, 0, 0);  // S, dP: M = 128 rows, N = 64 keys
+  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);   // dQ: N = D, B = K tile MN-major
 
-  if (warp == 0) {
-    if (lane == 0) {
-      mbar_expect_tx(&bar->qo_full, 2 * kTile);
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+    if (warp == 0 && lane == 0) {
+      mbar_expect_tx(&bar->qo_full, 2 * kQ);
       for (int i = 0; i < kNB; ++i) {
-        tma_load_4d(sQ + i * kBox, &tm_q, &bar->qo_full, i * 64, t0, h, b);
-        tma_load_4d(sDO + i * kBox, &tm_do, &bar->qo_full, i * 64, t0, h, b);
+        tma_load_4d(sQ + i * kBoxQ, &tm_q, &bar->qo_full, i * 64, t0, h, b);
+        tma_load_4d(sDO + i * kBoxQ, &tm_do, &bar->qo_full, i * 64, t0, h, b);
       }
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&bar->kv_empty[st], ph ^ 1, abort, p.err)) break;
-        mbar_expect_tx(&bar->kv_full[st], 2 * kTile);
+        const int st = j % kStages;
+        if (!mbar_wait(&bar->kv_empty[st], ((j / kStages) & 1) ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->kv_full[st], 2 * kKV);
         for (int i = 0; i < kNB; ++i) {
-          tma_load_4d(sK + st * kTile + i * kBox, &tm_k, &bar->kv_full[st], i * 64, j * BS, hk, b);
-          tma_load_4d(sV + st * kTile + i * kBox, &tm_v, &bar->kv_full[st], i * 64, j * BS, hk, b);
+          tma_load_4d(sK + st * kKV + i * kBoxKV, &tm_k, &bar->kv_full[st], i * 64, j * KT, hk, b);
+          tma_load_4d(sV + st * kKV + i * kBoxKV, &tm_v, &bar->kv_full[st], i * 64, j * KT, hk, b);
         }
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % kStages, x = j & 1;
+        if (!mbar_wait(&bar->kv_full[st], (j / kStages) & 1, abort, p.err)) return false;
+        tc_fence_after();
+        mma_kmajor<D>(tmem + x * 128, smem_u32(sQ), kBoxQ, smem_u32(sK + st * kKV), kBoxKV, idS);        // S
+        mma_kmajor<D>(tmem + x * 128 + 64, smem_u32(sDO), kBoxQ, smem_u32(sV + st * kKV), kBoxKV, idS);  // dP
+        tc_commit(&bar->s_full[x]);
+        return true;
+      };
       bool ok = mbar_wait(&bar->qo_full, 0, abort, p.err);
+      if (ok && n_kv > 0) ok = issue_s(0);
+      if (ok && n_kv > 1) ok = issue_s(1);
       for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!(ok = mbar_wait(&bar->kv_full[st], ph, abort, p.err))) break;
+        const int st = j % kStages, x = j & 1;
+        if (!(ok = mbar_wait(&bar->p_full[x], (j >> 1) & 1, abort, p.err))) break;
         tc_fence_after();
-        mma_kmajor<D>(tmem + 0, smem_u32(sQ), smem_u32(sK + st * kTile));     // S = Q K^T
-        mma_kmajor<D>(tmem + 128, smem_u32(sDO), smem_u32(sV + st * kTile));  // dP = dO V^T
-        tc_commit(&bar->s_full);
-        if (!(ok = mbar_wait(&bar->p_full, j & 1, abort, p.err))) break;
-        tc_fence_after();
-        mma_tmem_a<D>(tmem + 256, tmem + 0, smem_u32(sK + st * kTile), j > 0);  // dQ += dS K
+        mma_tmem_a<KT>(tmem + 256, tmem + x * 128, smem_u32(sK + st * kKV), kBoxKV, idG, j > 0);  // dQ += dS K
         tc_commit(&bar->kv_empty[st]);
+        if (j + 2 < n_kv) ok = issue_s(j + 2);
       }
       if (ok) tc_commit(&bar->o_full);
     }
-  } else if (warp >= 4) {
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+    const int x = warp >= 8 ? 1 : 0;
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;
     const int t = t0 + row;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tb = tmem + lane_off + x * 128;
     const float c = p.scale_log2;
     const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t;
-    const float neg_l = -p.lse2[vrow];  // +inf on padded rows -> P = 0
+    const float l2 = p.lse2[vrow];  // +inf on padded rows -> P = 0
     const float dsum = p.dsum[vrow];
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!(ok = mbar_wait(&bar->s_full, j & 1, abort, p.err))) break;
+    for (int j = x; j < n_kv; j += 2) {
+      if (!(ok = mbar_wait(&bar->s_full[x], (j >> 1) & 1, abort, p.err))) break;
       tc_fence_after();
-      const int lim = p.causal ? t + p.q_start + 1 - j * BS : 1 << 30;  // keys >= lim masked
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tmem + lane_off + ch * 32, sr);
-        tmem_ld32(tmem + lane_off + 128 + ch * 32, dr);
-        tmem_wait_ld();
-        uint32_t ds[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float dv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = ch * 32 + 2 * i + u;
-            float pr = ex2(fmaf(__uint_as_float(sr[2 * i + u]), c, neg_l));
-            pr = (col < lim) ? pr : 0.f;
-            dv[u] = pr * (__uint_as_float(dr[2 * i + u]) - dsum);
-          }
-          ds[i] = pack_bf16(dv[0], dv[1]);
-        }
-        tmem_st16(tmem + lane_off + ch * 16, ds);
-      }
+      const int lim = p.causal ? t + p.q_start + 1 - j * KT : (1 << 30);  // key columns >= lim masked
+      uint32_t sr[64], dr[64];
+      tmem_ld32(tb, *reinterpret_cast<uint32_t(*)[32]>(sr));
+      tmem_ld32(tb + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+      tmem_ld32(tb + 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
+      tmem_ld32(tb + 96, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
+      tmem_wait_ld();
+      uint32_t pp[32], dd[32];
+      p_ds_64(sr, dr, c, [&](int) { return l2; }, [&](int) { return dsum; }, [&](int col) { return col < lim; }, pp,
+              dd);
+      tmem_st32(tb, dd);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar->p_full);
+      mbar_arrive(&bar->p_full[x]);
     }
     if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
       tc_fence_after();
       __nv_bfloat16* dq = static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)h * p.s0[1] +
                           (int64_t)t * p.s0[2];
-      store_rows_bf16<D>(tmem + lane_off + 256, p.scale, dq, t < p.T);
+      // each warpgroup writes half of the dQ columns
+      store_cols_bf16<D / 2>(tmem + lane_off + 256 + x * (D / 2), p.scale, dq + x * (D / 2), t < p.T);
     }
   }
   tc_fence_before();
@@ -485,10 +522,10 @@ WsLayout ws_layout(const pdb_flash_bwd_desc& d) {
 }
 
 int map_bf16(CUtensorMap* m, const void* base, int D, int64_t rows, int64_t heads, int64_t batch,
-             const int64_t st[3]) {
+             const int64_t st[3], uint32_t box_rows) {
   const uint64_t dims[4] = {(uint64_t)D, (uint64_t)rows, (uint64_t)heads, (uint64_t)batch};
   const uint64_t str[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
-  const uint32_t box[4] = {64, 128, 1, 1};
+  const uint32_t box[4] = {64, box_rows, 1, 1};
   return encode_tma_4d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
@@ -507,11 +544,16 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
         (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (int)d.head_dim_v, rows);
     if (int st = cuda_status(cudaGetLastError(), "bwd prep launch")) return st;
   }
-  CUtensorMap tq, tk, tv, tdo;
-  if (int st = map_bf16(&tq, d.q, D, d.seqlen_q, d.heads_q, d.batch, d.q_stride)) return st;
-  if (int st = map_bf16(&tk, d.k, D, d.seqlen_k, d.heads_kv, d.batch, d.k_stride)) return st;
-  if (int st = map_bf16(&tv, d.v, D, d.seqlen_k, d.heads_kv, d.batch, d.v_stride)) return st;
-  if (int st = map_bf16(&tdo, d.dout, D, d.seqlen_q, d.heads_q, d.batch, d.do_stride)) return st;
+  // dK/dV kernel: 64-row query tiles, 128-key blocks; dQ kernel: 128-row query blocks, 64-key tiles
+  CUtensorMap tq64, tdo64, tk128, tv128, tq128, tdo128, tk64, tv64;
+  if (int st = map_bf16(&tq64, d.q, D, d.seqlen_q, d.heads_q, d.batch, d.q_stride, QT)) return st;
+  if (int st = map_bf16(&tdo64, d.dout, D, d.seqlen_q, d.heads_q, d.batch, d.do_stride, QT)) return st;
+  if (int st = map_bf16(&tk128, d.k, D, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, 128)) return st;
+  if (int st = map_bf16(&tv128, d.v, D, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, 128)) return st;
+  if (int st = map_bf16(&tq128, d.q, D, d.seqlen_q, d.heads_q, d.batch, d.q_stride, 128)) return st;
+  if (int st = map_bf16(&tdo128, d.dout, D, d.seqlen_q, d.heads_q, d.batch, d.do_stride, 128)) return st;
+  if (int st = map_bf16(&tk64, d.k, D, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, KT)) return st;
+  if (int st = map_bf16(&tv64, d.v, D, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, KT)) return st;
   BwdParams p{};
   p.lse2 = lse2;
   p.dsum = dsum;
@@ -525,10 +567,11 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
   p.scale = (float)d.scale;
   p.scale_log2 = (float)(d.scale * 1.4426950408889634);
   p.err = device_error_flag();
-  constexpr int kTile = 128 * D * 2;
   // >= 120 KB keeps one CTA per SM, so the 512-column TMEM allocation never waits
-  const int smem_kv = (6 * kTile + 2048 + 1024) > 120 * 1024 ? (6 * kTile + 2048 + 1024) : 120 * 1024;
-  const int smem_q = smem_kv;
+  const int need_kv = 2 * (128 * D * 2) + kStages * 2 * (QT * D * 2) + kStages * 2 * QT * 4 + 256 + 1024;
+  const int need_q = 2 * (128 * D * 2) + kStages * 2 * (KT * D * 2) + 256 + 1024;
+  const int smem_kv = need_kv > 120 * 1024 ? need_kv : 120 * 1024;
+  const int smem_q = need_q > 120 * 1024 ? need_q : 120 * 1024;
   {  // dK, dV
     p.out0 = d.dk;
     p.out1 = d.dv;
@@ -536,22 +579,22 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       p.s0[i] = d.dk_stride[i];
       p.s1[i] = d.dv_stride[i];
     }
-    p.n_blocks = (int)((d.seqlen_k + BS - 1) / BS);
+    p.n_blocks = (int)((d.seqlen_k + 127) / 128);
     const int64_t grid = (int64_t)p.n_blocks * d.heads_kv * d.batch;
     cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
     if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
-    bwd_dkdv_kernel<D><<<(unsigned)grid, kThreads, smem_kv, stream>>>(tq, tk, tv, tdo, p);
+    bwd_dkdv_kernel<D><<<(unsigned)grid, kThreads, smem_kv, stream>>>(tq64, tk128, tv128, tdo64, p);
     if (int st = cuda_status(cudaGetLastError(), "bwd dkdv launch")) return st;
   }
   {  // dQ
     p.out0 = d.dq;
     p.out1 = nullptr;
     for (int i = 0; i < 3; ++i) p.s0[i] = d.dq_stride[i];
-    p.n_blocks = (int)(tpad / BT);
+    p.n_blocks = (int)(tpad / 128);
     const int64_t grid = (int64_t)p.n_blocks * d.heads_q * d.batch;
     cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
     if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
-    bwd_dq_kernel<D><<<(unsigned)grid, kThreads, smem_q, stream>>>(tq, tk, tv, tdo, p);
+    bwd_dq_kernel<D><<<(unsigned)grid, kThreads, smem_q, stream>>>(tq128, tk64, tv64, tdo128, p);
     if (int st = cuda_status(cudaGetLastError(), "bwd dq launch")) return st;
   }
   return PDB_OK;
