@@ -302,7 +302,7 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def secondary(args, dev, stream, peaks):
+def secondary(args, dev, stream, peaks, parts=("rows", "gqa", "bwd")):
     """Config 2 (row reductions), 4 (GQA) and 5 (backward) at N=1."""
     import torch
 
@@ -310,6 +310,18 @@ def secondary(args, dev, stream, peaks):
 
     out = {}
     g = torch.Generator(device=dev).manual_seed(7)
+    if "rows" in parts:
+        _rows(out, kernels, dev, stream, peaks, g)
+    if "gqa" in parts:
+        _gqa(out, kernels, dev, stream, g)
+    if "bwd" in parts:
+        _bwd(out, kernels, dev, stream, g)
+    return out
+
+
+def _rows(out, kernels, dev, stream, peaks, g):
+    import torch
+
     x = torch.randn(8192, 4096, device=dev, generator=g)
     y = torch.empty_like(x)
     gam = 1 + 0.1 * torch.randn(4096, device=dev, generator=g)
@@ -321,7 +333,11 @@ def secondary(args, dev, stream, peaks):
         gbs = nbytes / (sum(per) / len(per) * 1e-3) / 1e9
         out[name] = {"GB/s": gbs, "frac_hbm": gbs / peaks["hbm_gbs"], "us_per_call": 1e3 * sum(per) / len(per),
                      "bytes_per_call": nbytes, "config": "X 8192x4096 f32 (config 2)"}
-    del x, y
+
+
+def _gqa(out, kernels, dev, stream, g):
+    import torch
+
     # config 4: GQA fwd, B4 Hq64 Hkv8 S8192 D128 causal
     Bq, Hq, Hk, Sq = 4, 64, 8, 8192
     q = torch.randn((Bq, Hq, Sq, D), device=dev, generator=g).to(torch.bfloat16)
@@ -332,7 +348,11 @@ def secondary(args, dev, stream, peaks):
     fl = 4.0 * Bq * Hq * Sq * Sq * D / 2
     out["gqa_fwd"] = {"TFLOP/s": fl / (sum(per) / len(per) * 1e-3) / 1e12, "ms": sum(per) / len(per),
                       "config": "B4 Hq64 Hkv8 S8192 D128 causal (config 4)"}
-    del q, k, v, o
+
+
+def _bwd(out, kernels, dev, stream, g):
+    import torch
+
     # config 5: backward, B4 H16 S2048 D64 causal
     Bb, Hb, Sb, Db = 4, 16, 2048, 64
     q, k, v, do = (torch.randn((Bb, Hb, Sb, Db), device=dev, generator=g).to(torch.bfloat16) for _ in range(4))
@@ -344,7 +364,6 @@ def secondary(args, dev, stream, peaks):
                             "config": "B4 H16 S2048 D64 causal (config 5), 2.5x fwd FLOP convention"}
     except Exception as e:  # the backward is reported, not required, for the headline line
         out["flash_bwd"] = {"error": str(e)[:200]}
-    return out
 
 
 def main():
@@ -358,7 +377,18 @@ def main():
     ap.add_argument("--shape", default=None,
                     help="B,H,S,D override of the flash workload (profiling a smaller case); implies --kernel-only")
     ap.add_argument("--kernel-only", action="store_true", help="time only the flash forward (no e2e/extra/cpu)")
+    ap.add_argument("--only", choices=("rows", "gqa", "bwd"), default=None,
+                    help="run only one secondary workload (config 2, 4 or 5) and print it (profiling)")
     args = ap.parse_args()
+    if args.only:
+        import torch
+
+        from pdum_dsl_b200._lib import load
+
+        load()
+        dev = torch.device("cuda", 0)
+        print(json.dumps(secondary(args, dev, torch.cuda.current_stream(dev), _peaks(), (args.only,))), flush=True)
+        return
     if args.shape:
         global B, H, S, D, FLOP_FULL
         B, H, S, D = (int(x) for x in args.shape.split(","))

@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);   // dV, dK: M = 128 keys, N = D, B MN-major
 
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");
     if (warp == 0 && lane == 0) {
       mbar_expect_tx(&bar->kv_full, 2 * kKV);
       for (int i = 0; i < kNB; ++i) {
@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) tc_commit(&bar->o_full);
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
     const int x = warp >= 8 ? 1 : 0;
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;  // key row within the block (TMEM lane)
@@ -268,17 +268,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* lse2 = sVec + st * 2 * QT;
       const float* dsum = lse2 + QT;
       const int lo = p.causal ? s - p.q_start - t0 : -1;  // query columns below lo cannot see key s
-      uint32_t sr[64], dr[64];
-      tmem_ld32(tb, *reinterpret_cast<uint32_t(*)[32]>(sr));
-      tmem_ld32(tb + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-      tmem_ld32(tb + 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
-      tmem_ld32(tb + 96, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
-      tmem_wait_ld();
-      uint32_t pp[32], dd[32];
-      p_ds_64(sr, dr, c, [&](int col) { return lse2[col]; }, [&](int col) { return dsum[col]; },
-              [&](int col) { return col >= lo; }, pp, dd);
-      tmem_st32(tb, pp);
-      tmem_st32(tb + 64, dd);
+      // two halves of 32 query columns; per-column lse2 / D read as float4 from shared memory
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tb + hf * 32, sr);
+        tmem_ld32(tb + 64 + hf * 32, dr);
+        tmem_wait_ld();
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 l4 = reinterpret_cast<const float4*>(lse2 + hf * 32)[q];
+          const float4 d4 = reinterpret_cast<const float4*>(dsum + hf * 32)[q];
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+          float pv[4], gv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int col = hf * 32 + 4 * q + u;
+            float pr = ex2(fmaf(__uint_as_float(sr[4 * q + u]), c, -lv[u]));
+            pr = col >= lo ? pr : 0.f;
+            pv[u] = pr;
+            gv[u] = pr * (__uint_as_float(dr[4 * q + u]) - dv4[u]);
+          }
+          pp[2 * q] = pack_bf16(pv[0], pv[1]);
+          pp[2 * q + 1] = pack_bf16(pv[2], pv[3]);
+          dd[2 * q] = pack_bf16(gv[0], gv[1]);
+          dd[2 * q + 1] = pack_bf16(gv[2], gv[3]);
+        }
+        tmem_st16(tb + hf * 16, pp);
+        tmem_st16(tb + 64 + hf * 16, dd);
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar->p_full[x]);
@@ -379,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);   // dQ: N = D, B = K tile MN-major
 
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");
     if (warp == 0 && lane == 0) {
       mbar_expect_tx(&bar->qo_full, 2 * kQ);
       for (int i = 0; i < kNB; ++i) {
@@ -419,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) tc_commit(&bar->o_full);
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
     const int x = warp >= 8 ? 1 : 0;
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;
@@ -466,33 +485,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- prologue
-// One warp per (b, h, padded row): D = sum(dO * O), lse2 = lse * log2(e).
+// D = sum(dO * O) and lse2 = lse * log2(e) per (b, h, padded row).  `tpr`
+// threads share a row, each reading 16-byte chunks (8 bf16) of O and dO.
 __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                 const float* __restrict__ lse, float* __restrict__ lse2, float* __restrict__ dsum,
                                 int64_t so0, int64_t so1, int64_t so2, int64_t sd0, int64_t sd1, int64_t sd2, int H,
-                                int T, int Tpad, int DV, int64_t rows) {
-  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+                                int T, int Tpad, int DV, int64_t rows, int tpr, int vec) {
+  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / tpr;
+  const int sub = threadIdx.x % tpr;
   if (r >= rows) return;
   const int t = (int)(r % Tpad);
   const int64_t bh = r / Tpad;
   const int b = (int)(bh / H), h = (int)(bh % H);
-  if (t >= T) {
-    if (lane == 0) {
-      lse2[r] = INFINITY;
-      dsum[r] = 0.f;
-    }
-    return;
-  }
-  const __nv_bfloat16* orow = o + b * so0 + h * so1 + t * so2;
-  const __nv_bfloat16* drow = dout + b * sd0 + h * sd1 + t * sd2;
   float acc = 0.f;
-  for (int i = lane; i < DV; i += 32) acc += __bfloat162float(orow[i]) * __bfloat162float(drow[i]);
+  if (t < T) {
+    const __nv_bfloat16* orow = o + b * so0 + h * so1 + t * so2;
+    const __nv_bfloat16* drow = dout + b * sd0 + h * sd1 + t * sd2;
+    if (vec) {
+      for (int i = sub * 8; i < DV; i += tpr * 8) {
+        const uint4 a = *reinterpret_cast<const uint4*>(orow + i);
+        const uint4 g = *reinterpret_cast<const uint4*>(drow + i);
+        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) {
-    dsum[r] = acc;
-    lse2[r] = lse[bh * T + t] * kLog2e;
+        for (int u = 0; u < 4; ++u) {
+          const float2 fa = __bfloat1622float2(a2[u]), fg = __bfloat1622float2(g2[u]);
+          acc = fmaf(fa.x, fg.x, fmaf(fa.y, fg.y, acc));
+        }
+      }
+    } else {
+      for (int i = sub; i < DV; i += tpr) acc += __bfloat162float(orow[i]) * __bfloat162float(drow[i]);
+    }
+  }
+  for (int off = tpr / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (sub == 0) {
+    dsum[r] = t < T ? acc : 0.f;
+    lse2[r] = t < T ? lse[bh * T + t] * kLog2e : INFINITY;
   }
 }
 
@@ -537,11 +565,19 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
   float* dsum = reinterpret_cast<float*>(ws + w.dsum);
   {
     const int64_t rows = d.batch * d.heads_q * tpad;
-    const int wpb = 8;
-    bwd_prep_kernel<<<(unsigned)((rows + wpb - 1) / wpb), 32 * wpb, 0, stream>>>(
+    const bool vec = (d.head_dim_v % 8 == 0) && ((d.o_stride[0] | d.o_stride[1] | d.o_stride[2]) % 8 == 0) &&
+                     ((d.do_stride[0] | d.do_stride[1] | d.do_stride[2]) % 8 == 0) &&
+                     (reinterpret_cast<uintptr_t>(d.o) & 15) == 0 && (reinterpret_cast<uintptr_t>(d.dout) & 15) == 0;
+    int tpr = 32;  // threads per row: a power of two dividing the warp
+    if (vec) {
+      tpr = 1;
+      while (tpr < 32 && tpr * 8 < d.head_dim_v) tpr *= 2;
+    }
+    const int64_t threads = rows * tpr;
+    bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(d.o), static_cast<const __nv_bfloat16*>(d.dout), lse, lse2, dsum,
         d.o_stride[0], d.o_stride[1], d.o_stride[2], d.do_stride[0], d.do_stride[1], d.do_stride[2],
-        (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (int)d.head_dim_v, rows);
+        (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (int)d.head_dim_v, rows, tpr, vec ? 1 : 0);
     if (int st = cuda_status(cudaGetLastError(), "bwd prep launch")) return st;
   }
   // dK/dV kernel: 64-row query tiles, 128-key blocks; dQ kernel: 128-row query blocks, 64-key tiles
