@@ -34,8 +34,6 @@ int validate_common(int64_t batch, int64_t hq, int64_t hkv, int64_t T, int64_t S
 namespace {
 
 constexpr int BT = 128;  // query rows per tile
-constexpr int BS = 128;  // keys per tile
-constexpr int kBox = 64 * 128 * 2;
 constexpr int kThreads = 384;  // warp0 TMA, warp1 MMA, warp2 TMEM, warps 4..11 two compute warpgroups
 constexpr float kLog2e = 1.4426950408889634f;
 

@@ -7,7 +7,8 @@
 // the causal tile bounds that _prune_flash derives (fusion.py:659-690,
 // hi = 1 + pid for BT = SI): key tiles past the diagonal are never visited.
 //
-// CTA = 256 query rows of one (batch, head), as two 128-row tiles A and B.
+// Work tile = 256 query rows of one (batch, head), as two 128-row tiles A and
+// B; a persistent grid of one CTA per SM walks the tiles.
 //   warp 0        TMA producer (Q once; K/V tiles through 2-stage rings)
 //   warp 1        MMA issuer (one thread): S = Q K^T into TMEM, O += P V
 //                 with P read from TMEM (the "TS" form)
@@ -39,12 +40,13 @@ constexpr int kBoxBytes = 64 * 128 * 2;  // one TMA box: 128 rows x 64 bf16 (128
 constexpr float kRescaleThreshold = 8.0f;
 
 struct __align__(8) Barriers {
-  uint64_t q_full;
+  uint64_t q_full, q_empty;
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2];  // MMA -> softmax (tile A, B)
   uint64_t p_full[2];  // softmax -> MMA
   uint64_t o_full[2];  // last PV done -> epilogue
+  uint64_t o_empty[2];  // epilogue read O -> next tile may accumulate
   uint32_t tmem_base;
   int abort;
 };
@@ -93,6 +95,51 @@ __device__ __forceinline__ void mma_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_
   }
 }
 
+struct TileInfo {
+  int b, h, hk, t0, nA, nB;
+};
+
+// Tile ordinals run head-major (concurrent CTAs share the K/V of a few heads
+// in L2); within a head they alternate heavy and light row blocks (last,
+// first, second-to-last, second, ...).  A CTA takes ordinals in pairs, so each
+// pair costs about the same under the causal mask and the static persistent
+// schedule stays balanced.
+__device__ __forceinline__ int kth_tile(int k) {
+  return (blockIdx.x + (k >> 1) * gridDim.x) * 2 + (k & 1);
+}
+
+__device__ __forceinline__ TileInfo tile_info(int tile, const FwdParams& p) {
+  TileInfo ti;
+  const int bh = tile / p.num_mblocks;
+  const int r = tile % p.num_mblocks;
+  const int mblk = (r & 1) ? (r >> 1) : p.num_mblocks - 1 - (r >> 1);
+  ti.b = bh / p.H;
+  ti.h = bh % p.H;
+  ti.hk = ti.h / (p.H / p.HKV);
+  ti.t0 = mblk * 2 * BM;
+  const int n_kv = (p.S + BN - 1) / BN;
+  int n[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    if (p.causal) {
+      int last_row = ti.t0 + x * BM + BM - 1;
+      if (last_row > p.T - 1) last_row = p.T - 1;
+      const int c = (last_row + p.q_start) / BN + 1;
+      n[x] = c < n_kv ? c : n_kv;
+    } else {
+      n[x] = n_kv;
+    }
+  }
+  ti.nA = n[0];
+  ti.nB = n[1] < n[0] ? n[0] : n[1];
+  return ti;
+}
+
+// Persistent: gridDim.x <= #SMs CTAs walk the tile list (pairs of ordinals with
+// stride gridDim.x pairs).
+// Barrier phases run on counters that continue across tiles, so the loads and
+// score MMAs of tile n+1 overlap the epilogue of tile n; O_x is only
+// overwritten after the epilogue of its previous tile released it (o_empty).
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -102,31 +149,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = Smem<D>;
   Barriers* bar = reinterpret_cast<Barriers*>(smem + L::kBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // ---- tile coordinates: head-major, heaviest (last) row block first ----
-  const int bh = blockIdx.x / p.num_mblocks;
-  const int mblk = p.num_mblocks - 1 - (blockIdx.x % p.num_mblocks);
-  const int b = bh / p.H, h = bh % p.H;
-  const int hk = h / (p.H / p.HKV);
-  const int t0 = mblk * 2 * BM;
-  const int n_kv = (p.S + BN - 1) / BN;
-  int n_tile[2];
-#pragma unroll
-  for (int x = 0; x < 2; ++x) {
-    if (p.causal) {
-      int last_row = t0 + x * BM + BM - 1;
-      if (last_row > p.T - 1) last_row = p.T - 1;
-      int n = (last_row + p.q_start) / BN + 1;
-      n_tile[x] = n < n_kv ? n : n_kv;
-    } else {
-      n_tile[x] = n_kv;
-    }
-  }
-  if (n_tile[1] < n_tile[0]) n_tile[1] = n_tile[0];
-  const int nA = n_tile[0], nB = n_tile[1];
+  const int num_tiles = p.num_mblocks * p.H * p.B;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->q_full, 1);
+    mbar_init(&bar->q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar->k_full[i], 1);
       mbar_init(&bar->k_empty[i], 1);
@@ -135,6 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->s_full[i], 1);
       mbar_init(&bar->p_full[i], BM);
       mbar_init(&bar->o_full[i], 1);
+      mbar_init(&bar->o_empty[i], BM);
     }
     bar->abort = 0;
     fence_barrier_init();
@@ -155,184 +183,197 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Register split (per warpgroup): the control warpgroup hands registers to
   // the two softmax warpgroups.  Launch budget 384 x 168 = 64512
-  // = 128 x 56 + 256 x 224.
+  // = 128 x 88 + 256 x 208.
   if (warp < 4) {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- producer
       prefetch_tensormap(&tm_q);
       prefetch_tensormap(&tm_k);
       prefetch_tensormap(&tm_v);
-      mbar_expect_tx(&bar->q_full, 2 * L::kTileBytes);
-      for (int i = 0; i < kNB; ++i) {
-        tma_load_4d(smem + L::kQ0 + i * kBoxBytes, &tm_q, &bar->q_full, i * 64, t0, h, b);
-        tma_load_4d(smem + L::kQ1 + i * kBoxBytes, &tm_q, &bar->q_full, i * 64, t0 + BM, h, b);
+      uint32_t g = 0, tt = 0;  // K/V tiles loaded, tiles started
+      for (int k = 0, tile = kth_tile(0); tile < num_tiles; tile = kth_tile(++k), ++tt) {
+        const TileInfo ti = tile_info(tile, p);
+        if (!mbar_wait(&bar->q_empty, (tt & 1) ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->q_full, 2 * L::kTileBytes);
+        for (int i = 0; i < kNB; ++i) {
+          tma_load_4d(smem + L::kQ0 + i * kBoxBytes, &tm_q, &bar->q_full, i * 64, ti.t0, ti.h, ti.b);
+          tma_load_4d(smem + L::kQ1 + i * kBoxBytes, &tm_q, &bar->q_full, i * 64, ti.t0 + BM, ti.h, ti.b);
+        }
+        bool ok = true;
+        for (int j = 0; j < ti.nB; ++j, ++g) {
+          const int st = g & 1;
+          const uint32_t ph = (g >> 1) & 1;
+          if (!(ok = mbar_wait(&bar->k_empty[st], ph ^ 1, abort, p.err))) break;
+          mbar_expect_tx(&bar->k_full[st], L::kTileBytes);
+          for (int i = 0; i < kNB; ++i)
+            tma_load_4d(smem + L::kK + st * L::kTileBytes + i * kBoxBytes, &tm_k, &bar->k_full[st], i * 64, j * BN,
+                        ti.hk, ti.b);
+          if (!(ok = mbar_wait(&bar->v_empty[st], ph ^ 1, abort, p.err))) break;
+          mbar_expect_tx(&bar->v_full[st], L::kTileBytes);
+          for (int i = 0; i < kNB; ++i)
+            tma_load_4d(smem + L::kV + st * L::kTileBytes + i * kBoxBytes, &tm_v, &bar->v_full[st], i * 64, j * BN,
+                        ti.hk, ti.b);
+        }
+        if (!ok) break;
       }
-      for (int j = 0; j < nB; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&bar->k_empty[st], ph ^ 1, abort, p.err)) break;
-        mbar_expect_tx(&bar->k_full[st], L::kTileBytes);
-        for (int i = 0; i < kNB; ++i)
-          tma_load_4d(smem + L::kK + st * L::kTileBytes + i * kBoxBytes, &tm_k, &bar->k_full[st], i * 64, j * BN,
-                      hk, b);
-        if (!mbar_wait(&bar->v_empty[st], ph ^ 1, abort, p.err)) break;
-        mbar_expect_tx(&bar->v_full[st], L::kTileBytes);
-        for (int i = 0; i < kNB; ++i)
-          tma_load_4d(smem + L::kV + st * L::kTileBytes + i * kBoxBytes, &tm_v, &bar->v_full[st], i * 64, j * BN,
-                      hk, b);
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
+      // -------------------------------------------------------- MMA issuer
       const uint32_t tS[2] = {tmem + 0, tmem + 128};
       const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
-      bool ok = mbar_wait(&bar->q_full, 0, abort, p.err) && mbar_wait(&bar->k_full[0], 0, abort, p.err);
-      if (ok) {
+      uint32_t g = 0, tt = 0, cs[2] = {0, 0};  // K/V tiles consumed, tiles, P tiles consumed per x
+      bool ok = true;
+      for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+        const TileInfo ti = tile_info(tile, p);
+        if (!(ok = mbar_wait(&bar->q_full, tt & 1, abort, p.err))) break;
+        if (!(ok = mbar_wait(&bar->k_full[g & 1], (g >> 1) & 1, abort, p.err))) break;
         tc_fence_after();
-        mma_qk<D>(tS[0], sQ0, sK);
+        mma_qk<D>(tS[0], sQ0, sK + (g & 1) * L::kTileBytes);
         tc_commit(&bar->s_full[0]);
-        mma_qk<D>(tS[1], sQ1, sK);
+        mma_qk<D>(tS[1], sQ1, sK + (g & 1) * L::kTileBytes);
         tc_commit(&bar->s_full[1]);
-        tc_commit(&bar->k_empty[0]);
-      }
-      for (int j = 0; ok && j < nB; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const int jn = j + 1, stn = jn & 1;
-        const uint32_t phn = (jn >> 1) & 1;
-        if (!(ok = mbar_wait(&bar->v_full[st], ph, abort, p.err))) break;
-        if (j < nA) {
-          if (!(ok = mbar_wait(&bar->p_full[0], j & 1, abort, p.err))) break;
+        tc_commit(&bar->k_empty[g & 1]);
+        for (int j = 0; ok && j < ti.nB; ++j) {
+          const uint32_t gj = g + j, gn = gj + 1;
+          const int st = gj & 1, stn = gn & 1;
+          const uint32_t ph = (gj >> 1) & 1, phn = (gn >> 1) & 1;
+          if (!(ok = mbar_wait(&bar->v_full[st], ph, abort, p.err))) break;
+          if (j < ti.nA) {
+            if (!(ok = mbar_wait(&bar->p_full[0], cs[0] & 1, abort, p.err))) break;
+            ++cs[0];
+            if (j == 0 && !(ok = mbar_wait(&bar->o_empty[0], (tt & 1) ^ 1, abort, p.err))) break;
+            tc_fence_after();
+            mma_pv<D>(tO[0], tS[0], sV + st * L::kTileBytes, j > 0);
+            if (j + 1 < ti.nA) {
+              if (!(ok = mbar_wait(&bar->k_full[stn], phn, abort, p.err))) break;
+              tc_fence_after();
+              mma_qk<D>(tS[0], sQ0, sK + stn * L::kTileBytes);
+              tc_commit(&bar->s_full[0]);
+            } else {
+              tc_commit(&bar->o_full[0]);
+            }
+          }
+          if (!(ok = mbar_wait(&bar->p_full[1], cs[1] & 1, abort, p.err))) break;
+          ++cs[1];
+          if (j == 0 && !(ok = mbar_wait(&bar->o_empty[1], (tt & 1) ^ 1, abort, p.err))) break;
           tc_fence_after();
-          mma_pv<D>(tO[0], tS[0], sV + st * L::kTileBytes, j > 0);
-          if (jn < nA) {
+          mma_pv<D>(tO[1], tS[1], sV + st * L::kTileBytes, j > 0);
+          tc_commit(&bar->v_empty[st]);
+          if (j + 1 < ti.nB) {
             if (!(ok = mbar_wait(&bar->k_full[stn], phn, abort, p.err))) break;
             tc_fence_after();
-            mma_qk<D>(tS[0], sQ0, sK + stn * L::kTileBytes);
-            tc_commit(&bar->s_full[0]);
+            mma_qk<D>(tS[1], sQ1, sK + stn * L::kTileBytes);
+            tc_commit(&bar->s_full[1]);
+            tc_commit(&bar->k_empty[stn]);
           } else {
-            tc_commit(&bar->o_full[0]);
+            tc_commit(&bar->o_full[1]);
+            tc_commit(&bar->q_empty);  // every score MMA of this tile has been issued
           }
         }
-        if (!(ok = mbar_wait(&bar->p_full[1], j & 1, abort, p.err))) break;
-        tc_fence_after();
-        mma_pv<D>(tO[1], tS[1], sV + st * L::kTileBytes, j > 0);
-        tc_commit(&bar->v_empty[st]);
-        if (jn < nB) {
-          if (!(ok = mbar_wait(&bar->k_full[stn], phn, abort, p.err))) break;
-          tc_fence_after();
-          mma_qk<D>(tS[1], sQ1, sK + stn * L::kTileBytes);
-          tc_commit(&bar->s_full[1]);
-          tc_commit(&bar->k_empty[stn]);
-        } else {
-          tc_commit(&bar->o_full[1]);
-        }
+        g += ti.nB;
       }
     }
-  }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
     // ------------------------------------------------------------- softmax
     const int x = (warp >= 8) ? 1 : 0;  // tile A / B
     const int q4 = warp & 3;            // TMEM lane quadrant of this warp
     const int row = q4 * 32 + lane;     // row within the tile (= TMEM lane)
-    const int t = t0 + x * BM + row;    // query row
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const uint32_t tS = tmem + lane_off + x * 128;
     const uint32_t tO = tmem + lane_off + 256 + x * D;
-    const int n = x ? nB : nA;
     const float c = p.scale_log2;
-    float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
+    uint32_t cs = 0, tt = 0;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      if (!(ok = mbar_wait(&bar->s_full[x], j & 1, abort, p.err))) break;
-      tc_fence_after();
-      // keys at or past `lim` (tile-relative) are masked for this row
-      int lim = p.S - j * BN;
-      if (p.causal) {
-        const int lc = t + p.q_start + 1 - j * BN;
-        lim = lc < lim ? lc : lim;
-      }
-      const bool need_mask = __any_sync(0xffffffffu, lim < BN);
-      // all 128 scores of the row in registers: one TMEM round trip
-      uint32_t sr[BN];
-#pragma unroll
-      for (int ch = 0; ch < BN / 32; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
-      tmem_wait_ld();
-      if (need_mask) {
-#pragma unroll
-        for (int i = 0; i < BN; ++i)
-          if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
-      }
-      float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;  // 4 independent chains
-#pragma unroll
-      for (int i = 0; i < BN; i += 8) {
-        mxa = max3(mxa, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
-        mxb = max3(mxb, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
-        mxc = max3(mxc, __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
-        mxd = max3(mxd, __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
-      }
-      const float mt = fmaxf(max3(mxa, mxb, mxc), mxd) * c;
-      m_true = fmaxf(m_true, mt);
-      if (j == 0) {
-        m_used = mt;
-      } else if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
-        const float m_new = fmaxf(m_used, mt);
-        const float alpha = ex2(m_used - m_new);
-        m_used = m_new;
-        l *= alpha;
-        // O is quiescent here: the commit that released S(j) also covers PV(j-1)
-        uint32_t r[32];
-#pragma unroll
-        for (int ch = 0; ch < D / 32; ++ch) {
-          tmem_ld32(tO + ch * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(tO + ch * 32, r);
+    for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+      const TileInfo ti = tile_info(tile, p);
+      const int t = ti.t0 + x * BM + row;  // query row
+      const int n = x ? ti.nB : ti.nA;
+      float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j, ++cs) {
+        if (!(ok = mbar_wait(&bar->s_full[x], cs & 1, abort, p.err))) break;
+        tc_fence_after();
+        // keys at or past `lim` (tile-relative) are masked for this row
+        int lim = p.S - j * BN;
+        if (p.causal) {
+          const int lc = t + p.q_start + 1 - j * BN;
+          lim = lc < lim ? lc : lim;
         }
-      }
-      const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
-      // pass 2: P = exp2(s c - m) as bf16 pairs over the first 64 columns of S
-      // (P chunk ch lands on columns already read: 16 ch < 32 (ch + 1))
-      // P = exp2(s c - m): packed f32x2 FMA for the argument, MUFU ex2 per
-      // element, packed f32x2 adds for the row sum (two independent chains)
-      const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(neg_m, neg_m);
-      uint64_t sum_a = 0, sum_b = 0;
+        const bool need_mask = __any_sync(0xffffffffu, lim < BN);
+        // all 128 scores of the row in registers: one TMEM round trip
+        uint32_t sr[BN];
 #pragma unroll
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t pk[16];
+        for (int ch = 0; ch < BN / 32; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
+        tmem_wait_ld();
+        if (need_mask) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint64_t sv = (uint64_t)sr[ch * 32 + 2 * i] | ((uint64_t)sr[ch * 32 + 2 * i + 1] << 32);
-          float x0, x1;
-          f2_unpack(f2_fma(sv, c2, nm2), x0, x1);
-          const float p0 = ex2(x0), p1 = ex2(x1);
-          const uint64_t pv = f2_pack(p0, p1);
-          if (i & 1) sum_b = f2_add(sum_b, pv); else sum_a = f2_add(sum_a, pv);
-          pk[i] = pack_bf16(p0, p1);
+          for (int i = 0; i < BN; ++i)
+            if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
         }
-        tmem_st16(tS + ch * 16, pk);
+        float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;  // 4 independent chains
+#pragma unroll
+        for (int i = 0; i < BN; i += 8) {
+          mxa = max3(mxa, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+          mxb = max3(mxb, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
+          mxc = max3(mxc, __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
+          mxd = max3(mxd, __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
+        }
+        const float mt = fmaxf(max3(mxa, mxb, mxc), mxd) * c;
+        m_true = fmaxf(m_true, mt);
+        if (j == 0) {
+          m_used = mt;
+        } else if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
+          const float m_new = fmaxf(m_used, mt);
+          const float alpha = ex2(m_used - m_new);
+          m_used = m_new;
+          l *= alpha;
+          // O is quiescent here: the commit that released S(j) also covers PV(j-1)
+          uint32_t r[32];
+#pragma unroll
+          for (int ch = 0; ch < D / 32; ++ch) {
+            tmem_ld32(tO + ch * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tO + ch * 32, r);
+          }
+        }
+        const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+        // P = exp2(s c - m) as bf16 pairs over the first 64 columns of S (chunk ch
+        // lands on columns already read): packed f32x2 FMA for the argument, MUFU
+        // ex2 per element, packed f32x2 adds for the row sum (two chains)
+        const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(neg_m, neg_m);
+        uint64_t sum_a = 0, sum_b = 0;
+#pragma unroll
+        for (int ch = 0; ch < BN / 32; ++ch) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint64_t sv = (uint64_t)sr[ch * 32 + 2 * i] | ((uint64_t)sr[ch * 32 + 2 * i + 1] << 32);
+            float x0, x1;
+            f2_unpack(f2_fma(sv, c2, nm2), x0, x1);
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            const uint64_t pv = f2_pack(p0, p1);
+            if (i & 1) sum_b = f2_add(sum_b, pv); else sum_a = f2_add(sum_a, pv);
+            pk[i] = pack_bf16(p0, p1);
+          }
+          tmem_st16(tS + ch * 16, pk);
+        }
+        float sa0, sa1, sb0, sb1;
+        f2_unpack(sum_a, sa0, sa1);
+        f2_unpack(sum_b, sb0, sb1);
+        l += (sa0 + sa1) + (sb0 + sb1);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bar->p_full[x]);
       }
-      float sa0, sa1, sb0, sb1;
-      f2_unpack(sum_a, sa0, sa1);
-      f2_unpack(sum_b, sb0, sb1);
-      const float rsa = sa0 + sa1, rsb = sb0 + sb1;
-      l += rsa + rsb;
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bar->p_full[x]);
-    }
-    if (ok && mbar_wait(&bar->o_full[x], 0, abort, p.err)) {
+      if (!ok || !(ok = mbar_wait(&bar->o_full[x], tt & 1, abort, p.err))) break;
       tc_fence_after();
       const float inv_l = 1.0f / l;
       const bool store = t < p.T;
-      const int64_t bhq = (int64_t)b * p.H + h;
-      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.o) + (int64_t)b * p.o_stride[0] +
-                            (int64_t)h * p.o_stride[1] + (int64_t)t * p.o_stride[2];
+      const int64_t bhq = (int64_t)ti.b * p.H + ti.h;
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.o) + (int64_t)ti.b * p.o_stride[0] +
+                            (int64_t)ti.h * p.o_stride[1] + (int64_t)t * p.o_stride[2];
 #pragma unroll
       for (int ch = 0; ch < D / 32; ++ch) {
         uint32_t r[32];
@@ -348,6 +389,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
       }
+      tc_fence_before();
+      mbar_arrive(&bar->o_empty[x]);  // O_x may now be overwritten by the next tile
       if (store) {
         const int64_t idx = bhq * p.T + t;
         constexpr float kLn2 = 0.6931471805599453f;
@@ -402,10 +445,14 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   p.err = device_error_flag();
   const int64_t nblk = (int64_t)p.num_mblocks * d.heads_q * d.batch;
   if (nblk > 0x7fffffffLL) return set_error(PDB_ERR_SHAPE, "bf16 flash: grid too large");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t units = (nblk + 1) / 2;  // tile pairs
+  const int64_t grid = units < sm_count(dev) ? units : sm_count(dev);  // persistent: one CTA per SM
   const int smem = Smem<D>::kTotal;
   cudaError_t e = cudaFuncSetAttribute(flash_fwd_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_status(e, "bf16 flash: set smem attribute");
-  flash_fwd_sm100_kernel<D><<<(unsigned)nblk, kThreads, smem, stream>>>(tq, tk, tv, p);
+  flash_fwd_sm100_kernel<D><<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, p);
   return cuda_status(cudaGetLastError(), "bf16 flash launch");
 }
 
