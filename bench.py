@@ -5,10 +5,13 @@
 Workload: causal bf16 flash-attention forward,
 B=8 H=32 S=4096 D=128, scale 1/sqrt(128), fp32 accumulate, synthetic N(0,1)
 inputs.  A step is one forward over the whole batch.  With N GPUs (torchrun,
-one process per GPU, NCCL) the 256 (batch, head) units are split into N
-contiguous shards, one per rank (strong scaling: total work fixed); each rank
-keeps its output shard in its own HBM -- there is no exchange step inside the
-forward, so no collective runs in the timed region.
+one process per GPU, NCCL) the job is partitioned by (batch, head) units with
+no exchange step inside the forward, so no collective runs in the timed
+region.  Default `--scaling weak`: the global batch is 8*N and every rank owns
+a config-3-sized block of 256 units (per-GPU work fixed); `--scaling strong`
+splits the fixed config-3 job's 256 units into N contiguous shards.  Each rank
+keeps its output shard in its own HBM; the optional final NCCL all-gather of
+the shards is timed separately (`gather`).
 Inputs (805 MB of q/k/v) exceed the 126 MB L2, so no L2 flush is needed.
 
 `value` = algorithmic TFLOP/s of the whole job (causal counted as half of
@@ -109,11 +112,13 @@ def _dist():
     return world, rank, local
 
 
-def _shard(world, rank):
+def _shard(world, rank, scaling):
+    """(lo, hi) units of this rank and the global unit count."""
     from pdum_dsl_b200.partition import shard_units
 
-    sh = shard_units(B * H, world, rank)
-    return sh.lo, sh.hi
+    total = B * H * (world if scaling == "weak" else 1)
+    sh = shard_units(total, world, rank)
+    return sh.lo, sh.hi, total
 
 
 def _timed(fn, steps, warmup, stream, world):
@@ -191,7 +196,7 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": "fused-attn TFLOP/s (causal flash fwd, config 3)", "value": v,
         "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps_ref, "warmup": args.warmup_ref,
-        "ms_per_step": 1e3 * t_all / max(1, args.steps_ref), "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": 1e3 * t_all / max(1, args.steps_ref), "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "f64", "data": "synthetic N(0,1), seeded",
         "config": {"workload": "flash-attention forward, causal, B=8 H=32 S=4096 D=128 (config 3)",
                    "sample": desc},
@@ -213,8 +218,9 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
-    lo, hi = _shard(world, rank)
+    lo, hi, total_units = _shard(world, rank, args.scaling)
     units = hi - lo
+    flop_job = FLOP_FULL * total_units / (B * H)  # the whole job over all ranks
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     # this rank's (batch, head) units as one (1, units, S, D) job
     q, k, v = (torch.randn((1, units, S, D), device=dev, generator=g, dtype=torch.float32).to(torch.bfloat16)
@@ -226,7 +232,7 @@ def run_ours(args):
         total_ms, per = _timed(step, args.steps, args.warmup, stream, world)
     kernels.check_device_errors()
     flop_rank = FLOP_FULL * units / (B * H)
-    value = FLOP_FULL * args.steps / (total_ms * 1e-3) / 1e12
+    value = flop_job * args.steps / (total_ms * 1e-3) / 1e12
     peaks = _peaks()
     launch_ms = sum(per) / len(per)
     achieved = flop_rank / (launch_ms * 1e-3) / 1e12
@@ -259,7 +265,7 @@ def run_ours(args):
 
     e2e_steps = max(1, min(args.steps, 10))
     e2e_ms, _ = _timed(e2e_step, e2e_steps, 1, stream, world)
-    e2e_val = FLOP_FULL * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    e2e_val = flop_job * e2e_steps / (e2e_ms * 1e-3) / 1e12
     h2d = 3 * q.numel() * q.element_size() * world
     d2h = o.numel() * o.element_size() * world
 
@@ -277,17 +283,21 @@ def run_ours(args):
         line = {
             "metric": "fused-attn TFLOP/s (causal flash fwd, config 3)", "value": value, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic N(0,1) (torch.randn, seeded), bf16",
             "config": {"workload": "flash-attention forward, causal, B=8 H=32 S=4096 D=128, scale 1/sqrt(128) "
-                                   "(config 3)", "global_batch": B, "heads": H, "seq_len": S, "head_dim": D,
-                       "parallelism": f"batch x head shards over {world} GPU(s)",
+                                   "(config 3)", "global_batch": B * total_units // (B * H), "heads": H, "seq_len": S, "head_dim": D,
+                       "parallelism": f"batch x head shards over {world} GPU(s), {args.scaling} scaling",
                        "l2": "inputs 805 MB > 126 MB L2 (no flush)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": achieved / peaks["bf16_tflops"], "peak_source": peaks["source"] + " (burst)",
                          "frac_sustained": achieved / peaks["bf16_tflops_sustained"]
                          if peaks.get("bf16_tflops_sustained") else None,
-                         "traffic": None, "kernel": "flash_fwd_sm100_kernel<128>",
+                         # ncu dram read+write of one launch at B=2 (profiles/flash_fwd_sm100_config3.md),
+                         # scaled by the 4x units of a config-3 launch; algorithmic bytes are 1073.7 MB
+                         "traffic": 4 * (202.08e6 + 43.79e6) * units / (B * H) if (B, H, S, D) == (8, 32, 4096, 128)
+                         else None, "traffic_unit": "bytes per launch",
+                         "kernel": "flash_fwd_sm100_kernel<128>",
                          "launch_ms": launch_ms},
             "clocks": sampler.summary(),
             "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -372,6 +382,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--scaling", choices=("weak", "strong"), default="weak")
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--shape", default=None,

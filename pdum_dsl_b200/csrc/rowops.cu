@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kThreads) layernorm_vec_kernel(const float* __
     }
   }
   const float var = block_reduce(q, red, SumOp{}, 0.f) / (float)cols;
-  const float sd = sqrtf(var + eps);
+  const float inv = 1.0f / sqrtf(var + eps);
   const float4* g4 = reinterpret_cast<const float4*>(g);
   const float4* b4 = reinterpret_cast<const float4*>(b);
 #pragma unroll
@@ -127,8 +127,8 @@ __global__ void __launch_bounds__(kThreads) layernorm_vec_kernel(const float* __
     if (c < n4) {
       float4 gg = g ? __ldg(g4 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
       float4 bb = b ? __ldg(b4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 o = make_float4(v[i].x / sd * gg.x + bb.x, v[i].y / sd * gg.y + bb.y, v[i].z / sd * gg.z + bb.z,
-                             v[i].w / sd * gg.w + bb.w);
+      float4 o = make_float4(v[i].x * inv * gg.x + bb.x, v[i].y * inv * gg.y + bb.y, v[i].z * inv * gg.z + bb.z,
+                             v[i].w * inv * gg.w + bb.w);
       __stcs(yr + c, o);
     }
   }
