@@ -482,6 +482,352 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// D = 64 backward with 128-wide score tiles and overlapped accumulation.
+// With D = 64 the score MMAs (N = 128) are full-width; the accumulations
+// (dV, dK, dQ: N = 64) are not, so the schedule overlaps them with the
+// next item's score math: P / dS of item i are copied to a TMEM staging area,
+// which frees the S / dP columns for item i+1's score MMAs; those are issued
+// before the accumulations of item i, and the compute warpgroups work on item
+// i+1 while the tensor core accumulates item i.
+struct __align__(8) Bars64 {
+  uint64_t fixed_full;                 // K/V (dK/dV kernel) or Q/dO (dQ kernel)
+  uint64_t op_full[kStages], op_empty[kStages];  // streamed operand ring
+  uint64_t s_full, p_full, stage_free, o_full;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// dK/dV, D = 64.  CTA = 128 keys; items = (query head, 128-row query tile).
+// TMEM: S^T [0,128)  dP^T [128,256)  staging P^T [256,320) dS^T [320,384)
+//       dV [384,448)  dK [448,512).  Compute warpgroup w owns query columns
+// [64w, 64w+64) of each item.
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dkdv64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                      const BwdParams p) {
+  constexpr int D = 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kT = 128 * D * 2;  // any 128-row tile (16 KB)
+  constexpr uint32_t kBox = 128 * 128;
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + kT;
+  uint8_t* sQ = smem + 2 * kT;         // kStages
+  uint8_t* sDO = sQ + kStages * kT;    // kStages
+  float* sVec = reinterpret_cast<float*>(sDO + kStages * kT);  // kStages x (lse2[128], dsum[128])
+  Bars64* bar = reinterpret_cast<Bars64*>(reinterpret_cast<uint8_t*>(sVec) + kStages * 2 * 128 * 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int bhk = blockIdx.x / p.n_blocks;
+  const int nblk = blockIdx.x % p.n_blocks;
+  const int b = bhk / p.HKV, hk = bhk % p.HKV;
+  const int group = p.H / p.HKV;
+  const int s0 = nblk * 128;
+  const int n_qt = p.Tpad / 128;
+  int qt0 = 0;
+  if (p.causal) {
+    const int first = s0 - p.q_start;
+    qt0 = first > 0 ? first / 128 : 0;
+  }
+  const int per_head = n_qt - qt0 > 0 ? n_qt - qt0 : 0;
+  const int n_items = per_head * group;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->fixed_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&bar->op_full[i], 1);
+      mbar_init(&bar->op_empty[i], 1);
+    }
+    mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->p_full, 256);
+    mbar_init(&bar->stage_free, 1);
+    mbar_init(&bar->o_full, 1);
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+  constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
+  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+    if (warp == 0 && lane == 0) {
+      mbar_expect_tx(&bar->fixed_full, 2 * kT);
+      tma_load_4d(sK, &tm_k, &bar->fixed_full, 0, s0, hk, b);
+      tma_load_4d(sV, &tm_v, &bar->fixed_full, 0, s0, hk, b);
+      for (int it = 0; it < n_items; ++it) {
+        const int st = it % kStages;
+        const int h = hk * group + it / per_head;
+        const int t0 = (qt0 + it % per_head) * 128;
+        if (!mbar_wait(&bar->op_empty[st], ((it / kStages) & 1) ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->op_full[st], 2 * kT + 2 * 128 * 4);
+        tma_load_4d(sQ + st * kT, &tm_q, &bar->op_full[st], 0, t0, h, b);
+        tma_load_4d(sDO + st * kT, &tm_do, &bar->op_full[st], 0, t0, h, b);
+        const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
+        bulk_load(sVec + st * 256, p.lse2 + vrow, 512, &bar->op_full[st]);
+        bulk_load(sVec + st * 256 + 128, p.dsum + vrow, 512, &bar->op_full[st]);
+      }
+    } else if (warp == 1 && lane == 0) {
+      bool ok = mbar_wait(&bar->fixed_full, 0, abort, p.err);
+      auto issue_s = [&](int it) -> bool {
+        const int st = it % kStages;
+        if (!mbar_wait(&bar->op_full[st], (it / kStages) & 1, abort, p.err)) return false;
+        tc_fence_after();
+        mma_kmajor<D>(tmem + 0, smem_u32(sK), kBox, smem_u32(sQ + st * kT), kBox, idS);     // S^T = K Q^T
+        mma_kmajor<D>(tmem + 128, smem_u32(sV), kBox, smem_u32(sDO + st * kT), kBox, idS);  // dP^T = V dO^T
+        tc_commit(&bar->s_full);
+        return true;
+      };
+      if (ok && n_items > 0) ok = issue_s(0);
+      for (int it = 0; ok && it < n_items; ++it) {
+        const int st = it % kStages;
+        if (!(ok = mbar_wait(&bar->p_full, it & 1, abort, p.err))) break;
+        tc_fence_after();
+        if (it + 1 < n_items && !(ok = issue_s(it + 1))) break;  // next scores first: the compute overlaps below
+        mma_tmem_a<128>(tmem + 384, tmem + 256, smem_u32(sDO + st * kT), kBox, idG, it > 0);  // dV += P^T dO
+        mma_tmem_a<128>(tmem + 448, tmem + 320, smem_u32(sQ + st * kT), kBox, idG, it > 0);   // dK += dS^T Q
+        tc_commit(&bar->op_empty[st]);
+        tc_commit(&bar->stage_free);
+      }
+      if (ok) tc_commit(&bar->o_full);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
+    const int w = warp >= 8 ? 1 : 0;  // query-column half
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int s = s0 + row;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tl = tmem + lane_off;
+    const float c = p.scale_log2;
+    bool ok = true;
+    for (int it = 0; it < n_items; ++it) {
+      const int st = it % kStages;
+      const int t0 = (qt0 + it % per_head) * 128;
+      if (!(ok = mbar_wait(&bar->op_full[st], (it / kStages) & 1, abort, p.err))) break;
+      if (!(ok = mbar_wait(&bar->s_full, it & 1, abort, p.err))) break;
+      tc_fence_after();
+      const float* lse2 = sVec + st * 256 + w * 64;
+      const float* dsum = sVec + st * 256 + 128 + w * 64;
+      const int lo = p.causal ? s - p.q_start - t0 - w * 64 : -(1 << 30);  // columns below lo are masked
+      uint32_t sr[64], dr[64];
+      tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(sr));
+      tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+      tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
+      tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
+      tmem_wait_ld();
+      uint32_t pp[32], dd[32];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const float4 l4 = reinterpret_cast<const float4*>(lse2)[q];
+        const float4 d4 = reinterpret_cast<const float4*>(dsum)[q];
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+        float pv[4], gv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int col = 4 * q + u;
+          float pr = ex2(fmaf(__uint_as_float(sr[col]), c, -lv[u]));
+          pr = col >= lo ? pr : 0.f;
+          pv[u] = pr;
+          gv[u] = pr * (__uint_as_float(dr[col]) - dv4[u]);
+        }
+        pp[2 * q] = pack_bf16(pv[0], pv[1]);
+        pp[2 * q + 1] = pack_bf16(pv[2], pv[3]);
+        dd[2 * q] = pack_bf16(gv[0], gv[1]);
+        dd[2 * q + 1] = pack_bf16(gv[2], gv[3]);
+      }
+      // S^T / dP^T fully read: the staging area must be free of item it-1's accumulations
+      if (it > 0 && !(ok = mbar_wait(&bar->stage_free, (it - 1) & 1, abort, p.err))) break;
+      tc_fence_after();
+      tmem_st32(tl + 256 + w * 32, pp);
+      tmem_st32(tl + 320 + w * 32, dd);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->p_full);
+    }
+    if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
+      tc_fence_after();
+      const bool store = s < p.S;
+      __nv_bfloat16* dst = w == 0
+          ? static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] + (int64_t)s * p.s1[2]
+          : static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] + (int64_t)s * p.s0[2];
+      if (n_items == 0) {
+        if (store)
+          for (int i = 0; i < D; i += 8) *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
+      } else {
+        store_cols_bf16<D>(tl + 384 + w * 64, w == 0 ? 1.0f : p.scale, dst, store);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dQ, D = 64.  CTA = 128 query rows; items = 128-key tiles.
+// TMEM: S [0,128)  dP [128,256)  staging dS [256,320)  dQ [320,384).
+// Compute warpgroup w owns key columns [64w, 64w+64).
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dq64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                    const BwdParams p) {
+  constexpr int D = 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kT = 128 * D * 2;
+  constexpr uint32_t kBox = 128 * 128;
+  uint8_t* sQ = smem;
+  uint8_t* sDO = smem + kT;
+  uint8_t* sK = smem + 2 * kT;        // kStages
+  uint8_t* sV = sK + kStages * kT;    // kStages
+  Bars64* bar = reinterpret_cast<Bars64*>(sV + kStages * kT);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int bh = blockIdx.x / p.n_blocks;
+  const int mblk = p.n_blocks - 1 - (blockIdx.x % p.n_blocks);
+  const int b = bh / p.H, h = bh % p.H;
+  const int hk = h / (p.H / p.HKV);
+  const int t0 = mblk * 128;
+  const int n_all = (p.S + 127) / 128;
+  int n_kv = n_all;
+  if (p.causal) {
+    int last = t0 + 127;
+    if (last > p.T - 1) last = p.T - 1;
+    const int n = (last + p.q_start) / 128 + 1;
+    n_kv = n < n_all ? n : n_all;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->fixed_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&bar->op_full[i], 1);
+      mbar_init(&bar->op_empty[i], 1);
+    }
+    mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->p_full, 256);
+    mbar_init(&bar->stage_free, 1);
+    mbar_init(&bar->o_full, 1);
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+  constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
+  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+    if (warp == 0 && lane == 0) {
+      mbar_expect_tx(&bar->fixed_full, 2 * kT);
+      tma_load_4d(sQ, &tm_q, &bar->fixed_full, 0, t0, h, b);
+      tma_load_4d(sDO, &tm_do, &bar->fixed_full, 0, t0, h, b);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % kStages;
+        if (!mbar_wait(&bar->op_empty[st], ((j / kStages) & 1) ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->op_full[st], 2 * kT);
+        tma_load_4d(sK + st * kT, &tm_k, &bar->op_full[st], 0, j * 128, hk, b);
+        tma_load_4d(sV + st * kT, &tm_v, &bar->op_full[st], 0, j * 128, hk, b);
+      }
+    } else if (warp == 1 && lane == 0) {
+      bool ok = mbar_wait(&bar->fixed_full, 0, abort, p.err);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % kStages;
+        if (!mbar_wait(&bar->op_full[st], (j / kStages) & 1, abort, p.err)) return false;
+        tc_fence_after();
+        mma_kmajor<D>(tmem + 0, smem_u32(sQ), kBox, smem_u32(sK + st * kT), kBox, idS);     // S = Q K^T
+        mma_kmajor<D>(tmem + 128, smem_u32(sDO), kBox, smem_u32(sV + st * kT), kBox, idS);  // dP = dO V^T
+        tc_commit(&bar->s_full);
+        return true;
+      };
+      if (ok && n_kv > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % kStages;
+        if (!(ok = mbar_wait(&bar->p_full, j & 1, abort, p.err))) break;
+        tc_fence_after();
+        if (j + 1 < n_kv && !(ok = issue_s(j + 1))) break;
+        mma_tmem_a<128>(tmem + 320, tmem + 256, smem_u32(sK + st * kT), kBox, idG, j > 0);  // dQ += dS K
+        tc_commit(&bar->op_empty[st]);
+        tc_commit(&bar->stage_free);
+      }
+      if (ok) tc_commit(&bar->o_full);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
+    const int w = warp >= 8 ? 1 : 0;
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int t = t0 + row;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tl = tmem + lane_off;
+    const float c = p.scale_log2;
+    const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t;
+    const float l2 = p.lse2[vrow];  // +inf on padded rows -> P = 0
+    const float dsum = p.dsum[vrow];
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!(ok = mbar_wait(&bar->s_full, j & 1, abort, p.err))) break;
+      tc_fence_after();
+      const int lim = p.causal ? t + p.q_start + 1 - j * 128 - w * 64 : (1 << 30);  // key columns >= lim masked
+      uint32_t sr[64], dr[64];
+      tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(sr));
+      tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+      tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
+      tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
+      tmem_wait_ld();
+      uint32_t dd[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float gv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int col = 2 * i + u;
+          float pr = ex2(fmaf(__uint_as_float(sr[col]), c, -l2));
+          pr = col < lim ? pr : 0.f;
+          gv[u] = pr * (__uint_as_float(dr[col]) - dsum);
+        }
+        dd[i] = pack_bf16(gv[0], gv[1]);
+      }
+      if (j > 0 && !(ok = mbar_wait(&bar->stage_free, (j - 1) & 1, abort, p.err))) break;
+      tc_fence_after();
+      tmem_st32(tl + 256 + w * 32, dd);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar->p_full);
+    }
+    if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
+      tc_fence_after();
+      __nv_bfloat16* dq = static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)h * p.s0[1] +
+                          (int64_t)t * p.s0[2];
+      store_cols_bf16<32>(tl + 320 + w * 32, p.scale, dq + w * 32, t < p.T);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ---------------------------------------------------------------- prologue
 // D = sum(dO * O) and lse2 = lse * log2(e) per (b, h, padded row).  `tpr`
 // threads share a row, each reading 16-byte chunks (8 bf16) of O and dO.
@@ -615,9 +961,16 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     }
     p.n_blocks = (int)((d.seqlen_k + 127) / 128);
     const int64_t grid = (int64_t)p.n_blocks * d.heads_kv * d.batch;
-    cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
-    if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
-    bwd_dkdv_kernel<D><<<(unsigned)grid, kThreads, smem_kv, stream>>>(tq64, tk128, tv128, tdo64, p);
+    if (D == 64) {
+      const int smem = 2 * 16384 + kStages * 2 * 16384 + kStages * 1024 + 256 + 1024;
+      cudaError_t e = cudaFuncSetAttribute(bwd_dkdv64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return cuda_status(e, "bwd dkdv64 smem attribute");
+      bwd_dkdv64_kernel<<<(unsigned)grid, kThreads, smem, stream>>>(tq128, tk128, tv128, tdo128, p);
+    } else {
+      cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
+      if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
+      bwd_dkdv_kernel<D><<<(unsigned)grid, kThreads, smem_kv, stream>>>(tq64, tk128, tv128, tdo64, p);
+    }
     if (int st = cuda_status(cudaGetLastError(), "bwd dkdv launch")) return st;
   }
   {  // dQ
@@ -626,9 +979,16 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     for (int i = 0; i < 3; ++i) p.s0[i] = d.dq_stride[i];
     p.n_blocks = (int)(tpad / 128);
     const int64_t grid = (int64_t)p.n_blocks * d.heads_q * d.batch;
-    cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
-    if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
-    bwd_dq_kernel<D><<<(unsigned)grid, kThreads, smem_q, stream>>>(tq128, tk64, tv64, tdo128, p);
+    if (D == 64) {
+      const int smem = 2 * 16384 + kStages * 2 * 16384 + 256 + 1024;
+      cudaError_t e = cudaFuncSetAttribute(bwd_dq64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return cuda_status(e, "bwd dq64 smem attribute");
+      bwd_dq64_kernel<<<(unsigned)grid, kThreads, smem, stream>>>(tq128, tk128, tv128, tdo128, p);
+    } else {
+      cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
+      if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
+      bwd_dq_kernel<D><<<(unsigned)grid, kThreads, smem_q, stream>>>(tq128, tk64, tv64, tdo128, p);
+    }
     if (int st = cuda_status(cudaGetLastError(), "bwd dq launch")) return st;
   }
   return PDB_OK;
