@@ -276,8 +276,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pp[16], dd[16];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const float4 l4 = reinterpret_cast<const float4*>(lse2 + hf * 32)[q];
-          const float4 d4 = reinterpret_cast<const float4*>(dsum + hf * 32)[q];
+          const float4 l4 = lds128(smem_u32(lse2 + hf * 32) + 16 * q);
+          const float4 d4 = lds128(smem_u32(dsum + hf * 32) + 16 * q);
           const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
           float pv[4], gv[4];
 #pragma unroll
@@ -628,8 +628,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t pp[32], dd[32];
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
-        const float4 l4 = reinterpret_cast<const float4*>(lse2)[q];
-        const float4 d4 = reinterpret_cast<const float4*>(dsum)[q];
+        const float4 l4 = lds128(smem_u32(lse2) + 16 * q);
+        const float4 d4 = lds128(smem_u32(dsum) + 16 * q);
         const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
         float pv[4], gv[4];
 #pragma unroll
