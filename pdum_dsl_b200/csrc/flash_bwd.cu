@@ -626,24 +626,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
       tmem_wait_ld();
       uint32_t pp[32], dd[32];
+      // packed f32x2 math; the causal select only on items that cross the diagonal
+      const bool need_mask = __any_sync(0xffffffffu, lo > 0);
+      const uint64_t c2 = f2_pack(c, c);
+      const uint32_t sl = smem_u32(lse2), sd = smem_u32(dsum);
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
-        const float4 l4 = lds128(smem_u32(lse2) + 16 * q);
-        const float4 d4 = lds128(smem_u32(dsum) + 16 * q);
-        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-        float pv[4], gv[4];
+        const float4 l4 = lds128(sl + 16 * q);
+        const float4 d4 = lds128(sd + 16 * q);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int col = 4 * q + u;
-          float pr = ex2(fmaf(__uint_as_float(sr[col]), c, -lv[u]));
-          pr = col >= lo ? pr : 0.f;
-          pv[u] = pr;
-          gv[u] = pr * (__uint_as_float(dr[col]) - dv4[u]);
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int col = 4 * q + 2 * h2;
+          const uint64_t s2 = (uint64_t)sr[col] | ((uint64_t)sr[col + 1] << 32);
+          const uint64_t g2 = (uint64_t)dr[col] | ((uint64_t)dr[col + 1] << 32);
+          const uint64_t l2 = h2 ? f2_pack(l4.z, l4.w) : f2_pack(l4.x, l4.y);
+          const uint64_t dd2 = h2 ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y);
+          float x0, x1;
+          f2_unpack(f2_sub(f2_mul(s2, c2), l2), x0, x1);
+          float p0 = ex2(x0), p1 = ex2(x1);
+          if (need_mask) {
+            p0 = col >= lo ? p0 : 0.f;
+            p1 = col + 1 >= lo ? p1 : 0.f;
+          }
+          const uint64_t pv = f2_pack(p0, p1);
+          float g0, g1;
+          f2_unpack(f2_mul(pv, f2_sub(g2, dd2)), g0, g1);
+          pp[2 * q + h2] = pack_bf16(p0, p1);
+          dd[2 * q + h2] = pack_bf16(g0, g1);
         }
-        pp[2 * q] = pack_bf16(pv[0], pv[1]);
-        pp[2 * q + 1] = pack_bf16(pv[2], pv[3]);
-        dd[2 * q] = pack_bf16(gv[0], gv[1]);
-        dd[2 * q + 1] = pack_bf16(gv[2], gv[3]);
       }
       // S^T / dP^T fully read: the staging area must be free of item it-1's accumulations
       if (it > 0 && !(ok = mbar_wait(&bar->stage_free, (it - 1) & 1, abort, p.err))) break;
@@ -794,17 +804,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
       tmem_wait_ld();
       uint32_t dd[32];
+      const bool need_mask = __any_sync(0xffffffffu, lim < 64);
+      const uint64_t c2 = f2_pack(c, c), nl2 = f2_pack(-l2, -l2), ds2 = f2_pack(dsum, dsum);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        float gv[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int col = 2 * i + u;
-          float pr = ex2(fmaf(__uint_as_float(sr[col]), c, -l2));
-          pr = col < lim ? pr : 0.f;
-          gv[u] = pr * (__uint_as_float(dr[col]) - dsum);
+        const int col = 2 * i;
+        const uint64_t s2 = (uint64_t)sr[col] | ((uint64_t)sr[col + 1] << 32);
+        const uint64_t g2 = (uint64_t)dr[col] | ((uint64_t)dr[col + 1] << 32);
+        float x0, x1;
+        f2_unpack(f2_fma(s2, c2, nl2), x0, x1);
+        float p0 = ex2(x0), p1 = ex2(x1);
+        if (need_mask) {
+          p0 = col < lim ? p0 : 0.f;
+          p1 = col + 1 < lim ? p1 : 0.f;
         }
-        dd[i] = pack_bf16(gv[0], gv[1]);
+        float g0, g1;
+        f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(g2, ds2)), g0, g1);
+        dd[i] = pack_bf16(g0, g1);
       }
       if (j > 0 && !(ok = mbar_wait(&bar->stage_free, (j - 1) & 1, abort, p.err))) break;
       tc_fence_after();
