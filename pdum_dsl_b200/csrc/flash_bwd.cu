@@ -619,40 +619,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* lse2 = sVec + st * 256 + w * 64;
       const float* dsum = sVec + st * 256 + 128 + w * 64;
       const int lo = p.causal ? s - p.q_start - t0 - w * 64 : -(1 << 30);  // columns below lo are masked
-      uint32_t sr[64], dr[64];
-      tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(sr));
-      tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-      tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
-      tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
-      tmem_wait_ld();
       uint32_t pp[32], dd[32];
       // packed f32x2 math; the causal select only on items that cross the diagonal
       const bool need_mask = __any_sync(0xffffffffu, lo > 0);
       const uint64_t c2 = f2_pack(c, c);
       const uint32_t sl = smem_u32(lse2), sd = smem_u32(dsum);
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const float4 l4 = lds128(sl + 16 * q);
-        const float4 d4 = lds128(sd + 16 * q);
+      for (int hf = 0; hf < 2; ++hf) {  // two halves of 32 columns keep the live registers low
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tl + w * 64 + hf * 32, sr);
+        tmem_ld32(tl + 128 + w * 64 + hf * 32, dr);
+        tmem_wait_ld();
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int col = 4 * q + 2 * h2;
-          const uint64_t s2 = (uint64_t)sr[col] | ((uint64_t)sr[col + 1] << 32);
-          const uint64_t g2 = (uint64_t)dr[col] | ((uint64_t)dr[col + 1] << 32);
-          const uint64_t l2 = h2 ? f2_pack(l4.z, l4.w) : f2_pack(l4.x, l4.y);
-          const uint64_t dd2 = h2 ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y);
-          float x0, x1;
-          f2_unpack(f2_sub(f2_mul(s2, c2), l2), x0, x1);
-          float p0 = ex2(x0), p1 = ex2(x1);
-          if (need_mask) {
-            p0 = col >= lo ? p0 : 0.f;
-            p1 = col + 1 >= lo ? p1 : 0.f;
+        for (int q = 0; q < 8; ++q) {
+          const float4 l4 = lds128(sl + 128 * hf + 16 * q);
+          const float4 d4 = lds128(sd + 128 * hf + 16 * q);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int cc = 4 * q + 2 * h2, col = 32 * hf + cc;
+            const uint64_t s2 = (uint64_t)sr[cc] | ((uint64_t)sr[cc + 1] << 32);
+            const uint64_t g2 = (uint64_t)dr[cc] | ((uint64_t)dr[cc + 1] << 32);
+            const uint64_t l2 = h2 ? f2_pack(l4.z, l4.w) : f2_pack(l4.x, l4.y);
+            const uint64_t dd2 = h2 ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y);
+            float x0, x1;
+            f2_unpack(f2_sub(f2_mul(s2, c2), l2), x0, x1);
+            float p0 = ex2(x0), p1 = ex2(x1);
+            if (need_mask) {
+              p0 = col >= lo ? p0 : 0.f;
+              p1 = col + 1 >= lo ? p1 : 0.f;
+            }
+            float g0, g1;
+            f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(g2, dd2)), g0, g1);
+            pp[16 * hf + 2 * q + h2] = pack_bf16(p0, p1);
+            dd[16 * hf + 2 * q + h2] = pack_bf16(g0, g1);
           }
-          const uint64_t pv = f2_pack(p0, p1);
-          float g0, g1;
-          f2_unpack(f2_mul(pv, f2_sub(g2, dd2)), g0, g1);
-          pp[2 * q + h2] = pack_bf16(p0, p1);
-          dd[2 * q + h2] = pack_bf16(g0, g1);
         }
       }
       // S^T / dP^T fully read: the staging area must be free of item it-1's accumulations
