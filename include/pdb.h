@@ -162,6 +162,13 @@ size_t pdb_flash_bwd_noalloc_max_scratch(void);
  * status returned on this thread.  pdb_version returns a constant string that
  * keys compiled kernels (the backend fingerprint, registry.py:56-70). */
 int pdb_check_error(void* stream);
+/* Exercises the failure path of the bounded device waits: launches one
+ * thread that waits on a barrier phase that never completes, gives up after
+ * limit_ns (<= 2 s) and sets the device error word, so that the next
+ * pdb_check_error(stream) returns PDB_ERR_TIMEOUT and clears it.  No fault,
+ * no trap; the context stays usable.  (Host-side check of the reference's
+ * refusal discipline, fusion.py:855-868; there is no device counterpart.) */
+int pdb_selftest_wait_timeout(int64_t limit_ns, void* stream);
 const char* pdb_last_error_string(void);
 const char* pdb_version(void);
 

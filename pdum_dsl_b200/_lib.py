@@ -35,6 +35,7 @@ EXPORTS = (
     "pdb_flash_bwd_noalloc",
     "pdb_flash_bwd_noalloc_max_scratch",
     "pdb_check_error",
+    "pdb_selftest_wait_timeout",
     "pdb_last_error_string",
     "pdb_version",
 )
@@ -171,6 +172,7 @@ def load(path: Path | None = None) -> C.CDLL:
     lib.pdb_flash_bwd_noalloc_max_scratch.argtypes = []
     lib.pdb_flash_bwd_noalloc_max_scratch.restype = C.c_size_t
     lib.pdb_check_error.argtypes = [vp]
+    lib.pdb_selftest_wait_timeout.argtypes = [C.c_int64, vp]
     lib.pdb_last_error_string.restype = C.c_char_p
     lib.pdb_version.restype = C.c_char_p
     for name in EXPORTS:

@@ -108,3 +108,32 @@ extern "C" int pdb_check_error(void* stream) {
 extern "C" const char* pdb_last_error_string(void) { return pdb::g_err_text; }
 
 extern "C" const char* pdb_version(void) { return "pdb-sm100a-0.1.0"; }
+
+// ---------------------------------------------------------------------------
+// Self-test of the bounded-wait failure path: one thread waits on an mbarrier
+// phase that nothing will complete, gives up after `limit_ns` and reports
+// through the device error word, exactly as a stuck pipeline stage would.
+namespace pdb {
+namespace {
+__global__ void selftest_wait_kernel(unsigned long long limit_ns, int* err) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, err, limit_ns);  // never arrives
+  __syncthreads();
+}
+}  // namespace
+}  // namespace pdb
+
+extern "C" int pdb_selftest_wait_timeout(int64_t limit_ns, void* stream) {
+  if (limit_ns <= 0 || limit_ns > 2000000000LL) return pdb::set_error(PDB_ERR_ARG, "limit_ns must be in (0, 2e9]");
+  int* flag = pdb::device_error_flag();
+  if (!flag) return pdb::set_error(PDB_ERR_CUDA, "device error flag unavailable");
+  pdb::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>((unsigned long long)limit_ns, flag);
+  return pdb::cuda_status(cudaGetLastError(), "selftest launch");
+}

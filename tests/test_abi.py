@@ -75,3 +75,9 @@ def test_python_layer_raises_on_host_tensors():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(_lib.BackendUnavailable):
         _lib.load(tmp_path / "nope.so")
+
+
+def test_selftest_rejects_unbounded_limits():
+    lib = _lib.load()
+    assert lib.pdb_selftest_wait_timeout(0, None) == _lib.PDB_ERR_ARG
+    assert lib.pdb_selftest_wait_timeout(3_000_000_000, None) == _lib.PDB_ERR_ARG
