@@ -241,8 +241,9 @@ def _attention_dims(region, q, k, v, e, s, t_hint=None):
     return qi, ki, vi, qd, kd, vd, t, o_cand[0], riders_k, group, tdim.start
 
 
-def match_naive_attention(region) -> AttentionSpec:
-    yld = region.body[-1].args[0]
+def match_naive_attention(region, yld=None) -> AttentionSpec:
+    """``yld`` (default: the region's yield) is the node to read as attention."""
+    yld = region.body[-1].args[0] if yld is None else yld
     artifacts = False
     m_out = den_out = None
     if yld.op == "core.tuple":

@@ -111,3 +111,17 @@ def test_widened_plan_region(dsl):
 
     (g,) = plan_region(row_softmax_region(4, 8)).groups  # untouched rows stay the reference's
     assert g.template == "row-normalization"
+
+
+def test_compile_grad_reads_the_autodiff_joint(dsl):
+    from pdum.tl.autodiff import grad
+
+    from pdum_dsl_b200.grad import compile_grad
+    from pdum_dsl_b200.regions import attention_region
+
+    r = attention_region(B=1, H=2, T=8, D=64, causal=True, scale=0.5)
+    out = r.body[-1].args[0]
+    names = {id(p): f"p{i}" for i, p in enumerate(r.params)}
+    names[id(out)] = "out"
+    run = compile_grad(grad(r, "out", seed="dO", names=names))
+    assert run.spec.causal and run.spec.scale == 0.5 and run.spec.riders == ("b", "h")
