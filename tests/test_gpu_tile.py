@@ -148,3 +148,41 @@ def test_row_regions_through_plan(cuda, dsl, case):
     region = row_softmax_region(r["R"], r["C"]) if r["kind"] == "softmax" else layernorm_region(r["R"], r["C"], r["eps"])
     (g,) = plan_region(region).groups
     assert_f32(compile_tile(g.kernel)(ins), want, what=case)
+
+
+def test_the_first_measurement_greens_the_group(cuda, dsl):
+    """A measured fact lands in the reference's ledger keyed by (kernel content,
+    machine) and is never re-measured warm (analysis.py:121-146), as the
+    reference's own device test does for its Triton column."""
+    import time
+    from dataclasses import replace
+
+    import torch
+    from pdum.tl.analysis import defanalysis, no_reanalysis
+    from pdum.tl.fusion import plan_region
+    from pdum.tl.zoo.tiles import flash_tile
+
+    from pdum_dsl_b200.tile import compile_tile
+
+    f = flash_tile(T=256, E=64, OD=64, SI=2)
+    (g,) = plan_region(f.naive).groups
+    arrays = [v.to_numpy() for v in f.inputs.values()]
+
+    @defanalysis("fusion.sm100a-ms", 1, ledger=True)
+    def sm100_ms(kernel, *, machine, reps=10):
+        run = compile_tile(kernel, dtype="bf16")
+        run(arrays)
+        laps = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            run(arrays)
+            laps.append(time.perf_counter() - t0)
+        return {"ms": sorted(laps)[len(laps) // 2] * 1e3, "reps": reps}
+
+    machine = torch.cuda.get_device_name(0)
+    fact = sm100_ms(g.kernel, machine=machine)
+    assert fact.value["ms"] > 0
+    with no_reanalysis():
+        again = sm100_ms(g.kernel, machine=machine)
+    assert again.key == fact.key
+    assert replace(g, confidence="green").confidence == "green"
