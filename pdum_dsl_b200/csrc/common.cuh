@@ -52,6 +52,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
 }
+// One arrival per warp: every lane orders its tcgen05 ops before the warp
+// sync, then lane 0 arrives (the barrier counts warps, not threads).
+__device__ __forceinline__ void warp_arrive_after_tc(uint64_t* bar) {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                                                static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+                                            : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

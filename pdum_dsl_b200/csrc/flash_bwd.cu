@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar->s_full[i], 1);
-      mbar_init(&bar->p_full[i], 128);
+      mbar_init(&bar->p_full[i], 4);  // one arrival per compute warp
     }
     mbar_init(&bar->o_full, 1);
     bar->abort = 0;
@@ -297,8 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st16(tb + 64 + hf * 16, dd);
       }
       tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bar->p_full[x]);
+      warp_arrive_after_tc(&bar->p_full[x]);
     }
     if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
       tc_fence_after();
@@ -376,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar->s_full[i], 1);
-      mbar_init(&bar->p_full[i], 128);
+      mbar_init(&bar->p_full[i], 4);  // one arrival per compute warp
     }
     mbar_init(&bar->o_full, 1);
     bar->abort = 0;
@@ -463,8 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               dd);
       tmem_st32(tb, dd);
       tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bar->p_full[x]);
+      warp_arrive_after_tc(&bar->p_full[x]);
     }
     if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
       tc_fence_after();
@@ -540,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->op_empty[i], 1);
     }
     mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->p_full, 256);
+    mbar_init(&bar->p_full, 8);  // one arrival per compute warp
     mbar_init(&bar->stage_free, 1);
     mbar_init(&bar->o_full, 1);
     bar->abort = 0;
@@ -661,8 +659,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st32(tl + 256 + w * 32, pp);
       tmem_st32(tl + 320 + w * 32, dd);
       tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bar->p_full);
+      warp_arrive_after_tc(&bar->p_full);
     }
     if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
       tc_fence_after();
@@ -726,7 +723,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->op_empty[i], 1);
     }
     mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->p_full, 256);
+    mbar_init(&bar->p_full, 8);  // one arrival per compute warp
     mbar_init(&bar->stage_free, 1);
     mbar_init(&bar->o_full, 1);
     bar->abort = 0;
@@ -826,8 +823,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       tmem_st32(tl + 256 + w * 32, dd);
       tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bar->p_full);
+      warp_arrive_after_tc(&bar->p_full);
     }
     if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
       tc_fence_after();

@@ -160,9 +160,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->v_full[i], 1);
       mbar_init(&bar->v_empty[i], 1);
       mbar_init(&bar->s_full[i], 1);
-      mbar_init(&bar->p_full[i], BM);
+      mbar_init(&bar->p_full[i], BM / 32);  // one arrival per softmax warp
       mbar_init(&bar->o_full[i], 1);
-      mbar_init(&bar->o_empty[i], BM);
+      mbar_init(&bar->o_empty[i], BM / 32);
     }
     bar->abort = 0;
     fence_barrier_init();
@@ -364,8 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         f2_unpack(sum_b, sb0, sb1);
         l += (sa0 + sa1) + (sb0 + sb1);
         tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&bar->p_full[x]);
+        warp_arrive_after_tc(&bar->p_full[x]);
       }
       if (!ok || !(ok = mbar_wait(&bar->o_full[x], tt & 1, abort, p.err))) break;
       tc_fence_after();
@@ -389,8 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&bar->o_empty[x]);  // O_x may now be overwritten by the next tile
+      warp_arrive_after_tc(&bar->o_empty[x]);  // O_x may now be overwritten by the next tile
       if (store) {
         const int64_t idx = bhq * p.T + t;
         constexpr float kLn2 = 0.6931471805599453f;
