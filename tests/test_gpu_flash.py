@@ -145,3 +145,23 @@ def test_bf16_config3_slices(cuda):
         ro, *_ = OA.attention_fwd(*(x[b, h].double().cpu().numpy() for x in (q, k, v)), scale=1 / math.sqrt(128),
                                   causal=True)
         assert_bf16(_np(o[b, h]), ro, what=f"head ({b},{h})")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_query_offset_rows_see_the_absolute_causal_mask(cuda, dtype):
+    """A row slab t in [q_start, q_start + T) of a longer sequence (the reference's
+    iota masks use absolute coordinates, dialect.py:1382-1383)."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device="cpu").manual_seed(17)
+    T, S, D, q_start = 200, 333, 64, 133
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    q = torch.randn(1, 2, T, D, generator=g).to(tdt)
+    k = torch.randn(1, 2, S, D, generator=g).to(tdt)
+    v = torch.randn(1, 2, S, D, generator=g).to(tdt)
+    o = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), scale=0.125, causal=True, q_start=q_start)
+    ro, *_ = OA.attention_fwd(q.double().numpy(), k.double().numpy(), v.double().numpy(), scale=0.125, causal=True,
+                              q_start=q_start)
+    (assert_bf16 if dtype == "bf16" else assert_f32)(_np(o), ro)

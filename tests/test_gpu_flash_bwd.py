@@ -84,3 +84,24 @@ def test_bwd_config5_slices(cuda):
         assert_bf16(_np(gq[b, h]), rq, what=f"dq ({b},{h})")
         assert_bf16(_np(gk[b, h]), rk, what=f"dk ({b},{h})")
         assert_bf16(_np(gv[b, h]), rv, what=f"dv ({b},{h})")
+
+
+def test_bwd_query_offset(cuda):
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device="cpu").manual_seed(21)
+    T, S, D, q_start = 130, 300, 64, 170
+    q = torch.randn(1, 2, T, D, generator=g).to(torch.bfloat16)
+    k, v = (torch.randn(1, 2, S, D, generator=g).to(torch.bfloat16) for _ in range(2))
+    do = torch.randn(1, 2, T, D, generator=g).to(torch.bfloat16)
+    o, lse = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), scale=0.125, causal=True,
+                                     q_start=q_start, return_lse=True)
+    gq, gk, gv = kernels.flash_attention_backward(q.to(cuda), k.to(cuda), v.to(cuda), o, do.to(cuda), lse,
+                                                  scale=0.125, causal=True, q_start=q_start)
+    rq, rk, rv = OA.attention_bwd(*(x.double().numpy() for x in (q, k, v, do)), scale=0.125, causal=True,
+                                  q_start=q_start)
+    assert_bf16(_np(gq), rq, what="dq")
+    assert_bf16(_np(gk), rk, what="dk")
+    assert_bf16(_np(gv), rv, what="dv")
