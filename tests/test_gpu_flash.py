@@ -165,3 +165,20 @@ def test_query_offset_rows_see_the_absolute_causal_mask(cuda, dtype):
     ro, *_ = OA.attention_fwd(q.double().numpy(), k.double().numpy(), v.double().numpy(), scale=0.125, causal=True,
                               q_start=q_start)
     (assert_bf16 if dtype == "bf16" else assert_f32)(_np(o), ro)
+
+
+@pytest.mark.parametrize("hq,hkv,chunks", [(4, 4, 3), (8, 2, 8), (2, 2, 1)])
+def test_host_buffer_entry_point_matches_the_device_path(cuda, hq, hkv, chunks):
+    import torch
+
+    from pdum_dsl_b200 import kernels
+    from pdum_dsl_b200.host import flash_attention_host
+
+    g = torch.Generator(device="cpu").manual_seed(hq * 10 + chunks)
+    q = torch.randn(2, hq, 300, 128, generator=g).to(torch.bfloat16).pin_memory()
+    k = torch.randn(2, hkv, 300, 128, generator=g).to(torch.bfloat16).pin_memory()
+    v = torch.randn(2, hkv, 300, 128, generator=g).to(torch.bfloat16).pin_memory()
+    out = torch.empty_like(q).pin_memory()
+    flash_attention_host(q, k, v, out, causal=True, chunks=chunks)
+    want = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), causal=True).cpu()
+    assert torch.equal(out, want)
