@@ -182,3 +182,22 @@ def test_host_buffer_entry_point_matches_the_device_path(cuda, hq, hkv, chunks):
     flash_attention_host(q, k, v, out, causal=True, chunks=chunks)
     want = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), causal=True).cpu()
     assert torch.equal(out, want)
+
+
+def test_bf16_config4_gqa_slices(cuda):
+    """Config 4 (B4 Hq64 Hkv8 S8192 D128 causal, GQA 8:1): full-size launch, sampled heads vs the oracle."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device=cuda).manual_seed(4)
+    q = torch.randn((4, 64, 8192, 128), device=cuda, generator=g).to(torch.bfloat16)
+    k = torch.randn((4, 8, 8192, 128), device=cuda, generator=g).to(torch.bfloat16)
+    v = torch.randn((4, 8, 8192, 128), device=cuda, generator=g).to(torch.bfloat16)
+    o = kernels.flash_attention(q, k, v, causal=True)
+    kernels.check_device_errors()
+    for b, h in ((0, 0), (3, 63)):
+        hk = h // 8
+        ro, *_ = OA.attention_fwd(q[b, h].double().cpu().numpy(), k[b, hk].double().cpu().numpy(),
+                                  v[b, hk].double().cpu().numpy(), scale=1 / math.sqrt(128), causal=True)
+        assert_bf16(_np(o[b, h]), ro, what=f"head ({b},{h})")
