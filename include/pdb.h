@@ -154,6 +154,64 @@ int pdb_flash_bwd(const pdb_flash_bwd_desc* d, void* stream);
 int pdb_flash_bwd_noalloc(const pdb_flash_bwd_desc* d, void* stream);
 size_t pdb_flash_bwd_noalloc_max_scratch(void);
 
+/* ---- contraction-epilogue and map-chain templates ---------------------------
+ * Replace the "contraction-epilogue" template (fusion.py:159-324: a sum over
+ * one contracted dim of a product of two operands, with an absorbed pointwise
+ * epilogue) and the "map-chain" template (a pure pointwise chain) as
+ * compile_tile lowers them (triton_tile.py:471-546).  The epilogue is a short
+ * program of pointwise steps applied to each accumulator element (or, for
+ * pdb_pointwise_f32, to each input element):
+ *   value = op(value)              (unary: exp, log, sqrt, tanh, neg)
+ *   value = op(value, operand)     (binary; swap = 1 gives op(operand, value))
+ * where the operand is a constant or a float32 tensor read at the element's
+ * (batch, m, n) coordinate through three element strides (0 broadcasts). */
+enum pdb_ew_opcode {
+  PDB_EW_ADD = 1, PDB_EW_SUB, PDB_EW_MUL, PDB_EW_DIV, PDB_EW_MAX, PDB_EW_MIN,
+  PDB_EW_EXP, PDB_EW_LOG, PDB_EW_SQRT, PDB_EW_TANH, PDB_EW_NEG
+};
+#define PDB_MAX_EW_OPS 8
+typedef struct {
+  int32_t op;       /* enum pdb_ew_opcode */
+  int32_t operand;  /* 0 none (unary), 1 constant, 2 tensor */
+  int32_t swap;
+  int32_t reserved;
+  double value;
+  const float* ptr;
+  int64_t stride[3]; /* (batch, m, n) */
+} pdb_ew_op;
+
+/* c[b, m, n] = epilogue(alpha * sum_k a[b, m, k] * b[b, n, k]).
+ * dtype PDB_F32: f32 operands / output, IEEE FMA (the reference's f32 column);
+ * dtype PDB_BF16: bf16 operands with k contiguous (TMA, 16-byte rows), fp32
+ * accumulate in TMEM (tcgen05), f32 epilogue, bf16 output. */
+typedef struct {
+  const void* a;
+  const void* b;
+  void* c;
+  int64_t batch, m, n, k;
+  int64_t a_stride[3]; /* (batch, m, k) */
+  int64_t b_stride[3]; /* (batch, n, k) */
+  int64_t c_stride[3]; /* (batch, m, n) */
+  double alpha;
+  int32_t dtype;
+  int32_t n_ops;
+  pdb_ew_op ops[PDB_MAX_EW_OPS];
+} pdb_contract_desc;
+int pdb_contract(const pdb_contract_desc* d, void* stream);
+
+/* y[b, m, n] = epilogue(x[b, m, n]), f32 (map-chain template; also the
+ * materialised prologue of a computed contraction operand). */
+typedef struct {
+  const float* x;
+  float* y;
+  int64_t batch, m, n;
+  int64_t x_stride[3], y_stride[3];
+  int32_t n_ops;
+  int32_t reserved;
+  pdb_ew_op ops[PDB_MAX_EW_OPS];
+} pdb_pointwise_desc;
+int pdb_pointwise_f32(const pdb_pointwise_desc* d, void* stream);
+
 /* ---- status --------------------------------------------------------------------
  * pdb_check_error synchronises `stream`, reads and clears the device error flag
  * of the current device (set by bounded waits that expired) and returns

@@ -34,6 +34,8 @@ EXPORTS = (
     "pdb_flash_bwd_workspace_size",
     "pdb_flash_bwd_noalloc",
     "pdb_flash_bwd_noalloc_max_scratch",
+    "pdb_contract",
+    "pdb_pointwise_f32",
     "pdb_check_error",
     "pdb_selftest_wait_timeout",
     "pdb_last_error_string",
@@ -143,6 +145,57 @@ class FlashBwdDesc(C.Structure):
     ]
 
 
+EW_OPS = {"add": 1, "sub": 2, "mul": 3, "div": 4, "maximum": 5, "minimum": 6, "exp": 7, "log": 8, "sqrt": 9,
+          "tanh": 10, "neg": 11}
+MAX_EW_OPS = 8
+
+
+class EwOp(C.Structure):
+    _fields_ = [
+        ("op", C.c_int32),
+        ("operand", C.c_int32),
+        ("swap", C.c_int32),
+        ("reserved", C.c_int32),
+        ("value", C.c_double),
+        ("ptr", C.c_void_p),
+        ("stride", I64x3),
+    ]
+
+
+class ContractDesc(C.Structure):
+    _fields_ = [
+        ("a", C.c_void_p),
+        ("b", C.c_void_p),
+        ("c", C.c_void_p),
+        ("batch", C.c_int64),
+        ("m", C.c_int64),
+        ("n", C.c_int64),
+        ("k", C.c_int64),
+        ("a_stride", I64x3),
+        ("b_stride", I64x3),
+        ("c_stride", I64x3),
+        ("alpha", C.c_double),
+        ("dtype", C.c_int32),
+        ("n_ops", C.c_int32),
+        ("ops", EwOp * MAX_EW_OPS),
+    ]
+
+
+class PointwiseDesc(C.Structure):
+    _fields_ = [
+        ("x", C.c_void_p),
+        ("y", C.c_void_p),
+        ("batch", C.c_int64),
+        ("m", C.c_int64),
+        ("n", C.c_int64),
+        ("x_stride", I64x3),
+        ("y_stride", I64x3),
+        ("n_ops", C.c_int32),
+        ("reserved", C.c_int32),
+        ("ops", EwOp * MAX_EW_OPS),
+    ]
+
+
 _LIB = None
 
 
@@ -171,6 +224,8 @@ def load(path: Path | None = None) -> C.CDLL:
     lib.pdb_flash_bwd_noalloc.argtypes = [C.POINTER(FlashBwdDesc), vp]
     lib.pdb_flash_bwd_noalloc_max_scratch.argtypes = []
     lib.pdb_flash_bwd_noalloc_max_scratch.restype = C.c_size_t
+    lib.pdb_contract.argtypes = [C.POINTER(ContractDesc), vp]
+    lib.pdb_pointwise_f32.argtypes = [C.POINTER(PointwiseDesc), vp]
     lib.pdb_check_error.argtypes = [vp]
     lib.pdb_selftest_wait_timeout.argtypes = [C.c_int64, vp]
     lib.pdb_last_error_string.restype = C.c_char_p

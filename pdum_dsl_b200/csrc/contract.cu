@@ -1,0 +1,341 @@
+// Contraction-epilogue and map-chain templates.
+//
+// Reference rows: _match_contraction_epilogue / _generate_contraction
+// (fusion.py:159-324): a sum over one contracted dim of a two-operand
+// product, the pointwise epilogue absorbed so the accumulator never touches
+// memory; and the map-chain row (fusion.py:830-860).  The reference lowers
+// both through compile_tile (triton_tile.py:471-546) as an f32 IEEE dot.
+//
+// Here the epilogue is a short step program (pdb_ew_op) interpreted per
+// element by the kernel, so one prebuilt kernel serves every chain:
+//   * contract_f32_kernel  -- f32 operands, IEEE FMA, 64 x 64 tiles staged
+//                             through shared memory (the reference's column);
+//   * contract_bf16_kernel -- bf16 operands by TMA (128B swizzle), tcgen05
+//                             MMAs into a 128 x 128 fp32 TMEM accumulator
+//                             with a 4-stage K pipeline, the epilogue read
+//                             back lane-per-row and stored as bf16;
+//   * pointwise_f32_kernel -- the map-chain template over a strided tensor.
+#include <cfloat>
+
+#include "common.cuh"
+#include "tma.h"
+
+namespace pdb {
+namespace {
+
+struct EwOp {  // device copy of pdb_ew_op with the constant already in f32
+  int32_t op, operand, swap;
+  float value;
+  const float* ptr;
+  int64_t stride[3];
+};
+struct EwProgram {
+  int32_t n;
+  EwOp ops[PDB_MAX_EW_OPS];
+};
+
+EwProgram make_program(int n, const pdb_ew_op* ops) {
+  EwProgram pg{};
+  pg.n = n;
+  for (int s = 0; s < n; ++s) {
+    pg.ops[s].op = ops[s].op;
+    pg.ops[s].operand = ops[s].operand;
+    pg.ops[s].swap = ops[s].swap;
+    pg.ops[s].value = (float)ops[s].value;
+    pg.ops[s].ptr = ops[s].ptr;
+    for (int i = 0; i < 3; ++i) pg.ops[s].stride[i] = ops[s].stride[i];
+  }
+  return pg;
+}
+
+__device__ __forceinline__ float ew_apply(const EwProgram& pg, float v, int64_t b, int64_t i, int64_t j) {
+  for (int s = 0; s < pg.n; ++s) {
+    const EwOp& o = pg.ops[s];
+    float w = 0.f;
+    if (o.operand == 1) w = o.value;
+    else if (o.operand == 2) w = __ldg(o.ptr + b * o.stride[0] + i * o.stride[1] + j * o.stride[2]);
+    float x = v, y = w;
+    if (o.swap) {
+      x = w;
+      y = v;
+    }
+    switch (o.op) {
+      case PDB_EW_ADD: v = x + y; break;
+      case PDB_EW_SUB: v = x - y; break;
+      case PDB_EW_MUL: v = x * y; break;
+      case PDB_EW_DIV: v = x / y; break;
+      case PDB_EW_MAX: v = fmaxf(x, y); break;
+      case PDB_EW_MIN: v = fminf(x, y); break;
+      case PDB_EW_EXP: v = expf(v); break;
+      case PDB_EW_LOG: v = logf(v); break;
+      case PDB_EW_SQRT: v = sqrtf(v); break;
+      case PDB_EW_TANH: v = tanhf(v); break;
+      case PDB_EW_NEG: v = -v; break;
+      default: break;
+    }
+  }
+  return v;
+}
+
+struct ContractParams {
+  const void* a;
+  const void* b;
+  void* c;
+  int64_t batch, m, n, k;
+  int64_t as[3], bs[3], cs[3];
+  float alpha;
+  int* err;
+  EwProgram pg;
+};
+
+// ------------------------------------------------------------------ f32 path
+constexpr int FT = 64, FK = 16, FTHREADS = 256;
+
+__global__ void __launch_bounds__(FTHREADS) contract_f32_kernel(const ContractParams p) {
+  __shared__ float As[FK][FT + 1];
+  __shared__ float Bs[FK][FT + 1];
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int64_t bidx = blockIdx.z;
+  const int64_t m0 = (int64_t)blockIdx.y * FT, n0 = (int64_t)blockIdx.x * FT;
+  const float* A = static_cast<const float*>(p.a) + bidx * p.as[0];
+  const float* B = static_cast<const float*>(p.b) + bidx * p.bs[0];
+  float acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < p.k; k0 += FK) {
+    for (int e = tid; e < FT * FK; e += FTHREADS) {
+      const int r = e / FK, kk = e % FK;
+      const int64_t gm = m0 + r, gn = n0 + r, gk = k0 + kk;
+      As[kk][r] = (gm < p.m && gk < p.k) ? A[gm * p.as[1] + gk * p.as[2]] : 0.f;
+      Bs[kk][r] = (gn < p.n && gk < p.k) ? B[gn * p.bs[1] + gk * p.bs[2]] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < FK; ++kk) {
+      float a[4], bb[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        a[u] = As[kk][ty * 4 + u];
+        bb[u] = Bs[kk][tx + 16 * u];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int w = 0; w < 4; ++w) acc[u][w] = fmaf(a[u], bb[w], acc[u][w]);
+    }
+    __syncthreads();
+  }
+  float* C = static_cast<float*>(p.c);
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int64_t gm = m0 + ty * 4 + u, gn = n0 + tx + 16 * w;
+      if (gm < p.m && gn < p.n)
+        C[bidx * p.cs[0] + gm * p.cs[1] + gn * p.cs[2]] = ew_apply(p.pg, acc[u][w] * p.alpha, bidx, gm, gn);
+    }
+}
+
+// ----------------------------------------------------------------- bf16 path
+constexpr int GM = 128, GN = 128, GK = 64, GSTAGES = 4, GTHREADS = 256;
+constexpr int kStageA = GM * GK * 2, kStageB = GN * GK * 2;
+
+struct __align__(8) GemmBars {
+  uint64_t full[GSTAGES], empty[GSTAGES], done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(GTHREADS, 1)
+    contract_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                         const ContractParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + GSTAGES * kStageA;
+  GemmBars* bar = reinterpret_cast<GemmBars*>(sB + GSTAGES * kStageB);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bidx = blockIdx.z, m0 = blockIdx.y * GM, n0 = blockIdx.x * GN;
+  const int nk = (int)((p.k + GK - 1) / GK);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < GSTAGES; ++i) {
+      mbar_init(&bar->full[i], 1);
+      mbar_init(&bar->empty[i], 1);
+    }
+    mbar_init(&bar->done, 1);
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+
+  if (warp == 0 && lane == 0) {
+    for (int kb = 0; kb < nk; ++kb) {
+      const int st = kb % GSTAGES;
+      if (!mbar_wait(&bar->empty[st], ((kb / GSTAGES) & 1) ^ 1, abort, p.err)) break;
+      mbar_expect_tx(&bar->full[st], kStageA + kStageB);
+      tma_load_4d(sA + st * kStageA, &tm_a, &bar->full[st], kb * GK, m0, bidx, 0);
+      tma_load_4d(sB + st * kStageB, &tm_b, &bar->full[st], kb * GK, n0, bidx, 0);
+    }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = idesc_bf16(GM, GN, 0, 0);
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int st = kb % GSTAGES;
+      if (!(ok = mbar_wait(&bar->full[st], (kb / GSTAGES) & 1, abort, p.err))) break;
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(sA + st * kStageA), b0 = smem_u32(sB + st * kStageB);
+#pragma unroll
+      for (int kk = 0; kk < GK / 16; ++kk)
+        mma_ss(tmem, sdesc_sw128(a0 + kk * 32, 16, 1024), sdesc_sw128(b0 + kk * 32, 16, 1024), idesc,
+               (kb > 0 || kk > 0) ? 1u : 0u);
+      tc_commit(&bar->empty[st]);
+    }
+    if (ok) tc_commit(&bar->done);
+  } else if (warp >= 4) {
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int64_t gm = m0 + row;
+    const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16);
+    if (mbar_wait(&bar->done, 0, abort, p.err)) {
+      tc_fence_after();
+      __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.c) + (int64_t)bidx * p.cs[0] + gm * p.cs[1];
+#pragma unroll 1
+      for (int ch = 0; ch < GN / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(taddr + ch * 32, r);
+        tmem_wait_ld();
+        if (gm < p.m) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int64_t gn = n0 + ch * 32 + i;
+            if (gn < p.n)
+              C[gn * p.cs[2]] = __float2bfloat16(ew_apply(p.pg, __uint_as_float(r[i]) * p.alpha, bidx, gm, gn));
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+// -------------------------------------------------------------- map-chain
+struct PointwiseArgs {
+  const float* x;
+  float* y;
+  int64_t batch, m, n;
+  int64_t xs[3], ys[3];
+};
+
+__global__ void pointwise_f32_kernel(const PointwiseArgs d, const EwProgram pg) {
+  const int64_t total = d.batch * d.m * d.n;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j = e % d.n, i = (e / d.n) % d.m, b = e / (d.n * d.m);
+    const float v = d.x[b * d.xs[0] + i * d.xs[1] + j * d.xs[2]];
+    d.y[b * d.ys[0] + i * d.ys[1] + j * d.ys[2]] = ew_apply(pg, v, b, i, j);
+  }
+}
+
+int check_ops(int n, const pdb_ew_op* ops) {
+  if (n < 0 || n > PDB_MAX_EW_OPS) return set_error(PDB_ERR_ARG, "n_ops must be in [0, %d]", PDB_MAX_EW_OPS);
+  for (int s = 0; s < n; ++s) {
+    const pdb_ew_op& o = ops[s];
+    if (o.op < PDB_EW_ADD || o.op > PDB_EW_NEG) return set_error(PDB_ERR_ARG, "epilogue step %d: bad opcode", s);
+    const bool unary = o.op >= PDB_EW_EXP;
+    if (unary != (o.operand == 0)) return set_error(PDB_ERR_ARG, "epilogue step %d: operand kind mismatch", s);
+    if (o.operand == 2 && o.ptr == nullptr) return set_error(PDB_ERR_ARG, "epilogue step %d: null tensor", s);
+  }
+  return PDB_OK;
+}
+
+}  // namespace
+}  // namespace pdb
+
+using namespace pdb;
+
+extern "C" int pdb_contract(const pdb_contract_desc* d, void* stream) {
+  if (!d) return set_error(PDB_ERR_ARG, "null descriptor");
+  if (d->batch <= 0 || d->m <= 0 || d->n <= 0 || d->k <= 0)
+    return set_error(PDB_ERR_SHAPE, "contract: sizes must be positive");
+  if (!d->a || !d->b || !d->c) return set_error(PDB_ERR_ARG, "null a / b / c");
+  if (int st = check_ops(d->n_ops, d->ops)) return st;
+  if (d->batch > 65535 || d->m > (int64_t)65535 * GM || d->n > 0x7fffffffLL)
+    return set_error(PDB_ERR_SHAPE, "contract: grid too large");
+  ContractParams p{};
+  p.a = d->a;
+  p.b = d->b;
+  p.c = d->c;
+  p.batch = d->batch;
+  p.m = d->m;
+  p.n = d->n;
+  p.k = d->k;
+  for (int i = 0; i < 3; ++i) {
+    p.as[i] = d->a_stride[i];
+    p.bs[i] = d->b_stride[i];
+    p.cs[i] = d->c_stride[i];
+  }
+  p.alpha = (float)d->alpha;
+  p.err = device_error_flag();
+  p.pg = make_program(d->n_ops, d->ops);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (d->dtype == PDB_F32) {
+    dim3 grid((unsigned)((d->n + FT - 1) / FT), (unsigned)((d->m + FT - 1) / FT), (unsigned)d->batch);
+    contract_f32_kernel<<<grid, FTHREADS, 0, s>>>(p);
+    return cuda_status(cudaGetLastError(), "contract f32 launch");
+  }
+  if (d->dtype != PDB_BF16) return set_error(PDB_ERR_UNSUPPORTED, "contract: unknown dtype %d", d->dtype);
+  if (d->a_stride[2] != 1 || d->b_stride[2] != 1)
+    return set_error(PDB_ERR_ALIGN, "contract bf16: the contracted dim must be contiguous in a and b");
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[4] = {(uint64_t)d->k, (uint64_t)d->m, (uint64_t)d->batch, 1};
+    const uint64_t str[3] = {(uint64_t)d->a_stride[1] * 2, (uint64_t)(d->batch > 1 ? d->a_stride[0] : d->m * d->a_stride[1]) * 2,
+                             (uint64_t)(d->batch * (d->batch > 1 ? d->a_stride[0] : d->m * d->a_stride[1])) * 2};
+    const uint32_t box[4] = {GK, GM, 1, 1};
+    if (int st = encode_tma_4d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+  }
+  {
+    const uint64_t dims[4] = {(uint64_t)d->k, (uint64_t)d->n, (uint64_t)d->batch, 1};
+    const uint64_t str[3] = {(uint64_t)d->b_stride[1] * 2, (uint64_t)(d->batch > 1 ? d->b_stride[0] : d->n * d->b_stride[1]) * 2,
+                             (uint64_t)(d->batch * (d->batch > 1 ? d->b_stride[0] : d->n * d->b_stride[1])) * 2};
+    const uint32_t box[4] = {GK, GN, 1, 1};
+    if (int st = encode_tma_4d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+  }
+  const int smem = GSTAGES * (kStageA + kStageB) + 256 + 1024;
+  cudaError_t e = cudaFuncSetAttribute(contract_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_status(e, "contract bf16: smem attribute");
+  dim3 grid((unsigned)((d->n + GN - 1) / GN), (unsigned)((d->m + GM - 1) / GM), (unsigned)d->batch);
+  contract_bf16_kernel<<<grid, GTHREADS, smem, s>>>(ta, tb, p);
+  return cuda_status(cudaGetLastError(), "contract bf16 launch");
+}
+
+extern "C" int pdb_pointwise_f32(const pdb_pointwise_desc* d, void* stream) {
+  if (!d) return set_error(PDB_ERR_ARG, "null descriptor");
+  if (d->batch < 0 || d->m < 0 || d->n < 0) return set_error(PDB_ERR_SHAPE, "pointwise: negative size");
+  const int64_t total = d->batch * d->m * d->n;
+  if (total == 0) return PDB_OK;
+  if (!d->x || !d->y) return set_error(PDB_ERR_ARG, "null x / y");
+  if (int st = check_ops(d->n_ops, d->ops)) return st;
+  const EwProgram pg = make_program(d->n_ops, d->ops);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t blocks = (total + 255) / 256;
+  const int64_t cap = (int64_t)sm_count(dev) * 16;
+  PointwiseArgs a{d->x, d->y, d->batch, d->m, d->n, {d->x_stride[0], d->x_stride[1], d->x_stride[2]},
+                  {d->y_stride[0], d->y_stride[1], d->y_stride[2]}};
+  pointwise_f32_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, static_cast<cudaStream_t>(stream)>>>(a, pg);
+  return cuda_status(cudaGetLastError(), "pointwise launch");
+}

@@ -168,3 +168,74 @@ def check_device_errors() -> None:
     """Synchronise the current stream and raise if a bounded device wait expired."""
     s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
     check(load().pdb_check_error(s), "pdb_check_error")
+
+
+def _ew_program(ops, out_shape):
+    """ops: list of (name, operand) with operand None (unary), a float, or a CUDA
+    float32 tensor broadcastable to out_shape (batch, m, n)."""
+    if len(ops) > _lib.MAX_EW_OPS:
+        raise ValueError(f"at most {_lib.MAX_EW_OPS} epilogue steps")
+    arr = (_lib.EwOp * _lib.MAX_EW_OPS)()
+    keep = []
+    for i, (name, operand, swap) in enumerate(ops):
+        o = arr[i]
+        o.op = _lib.EW_OPS[name]
+        o.swap = int(bool(swap))
+        if operand is None:
+            o.operand = 0
+        elif isinstance(operand, (int, float)):
+            o.operand, o.value = 1, float(operand)
+        else:
+            t = operand.float().expand(out_shape)
+            keep.append(t)
+            o.operand, o.ptr = 2, t.data_ptr()
+            o.stride = _lib.I64x3(t.stride(0), t.stride(1), t.stride(2))
+    return arr, keep
+
+
+def contract(a: torch.Tensor, b: torch.Tensor, *, epilogue=(), alpha: float = 1.0,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """c[b, m, n] = epilogue(alpha * sum_k a[b, m, k] * b[b, n, k]).
+
+    a (batch, m, k), b (batch, n, k): f32 (IEEE path, f32 out) or bf16 with k
+    contiguous (tcgen05 path, bf16 out).  ``epilogue`` is a sequence of
+    (op, operand, swap) steps with operand None (unary), a float, or a CUDA
+    tensor broadcastable to (batch, m, n)."""
+    _need_cuda(a, b)
+    if a.dtype not in _DTYPES or b.dtype != a.dtype:
+        raise TypeError("contract: a and b must both be float32 or bfloat16")
+    Bt, M, K = a.shape
+    Bb, N, Kb = b.shape
+    if Bb != Bt or Kb != K:
+        raise ValueError(f"contract: incompatible a {tuple(a.shape)} b {tuple(b.shape)}")
+    if a.dtype == torch.bfloat16:
+        a = a if a.stride(2) == 1 else a.contiguous()
+        b = b if b.stride(2) == 1 else b.contiguous()
+    c = torch.empty((Bt, M, N), dtype=a.dtype, device=a.device) if out is None else out
+    d = _lib.ContractDesc()
+    d.a, d.b, d.c = a.data_ptr(), b.data_ptr(), c.data_ptr()
+    d.batch, d.m, d.n, d.k = Bt, M, N, K
+    d.a_stride, d.b_stride, d.c_stride = _s3(a), _s3(b), _s3(c)
+    d.alpha, d.dtype = float(alpha), _DTYPES[a.dtype]
+    ops, keep = _ew_program(list(epilogue), (Bt, M, N))
+    d.ops, d.n_ops = ops, len(epilogue)
+    check(load().pdb_contract(C.byref(d), _stream(a)), "pdb_contract")
+    del keep
+    return c
+
+
+def pointwise(x: torch.Tensor, program, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = program(x) elementwise over an f32 (batch, m, n) CUDA tensor (map-chain)."""
+    _need_cuda(x)
+    if x.dtype != torch.float32 or x.dim() != 3:
+        raise TypeError("pointwise: a 3-D float32 tensor")
+    y = torch.empty(x.shape, dtype=torch.float32, device=x.device) if out is None else out
+    d = _lib.PointwiseDesc()
+    d.x, d.y = x.data_ptr(), y.data_ptr()
+    d.batch, d.m, d.n = x.shape
+    d.x_stride, d.y_stride = _s3(x), _s3(y)
+    ops, keep = _ew_program(list(program), tuple(x.shape))
+    d.ops, d.n_ops = ops, len(program)
+    check(load().pdb_pointwise_f32(C.byref(d), _stream(x)), "pdb_pointwise_f32")
+    del keep
+    return y

@@ -472,11 +472,219 @@ def match_rows(region) -> RowSpec:
 
 
 def recognize(region):
-    """-> AttentionSpec | RowSpec, or raise Untranslatable."""
-    try:
-        return match_attention(region)
-    except Untranslatable as attn_err:
+    """-> AttentionSpec | RowSpec | ContractSpec, or raise Untranslatable."""
+    errs = []
+    for name, fn in (("attention", match_attention), ("rows", match_rows), ("contraction", lambda r: match_any_contraction(r))):
         try:
-            return match_rows(region)
-        except Untranslatable as row_err:
-            raise Untranslatable(f"no sm_100a template: attention: {attn_err}; rows: {row_err}") from None
+            return fn(region)
+        except Untranslatable as e:
+            errs.append(f"{name}: {e}")
+    raise Untranslatable("no sm_100a template: " + "; ".join(errs))
+
+
+# ------------------------------------------------------- contraction-epilogue
+_UNARY = ("exp", "log", "sqrt", "tanh", "neg")
+_BINARY = ("add", "sub", "mul", "div", "maximum", "minimum")
+
+
+@dataclass(frozen=True)
+class Leaf:
+    """An epilogue operand: a constant, or a region param read at the output's coordinates."""
+
+    const: float | None = None
+    param: int | None = None
+    dims: tuple = ()
+
+
+@dataclass(frozen=True)
+class ContractSpec:
+    a: int  # param indices of the two operand params
+    b: int
+    a_pro: tuple  # unary prologue steps applied to the operand params (innermost first)
+    b_pro: tuple
+    a_dims: tuple
+    b_dims: tuple
+    k: tuple  # contracted dims
+    batch: tuple  # kept dims shared by both operands
+    m: tuple  # kept dims of a only
+    n: tuple  # kept dims of b only
+    mean: bool
+    epilogue: tuple  # (op, Leaf | None, swap), applied from the accumulator outwards
+    out_dims: tuple
+
+
+def _contains(n, target, memo=None) -> bool:
+    memo = {} if memo is None else memo
+    if n is target:
+        return True
+    if id(n) in memo:
+        return memo[id(n)]
+    args = n.args[:1] if n.op == "tl.repeat_like" else n.args  # the "like" operand is shape only
+    r = any(_contains(a, target, memo) for a in args)
+    memo[id(n)] = r
+    return r
+
+
+def _leaf(region, n) -> Leaf | None:
+    while n.op in ("tl.repeat_like", "tl.stage"):
+        n = n.args[0]
+    if is_const(n):
+        return Leaf(const=const_value(n))
+    i = _param_index(region, n)
+    if i is not None:
+        return Leaf(param=i, dims=names_of(n))
+    return None
+
+
+def _operand(region, x):
+    """param, or a unary pointwise chain over a param -> (index, prologue, dims)."""
+    pro = []
+    while f_of(x) in _UNARY and len(x.args) == 1:
+        pro.append(f_of(x))
+        x = unstage(x.args[0])
+    i = _param_index(region, x)
+    if i is None:
+        raise Untranslatable(f"contraction operand {x.op} is not a param or a unary chain over one")
+    return i, tuple(reversed(pro)), names_of(x)
+
+
+def match_contraction(region) -> ContractSpec:
+    yld = region.body[-1].args[0]
+    if yld.op == "core.tuple":
+        raise Untranslatable("tuple yield")
+    reduces = [n for n in _walk(region) if n.op == "tl.reduce"]
+    if len(reduces) != 1:
+        raise Untranslatable("a contraction-epilogue region has exactly one reduce")
+    red = reduces[0]
+    a_ = attrs(red)
+    if a_.get("f") not in ("sum", "mean") or a_.get("zero") is not None:
+        raise Untranslatable("the reduce is not a sum / mean")
+    kdims = red_dims(red)
+    prod = red.args[0]
+    if f_of(prod) != "mul" or len(prod.args) != 2 or any(x.op != "tl.repeat_like" for x in prod.args):
+        raise Untranslatable("the reduce is not over a broadcast product (the GEMM shape)")
+    ra, rb = prod.args
+    xa, xb = unstage(ra.args[0]), unstage(rb.args[0])
+    if ra.args[1] is not rb.args[0] or rb.args[1] is not ra.args[0]:
+        raise Untranslatable("the product is not the broadcast pair of two operands")
+    ia, pa, da = _operand(region, xa)
+    ib, pb, db = _operand(region, xb)
+    if any(k not in da or k not in db for k in kdims):
+        raise Untranslatable("both operands must carry the contracted dims")
+    batch = tuple(n for n in da if n in db and n not in kdims)
+    m = tuple(n for n in da if n not in db)
+    n_ = tuple(n for n in db if n not in da)
+    if da == db:
+        raise Untranslatable("same-space operands (the rowsum shape) are not lowered")
+    for x, dd in ((xa, da), (xb, db)):
+        for d in dims_of(x):
+            if d.start != 0:
+                raise Untranslatable("operand dims must start at 0")
+    # epilogue: a linear chain from the yield down to the reduce
+    steps = []
+    node = yld
+    while node is not red:
+        f = f_of(node)
+        if f in _UNARY and len(node.args) == 1:
+            steps.append((f, None, False))
+            node = node.args[0]
+            continue
+        if f in _BINARY and len(node.args) == 2:
+            l, r = node.args
+            lc, rc = _contains(l, red), _contains(r, red)
+            if lc == rc:
+                raise Untranslatable("epilogue is not a chain over the accumulator")
+            other = r if lc else l
+            leaf = _leaf(region, other)
+            if leaf is None:
+                raise Untranslatable("epilogue operand is not a constant or a param")
+            if leaf.param is not None and not set(leaf.dims) <= set(names_of(red)):
+                raise Untranslatable("epilogue param has dims outside the output")
+            steps.append((f, leaf, not lc))
+            node = l if lc else r
+            continue
+        raise Untranslatable(f"epilogue step {node.op}/{f} is not lowered")
+    if len(steps) > 8:
+        raise Untranslatable("epilogue longer than 8 steps")
+    return ContractSpec(ia, ib, pa, pb, da, db, kdims, batch, m, n_, a_.get("f") == "mean", tuple(reversed(steps)),
+                        names_of(yld))
+
+
+def _walk(region):
+    seen, stack = set(), list(region.body)
+    while stack:
+        n = stack.pop()
+        if id(n) in seen:
+            continue
+        seen.add(id(n))
+        yield n
+        stack.extend(n.args)
+        for r in n.regions:
+            stack.extend(r.body)
+
+
+def match_contraction_tile(region) -> ContractSpec:
+    """The tile region _generate_contraction emits (fusion.py:268-324): a fold
+    over ``ko`` whose step adds reduce(sum over ki [+ rest], mul(rl(a), rl(b)))
+    to the accumulator, operands split at k, the epilogue rebuilt over the
+    fold's final (a mean's 1/N finalize is one more epilogue step)."""
+    yld = region.body[-1].args[0]
+    folds = [n for n in _walk(region) if n.op == "tl.fold"]
+    if len(folds) != 1:
+        raise Untranslatable("not a single-fold contraction tile")
+    fold = folds[0]
+    fa = attrs(fold)
+    if tuple(fa.get("state", ())) != ("acc",) or tuple(fa.get("element", ())) != ("a", "b"):
+        raise Untranslatable("fold is not the (acc | a, b) contraction fold")
+    acc0, at, bt = fold.args
+    if not is_const(acc0) or const_value(acc0) != 0.0 or at.op != "tl.split" or bt.op != "tl.split":
+        raise Untranslatable("fold sources are not split operands")
+    k = attrs(at)["name"]
+    step = fold.regions[0]
+    nxt = step.body[-1].args[0]
+    if f_of(nxt) != "add" or nxt.args[0] is not step.params[0] or nxt.args[1].op != "tl.reduce":
+        raise Untranslatable("fold step is not acc + reduce")
+    part = nxt.args[1]
+    rest = tuple(d for d in red_dims(part) if d != "ki")
+    prod = part.args[0]
+    if f_of(prod) != "mul" or any(x.op != "tl.repeat_like" for x in prod.args):
+        raise Untranslatable("fold step is not the broadcast product")
+    ia, pa, da = _operand(region, unstage(at.args[0]))
+    ib, pb, db = _operand(region, unstage(bt.args[0]))
+    kdims = (k,) + rest
+    batch = tuple(n for n in da if n in db and n not in kdims)
+    m = tuple(n for n in da if n not in db)
+    n_ = tuple(n for n in db if n not in da)
+    steps = []
+    node = yld
+    while node is not fold:
+        f = f_of(node)
+        if f in _UNARY and len(node.args) == 1:
+            steps.append((f, None, False))
+            node = node.args[0]
+            continue
+        if f in _BINARY and len(node.args) == 2:
+            l, r = node.args
+            lc, rc = _contains(l, fold), _contains(r, fold)
+            if lc == rc:
+                raise Untranslatable("epilogue is not a chain over the accumulator")
+            leaf = _leaf(region, r if lc else l)
+            if leaf is None:
+                raise Untranslatable("epilogue operand is not a constant or a param")
+            steps.append((f, leaf, not lc))
+            node = l if lc else r
+            continue
+        raise Untranslatable(f"epilogue step {node.op}/{f} is not lowered")
+    if len(steps) > 8:
+        raise Untranslatable("epilogue longer than 8 steps")
+    return ContractSpec(ia, ib, pa, pb, da, db, kdims, batch, m, n_, False, tuple(reversed(steps)), names_of(yld))
+
+
+def match_any_contraction(region) -> ContractSpec:
+    try:
+        return match_contraction(region)
+    except Untranslatable as e:
+        try:
+            return match_contraction_tile(region)
+        except Untranslatable:
+            raise e from None

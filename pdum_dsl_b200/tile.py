@@ -30,10 +30,60 @@ import math
 
 import numpy as np
 
-from .recognize import AttentionSpec, RowSpec, Untranslatable, recognize
+from .recognize import AttentionSpec, ContractSpec, RowSpec, Untranslatable, recognize
 
 # the executor fingerprint (the reference's Pair seat is keyed the same way, triton_tile.py:54)
 B200_FP = ("tile_sm100a", "pdb")
+
+
+def _prod(xs):
+    return math.prod(xs) if xs else 1
+
+
+def _run_contract(spec: ContractSpec, tensors, dtype):
+    """Device tensors -> c in the yield's dim order, through pdb_contract."""
+    import torch
+
+    from . import kernels
+
+    def sizes(t, dims, names):
+        return [t.shape[dims.index(n)] for n in names]
+
+    def operand(t, pro, dims, kept):
+        t = t.float() if t.dtype != torch.float32 else t
+        if pro:  # unary prologue chain, materialised once by the map-chain kernel
+            flat = kernels.pointwise(t.contiguous().reshape(1, 1, -1), [(f, None, False) for f in pro])
+            t = flat.reshape(t.shape)
+        v = t.permute(*[dims.index(n) for n in spec.batch + kept + spec.k])
+        return v.reshape(_prod(sizes(t, dims, spec.batch)), _prod(sizes(t, dims, kept)),
+                         _prod(sizes(t, dims, spec.k)))
+
+    a, b = tensors[spec.a], tensors[spec.b]
+    A = operand(a, spec.a_pro, spec.a_dims, spec.m)
+    Bm = operand(b, spec.b_pro, spec.b_dims, spec.n)
+    if dtype == "bf16":
+        A, Bm = A.to(torch.bfloat16).contiguous(), Bm.to(torch.bfloat16).contiguous()
+    bs = sizes(a, spec.a_dims, spec.batch)
+    ms = sizes(a, spec.a_dims, spec.m)
+    ns = sizes(b, spec.b_dims, spec.n)
+    full_names = spec.batch + spec.m + spec.n
+    full = bs + ms + ns
+    epi = []
+    for f, leaf, swap in spec.epilogue:
+        if leaf is None:
+            epi.append((f, None, False))
+        elif leaf.param is None:
+            epi.append((f, leaf.const, swap))
+        else:
+            t = tensors[leaf.param].float()
+            v = t.permute(*[leaf.dims.index(n) for n in full_names if n in leaf.dims])
+            shape = [full[i] if n in leaf.dims else 1 for i, n in enumerate(full_names)]
+            v = v.reshape(shape).expand(full).reshape(A.shape[0], A.shape[1], Bm.shape[1])
+            epi.append((f, v, swap))
+    alpha = 1.0 / _prod(sizes(a, spec.a_dims, spec.k)) if spec.mean else 1.0
+    c = kernels.contract(A, Bm, epilogue=epi, alpha=alpha)
+    c = c.reshape(full)
+    return c.permute(*[full_names.index(n) for n in spec.out_dims])
 
 
 def _check_launch(spec, launch, prune, region):
@@ -41,7 +91,12 @@ def _check_launch(spec, launch, prune, region):
     bounds (fusion.py:659-690).  The kernels tile internally (128/256-row programs) and
     visit only live key tiles, so these artifacts are validated and recorded, not obeyed."""
     out_dims = spec.out_dims
-    carried = {spec.s, spec.e} if isinstance(spec, AttentionSpec) else {spec.dim}
+    if isinstance(spec, AttentionSpec):
+        carried = {spec.s, spec.e}
+    elif isinstance(spec, ContractSpec):
+        carried = set(spec.k)
+    else:
+        carried = {spec.dim}
     for name, tile in launch:
         if name not in out_dims:
             raise Untranslatable(f"launch dim {name!r} is not an output dim")
@@ -78,6 +133,20 @@ class _Runner:
             self.source = (f"pdb_flash_fwd dtype={dtype} causal={spec.causal} scale={spec.scale} "
                            f"riders={spec.riders} group={spec.group} artifacts={spec.artifacts} "
                            f"kernel={'flash_fwd_sm100_kernel (tcgen05/TMEM, TMA)' if dtype == 'bf16' else 'flash_f32_kernel (IEEE FMA)'}")
+        elif isinstance(spec, ContractSpec):
+            def ext(i, names):
+                return _prod([next(d.stop - d.start for d in region.params[i].type.dims if d.name == n)
+                              for n in names])
+            Bt, M, N = ext(spec.a, spec.batch), ext(spec.a, spec.m), ext(spec.b, spec.n)
+            if dtype == "bf16":
+                self.grid = Bt * -(-M // 128) * -(-N // 128)
+                kern = "contract_bf16_kernel (tcgen05/TMEM, TMA)"
+            else:
+                self.grid = Bt * -(-M // 64) * -(-N // 64)
+                kern = "contract_f32_kernel (IEEE FMA)"
+            self.source = (f"pdb_contract dtype={dtype} batch={spec.batch} m={spec.m} n={spec.n} k={spec.k} "
+                           f"prologue=({spec.a_pro}, {spec.b_pro}) epilogue={[e[0] for e in spec.epilogue]} "
+                           f"kernel={kern}")
         else:
             R = 1
             for d in region.params[spec.x].type.dims:
@@ -92,6 +161,8 @@ class _Runner:
         from . import kernels
 
         spec = self.spec
+        if isinstance(spec, ContractSpec):
+            return _run_contract(spec, tensors, self.dtype)
         if isinstance(spec, RowSpec):
             x = tensors[spec.x]
             perm = [spec.x_dims.index(n) for n in spec.x_dims if n != spec.dim] + [spec.x_dims.index(spec.dim)]
@@ -182,6 +253,10 @@ def compile_tile(region, launch: tuple = (), prune: tuple = (), *, dtype: str = 
     spec = recognize(region)
     if isinstance(spec, RowSpec) and dtype != "f32":
         raise Untranslatable("row-reduction kernels are f32")
+    if isinstance(spec, ContractSpec) and dtype == "bf16":
+        kx = _prod([next(d.stop - d.start for d in region.params[spec.a].type.dims if d.name == n) for n in spec.k])
+        if kx % 8:
+            raise Untranslatable("bf16 contraction needs the contracted extent to be a multiple of 8 (16-byte rows)")
     if isinstance(spec, AttentionSpec) and dtype == "bf16":
         D = _extent(region, spec.q, spec.e)
         DV = _extent(region, spec.v, spec.o)

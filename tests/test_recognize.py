@@ -125,3 +125,34 @@ def test_compile_grad_reads_the_autodiff_joint(dsl):
     names[id(out)] = "out"
     run = compile_grad(grad(r, "out", seed="dO", names=names))
     assert run.spec.causal and run.spec.scale == 0.5 and run.spec.riders == ("b", "h")
+
+
+def _gemm_subject():
+    from pdum.dsl.ir import Builder, Region
+    from pdum.dsl.ops import CORE_OPS
+    from pdum.dsl.types import f64
+    from pdum.tl.dialect import TL_OPS, tensor_type_of_layout
+    from pdum.tl.tensor import Tensor
+
+    b = Builder({**CORE_OPS, **TL_OPS})
+    t = lambda shape, names: tensor_type_of_layout(Tensor.from_numpy(np.zeros(shape), names).layout)
+    pa, pb, pc = b.param(0, t((6, 8), ("m", "k"))), b.param(1, t((8, 5), ("k", "n"))), b.param(2, t((5,), ("n",)))
+    prod = b.emit("tl.pointwise", b.emit("tl.repeat_like", pa, pb), b.emit("tl.repeat_like", pb, pa), f="mul")
+    z = b.emit("tl.reduce", prod, dims=("k",), f="sum")
+    zb = b.emit("tl.pointwise", z, b.emit("tl.repeat_like", pc, z), f="add")
+    y = b.emit("tl.pointwise", zb, b.emit("core.const", type=f64, value=0.0), f="maximum")
+    return Region(params=(pa, pb, pc), body=(b.emit("core.yield", y),))
+
+
+def test_contraction_epilogue_naive_and_tile(dsl):
+    from pdum.tl.fusion import plan_region
+
+    from pdum_dsl_b200.recognize import ContractSpec
+
+    r = _gemm_subject()
+    s = recognize(r)
+    assert isinstance(s, ContractSpec) and (s.m, s.n, s.k) == (("m",), ("n",), ("k",))
+    assert [e[0] for e in s.epilogue] == ["add", "maximum"] and s.epilogue[0][1].param == 2
+    (g,) = plan_region(r).groups
+    assert g.template == "contraction-epilogue"
+    assert recognize(g.kernel) == s  # the generated fold reads the same
