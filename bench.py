@@ -310,7 +310,7 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def secondary(args, dev, stream, peaks, parts=("rows", "gqa", "bwd")):
+def secondary(args, dev, stream, peaks, parts=("rows", "gqa", "bwd", "gemm")):
     """Config 2 (row reductions), 4 (GQA) and 5 (backward) at N=1."""
     import torch
 
@@ -324,7 +324,25 @@ def secondary(args, dev, stream, peaks, parts=("rows", "gqa", "bwd")):
         _gqa(out, kernels, dev, stream, g)
     if "bwd" in parts:
         _bwd(out, kernels, dev, stream, g)
+    if "gemm" in parts:
+        _gemm(out, kernels, dev, stream, g, peaks)
     return out
+
+
+def _gemm(out, kernels, dev, stream, g, peaks):
+    """Contraction-epilogue template (bf16 tcgen05 path): relu(A B^T + bias), 8192^3."""
+    import torch
+
+    M = N = K = 8192
+    a = torch.randn((1, M, K), device=dev, generator=g).to(torch.bfloat16)
+    b = torch.randn((1, N, K), device=dev, generator=g).to(torch.bfloat16)
+    bias = torch.randn((1, 1, N), device=dev, generator=g)
+    c = torch.empty((1, M, N), dtype=torch.bfloat16, device=dev)
+    ep = [("add", bias, False), ("maximum", 0.0, False)]
+    ms, per = _timed(lambda: kernels.contract(a, b, epilogue=ep, out=c), 10, 3, stream, 1)
+    tf = 2.0 * M * N * K / (sum(per) / len(per) * 1e-3) / 1e12
+    out["contract_bf16"] = {"TFLOP/s": tf, "frac_peak": tf / peaks["bf16_tflops"], "ms": sum(per) / len(per),
+                            "config": "relu(A B^T + bias), M=N=K=8192, bf16 in/out, fp32 accumulate"}
 
 
 def _rows(out, kernels, dev, stream, peaks, g):
@@ -386,7 +404,7 @@ def main():
     ap.add_argument("--shape", default=None,
                     help="B,H,S,D override of the flash workload (profiling a smaller case); implies --kernel-only")
     ap.add_argument("--kernel-only", action="store_true", help="time only the flash forward (no e2e/extra/cpu)")
-    ap.add_argument("--only", choices=("rows", "gqa", "bwd"), default=None,
+    ap.add_argument("--only", choices=("rows", "gqa", "bwd", "gemm"), default=None,
                     help="run only one secondary workload (config 2, 4 or 5) and print it (profiling)")
     args = ap.parse_args()
     if args.only:

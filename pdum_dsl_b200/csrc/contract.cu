@@ -10,10 +10,10 @@
 // element by the kernel, so one prebuilt kernel serves every chain:
 //   * contract_f32_kernel  -- f32 operands, IEEE FMA, 64 x 64 tiles staged
 //                             through shared memory (the reference's column);
-//   * contract_bf16_kernel -- bf16 operands by TMA (128B swizzle), tcgen05
-//                             MMAs into a 128 x 128 fp32 TMEM accumulator
-//                             with a 4-stage K pipeline, the epilogue read
-//                             back lane-per-row and stored as bf16;
+//   * contract_bf16_kernel -- persistent; bf16 operands by TMA (128B swizzle),
+//                             tcgen05 M128 N256 MMAs into two fp32 TMEM
+//                             accumulators (epilogue of one tile overlaps the
+//                             next tile's K loop), stored as bf16;
 //   * pointwise_f32_kernel -- the map-chain template over a strided tensor.
 #include <cfloat>
 
@@ -135,11 +135,17 @@ __global__ void __launch_bounds__(FTHREADS) contract_f32_kernel(const ContractPa
 }
 
 // ----------------------------------------------------------------- bf16 path
-constexpr int GM = 128, GN = 128, GK = 64, GSTAGES = 4, GTHREADS = 256;
+// Persistent: one CTA per SM walks 128 x 256 output tiles.  Warp 0 streams A
+// (128 x 64) and B (256 x 64) k-blocks by TMA through a 4-stage ring, warp 1
+// issues M128 N256 K16 tcgen05 MMAs into one of two TMEM accumulators
+// (2 x 256 columns), warps 4..7 drain the other accumulator through the
+// epilogue program while the next tile accumulates.
+constexpr int GM = 128, GN = 256, GK = 64, GSTAGES = 4, GTHREADS = 256;
 constexpr int kStageA = GM * GK * 2, kStageB = GN * GK * 2;
 
 struct __align__(8) GemmBars {
-  uint64_t full[GSTAGES], empty[GSTAGES], done;
+  uint64_t full[GSTAGES], empty[GSTAGES];
+  uint64_t acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort;
 };
@@ -153,20 +159,24 @@ __global__ void __launch_bounds__(GTHREADS, 1)
   uint8_t* sB = smem + GSTAGES * kStageA;
   GemmBars* bar = reinterpret_cast<GemmBars*>(sB + GSTAGES * kStageB);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bidx = blockIdx.z, m0 = blockIdx.y * GM, n0 = blockIdx.x * GN;
   const int nk = (int)((p.k + GK - 1) / GK);
+  const int tm = (int)((p.m + GM - 1) / GM), tn = (int)((p.n + GN - 1) / GN);
+  const int num_tiles = (int)p.batch * tm * tn;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < GSTAGES; ++i) {
       mbar_init(&bar->full[i], 1);
       mbar_init(&bar->empty[i], 1);
     }
-    mbar_init(&bar->done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->acc_full[i], 1);
+      mbar_init(&bar->acc_empty[i], 4);  // one arrival per epilogue warp
+    }
     bar->abort = 0;
     fence_barrier_init();
   }
   if (warp == 2) {
-    tmem_alloc(&bar->tmem_base, 128);
+    tmem_alloc(&bar->tmem_base, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -174,59 +184,96 @@ __global__ void __launch_bounds__(GTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
   volatile int* abort = &bar->abort;
+  // tile t -> (batch, m-tile, n-tile), n fastest: consecutive CTAs share the A row-block in L2
+  auto coords = [&](int t, int& bi, int& m0, int& n0) {
+    bi = t / (tm * tn);
+    const int r = t % (tm * tn);
+    m0 = (r / tn) * GM;
+    n0 = (r % tn) * GN;
+  };
 
   if (warp == 0 && lane == 0) {
-    for (int kb = 0; kb < nk; ++kb) {
-      const int st = kb % GSTAGES;
-      if (!mbar_wait(&bar->empty[st], ((kb / GSTAGES) & 1) ^ 1, abort, p.err)) break;
-      mbar_expect_tx(&bar->full[st], kStageA + kStageB);
-      tma_load_4d(sA + st * kStageA, &tm_a, &bar->full[st], kb * GK, m0, bidx, 0);
-      tma_load_4d(sB + st * kStageB, &tm_b, &bar->full[st], kb * GK, n0, bidx, 0);
+    uint32_t g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+      int bi, m0, n0;
+      coords(t, bi, m0, n0);
+      for (int kb = 0; kb < nk; ++kb, ++g) {
+        const int st = g % GSTAGES;
+        if (!(ok = mbar_wait(&bar->empty[st], ((g / GSTAGES) & 1) ^ 1, abort, p.err))) break;
+        mbar_expect_tx(&bar->full[st], kStageA + kStageB);
+        tma_load_4d(sA + st * kStageA, &tm_a, &bar->full[st], kb * GK, m0, bi, 0);
+        tma_load_4d(sB + st * kStageB, &tm_b, &bar->full[st], kb * GK, n0, bi, 0);
+      }
     }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = idesc_bf16(GM, GN, 0, 0);
+    uint32_t g = 0, tt = 0;
     bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int st = kb % GSTAGES;
-      if (!(ok = mbar_wait(&bar->full[st], (kb / GSTAGES) & 1, abort, p.err))) break;
+    for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, ++tt) {
+      const int buf = tt & 1;
+      if (!(ok = mbar_wait(&bar->acc_empty[buf], ((tt >> 1) & 1) ^ 1, abort, p.err))) break;
       tc_fence_after();
-      const uint32_t a0 = smem_u32(sA + st * kStageA), b0 = smem_u32(sB + st * kStageB);
+      const uint32_t acc = tmem + buf * GN;
+      for (int kb = 0; kb < nk; ++kb, ++g) {
+        const int st = g % GSTAGES;
+        if (!(ok = mbar_wait(&bar->full[st], (g / GSTAGES) & 1, abort, p.err))) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + st * kStageA), b0 = smem_u32(sB + st * kStageB);
 #pragma unroll
-      for (int kk = 0; kk < GK / 16; ++kk)
-        mma_ss(tmem, sdesc_sw128(a0 + kk * 32, 16, 1024), sdesc_sw128(b0 + kk * 32, 16, 1024), idesc,
-               (kb > 0 || kk > 0) ? 1u : 0u);
-      tc_commit(&bar->empty[st]);
+        for (int kk = 0; kk < GK / 16; ++kk)
+          mma_ss(acc, sdesc_sw128(a0 + kk * 32, 16, 1024), sdesc_sw128(b0 + kk * 32, 16, 1024), idesc,
+                 (kb > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&bar->empty[st]);
+      }
+      if (ok) tc_commit(&bar->acc_full[buf]);
     }
-    if (ok) tc_commit(&bar->done);
   } else if (warp >= 4) {
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;
-    const int64_t gm = m0 + row;
-    const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16);
-    if (mbar_wait(&bar->done, 0, abort, p.err)) {
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const bool vec = p.cs[2] == 1 && (p.cs[1] & 7) == 0 && (p.cs[0] & 7) == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.c) & 15) == 0;
+    uint32_t tt = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tt) {
+      int bi, m0, n0;
+      coords(t, bi, m0, n0);
+      const int buf = tt & 1;
+      if (!mbar_wait(&bar->acc_full[buf], (tt >> 1) & 1, abort, p.err)) break;
       tc_fence_after();
-      __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.c) + (int64_t)bidx * p.cs[0] + gm * p.cs[1];
+      const int64_t gm = m0 + row;
+      __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.c) + (int64_t)bi * p.cs[0] + gm * p.cs[1];
 #pragma unroll 1
       for (int ch = 0; ch < GN / 32; ++ch) {
         uint32_t r[32];
-        tmem_ld32(taddr + ch * 32, r);
+        tmem_ld32(tmem + lane_off + buf * GN + ch * 32, r);
         tmem_wait_ld();
-        if (gm < p.m) {
+        const int64_t c0 = n0 + ch * 32;
+        if (gm >= p.m || c0 >= p.n) continue;
+        uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int64_t gn = n0 + ch * 32 + i;
-            if (gn < p.n)
-              C[gn * p.cs[2]] = __float2bfloat16(ew_apply(p.pg, __uint_as_float(r[i]) * p.alpha, bidx, gm, gn));
-          }
+        for (int i = 0; i < 16; ++i) {
+          const float v0 = ew_apply(p.pg, __uint_as_float(r[2 * i]) * p.alpha, bi, gm, c0 + 2 * i);
+          const float v1 = ew_apply(p.pg, __uint_as_float(r[2 * i + 1]) * p.alpha, bi, gm, c0 + 2 * i + 1);
+          pk[i] = pack_bf16(v0, v1);
+        }
+        if (vec && c0 + 32 <= p.n) {
+          uint4* dst = reinterpret_cast<uint4*>(C + c0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        } else {
+          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(pk);
+          for (int i = 0; i < 32 && c0 + i < p.n; ++i) C[(c0 + i) * p.cs[2]] = h[i];
         }
       }
+      warp_arrive_after_tc(&bar->acc_empty[buf]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -317,8 +364,12 @@ extern "C" int pdb_contract(const pdb_contract_desc* d, void* stream) {
   const int smem = GSTAGES * (kStageA + kStageB) + 256 + 1024;
   cudaError_t e = cudaFuncSetAttribute(contract_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_status(e, "contract bf16: smem attribute");
-  dim3 grid((unsigned)((d->n + GN - 1) / GN), (unsigned)((d->m + GM - 1) / GM), (unsigned)d->batch);
-  contract_bf16_kernel<<<grid, GTHREADS, smem, s>>>(ta, tb, p);
+  const int64_t tiles = d->batch * ((d->m + GM - 1) / GM) * ((d->n + GN - 1) / GN);
+  if (tiles > 0x7fffffffLL) return set_error(PDB_ERR_SHAPE, "contract bf16: too many tiles");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
+  contract_bf16_kernel<<<(unsigned)grid, GTHREADS, smem, s>>>(ta, tb, p);
   return cuda_status(cudaGetLastError(), "contract bf16 launch");
 }
 
