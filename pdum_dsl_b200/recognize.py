@@ -474,7 +474,7 @@ def match_rows(region) -> RowSpec:
 def recognize(region):
     """-> AttentionSpec | RowSpec | ContractSpec, or raise Untranslatable."""
     errs = []
-    for name, fn in (("attention", match_attention), ("rows", match_rows), ("contraction", lambda r: match_any_contraction(r))):
+    for name, fn in (("attention", match_attention), ("rows", match_rows), ("contraction", lambda r: match_any_contraction(r)), ("map-chain", lambda r: match_map_chain(r))):
         try:
             return fn(region)
         except Untranslatable as e:
@@ -688,3 +688,53 @@ def match_any_contraction(region) -> ContractSpec:
             return match_contraction_tile(region)
         except Untranslatable:
             raise e from None
+
+
+# ---------------------------------------------------------------- map-chain
+@dataclass(frozen=True)
+class MapSpec:
+    x: int  # the param at the bottom of the chain
+    x_dims: tuple
+    steps: tuple  # (op, Leaf | None, swap), innermost first
+    out_dims: tuple
+
+
+def match_map_chain(region) -> MapSpec:
+    """A linear pointwise chain over one param (the map-chain row, fusion.py:
+    847-858) whose other operands are constants or params broadcast to it."""
+    yld = region.body[-1].args[0]
+    if yld.op == "core.tuple":
+        raise Untranslatable("tuple yield")
+    steps = []
+    node = yld
+    while _param_index(region, unstage(node)) is None:
+        node = unstage(node)
+        f = f_of(node)
+        if f in _UNARY and len(node.args) == 1:
+            steps.append((f, None, False))
+            node = node.args[0]
+            continue
+        if f in _BINARY and len(node.args) == 2:
+            l, r = (unstage(a) for a in node.args)
+            lp = l.op == "tl.repeat_like" or is_const(l)
+            rp = r.op == "tl.repeat_like" or is_const(r)
+            # the spine is the operand that is not a broadcast leaf / constant
+            if not lp and (rp or _param_index(region, r) is not None):
+                spine, other, swap = l, r, False
+            elif not rp and (lp or _param_index(region, l) is not None):
+                spine, other, swap = r, l, True
+            else:
+                raise Untranslatable("map chain is not linear")
+            leaf = _leaf(region, other)
+            if leaf is None:
+                raise Untranslatable("map-chain operand is not a constant or a param")
+            steps.append((f, leaf, swap))
+            node = spine
+            continue
+        raise Untranslatable(f"map-chain step {node.op}/{f} is not lowered")
+    x = unstage(node)
+    if len(steps) > 8 or not steps:
+        raise Untranslatable("map chain must have 1..8 steps")
+    if set(names_of(x)) != set(names_of(yld)):
+        raise Untranslatable("the chain's base param must span the output")
+    return MapSpec(_param_index(region, x), names_of(x), tuple(reversed(steps)), names_of(yld))

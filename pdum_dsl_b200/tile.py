@@ -30,7 +30,7 @@ import math
 
 import numpy as np
 
-from .recognize import AttentionSpec, ContractSpec, RowSpec, Untranslatable, recognize
+from .recognize import AttentionSpec, ContractSpec, MapSpec, RowSpec, Untranslatable, recognize
 
 # the executor fingerprint (the reference's Pair seat is keyed the same way, triton_tile.py:54)
 B200_FP = ("tile_sm100a", "pdb")
@@ -86,6 +86,27 @@ def _run_contract(spec: ContractSpec, tensors, dtype):
     return c.permute(*[full_names.index(n) for n in spec.out_dims])
 
 
+def _run_map(spec: MapSpec, tensors):
+    """Device tensors -> the chain's output in the yield's dim order (pdb_pointwise_f32)."""
+    from . import kernels
+
+    x = tensors[spec.x].float().permute(*[spec.x_dims.index(n) for n in spec.out_dims])
+    full = list(x.shape)
+    flat = x.reshape(1, 1, -1)
+    prog = []
+    for f, leaf, swap in spec.steps:
+        if leaf is None:
+            prog.append((f, None, False))
+        elif leaf.param is None:
+            prog.append((f, leaf.const, swap))
+        else:
+            t = tensors[leaf.param].float()
+            v = t.permute(*[leaf.dims.index(n) for n in spec.out_dims if n in leaf.dims])
+            v = v.reshape([full[i] if n in leaf.dims else 1 for i, n in enumerate(spec.out_dims)]).expand(full)
+            prog.append((f, v.reshape(1, 1, -1), swap))
+    return kernels.pointwise(flat, prog).reshape(full)
+
+
 def _check_launch(spec, launch, prune, region):
     """launch: (output dim, tile) pairs (launch.py:95); prune: (scan dim, lo, hi) affine
     bounds (fusion.py:659-690).  The kernels tile internally (128/256-row programs) and
@@ -93,6 +114,8 @@ def _check_launch(spec, launch, prune, region):
     out_dims = spec.out_dims
     if isinstance(spec, AttentionSpec):
         carried = {spec.s, spec.e}
+    elif isinstance(spec, MapSpec):
+        carried = set()
     elif isinstance(spec, ContractSpec):
         carried = set(spec.k)
     else:
@@ -133,6 +156,10 @@ class _Runner:
             self.source = (f"pdb_flash_fwd dtype={dtype} causal={spec.causal} scale={spec.scale} "
                            f"riders={spec.riders} group={spec.group} artifacts={spec.artifacts} "
                            f"kernel={'flash_fwd_sm100_kernel (tcgen05/TMEM, TMA)' if dtype == 'bf16' else 'flash_f32_kernel (IEEE FMA)'}")
+        elif isinstance(spec, MapSpec):
+            n = _prod([d.stop - d.start for d in region.params[spec.x].type.dims])
+            self.grid = -(-n // 256)
+            self.source = f"pdb_pointwise_f32 steps={[e[0] for e in spec.steps]}"
         elif isinstance(spec, ContractSpec):
             def ext(i, names):
                 return _prod([next(d.stop - d.start for d in region.params[i].type.dims if d.name == n)
@@ -163,6 +190,8 @@ class _Runner:
         spec = self.spec
         if isinstance(spec, ContractSpec):
             return _run_contract(spec, tensors, self.dtype)
+        if isinstance(spec, MapSpec):
+            return _run_map(spec, tensors)
         if isinstance(spec, RowSpec):
             x = tensors[spec.x]
             perm = [spec.x_dims.index(n) for n in spec.x_dims if n != spec.dim] + [spec.x_dims.index(spec.dim)]
@@ -251,6 +280,8 @@ def compile_tile(region, launch: tuple = (), prune: tuple = (), *, dtype: str = 
     if dtype not in ("f32", "bf16"):
         raise ValueError("dtype must be 'f32' or 'bf16'")
     spec = recognize(region)
+    if isinstance(spec, MapSpec) and dtype != "f32":
+        raise Untranslatable("the map-chain kernel is f32")
     if isinstance(spec, RowSpec) and dtype != "f32":
         raise Untranslatable("row-reduction kernels are f32")
     if isinstance(spec, ContractSpec) and dtype == "bf16":

@@ -121,3 +121,27 @@ def test_batched_bf16_contract_kernel(cuda):
                                                            ("tanh", None, False)])
     want = torch.tanh(0.5 * torch.einsum("bmk,bnk->bmn", a.double(), b.double()) + bias.double())
     assert (c.double().cpu() - want).abs().max() <= 2 ** -7
+
+
+def test_map_chain(cuda, dsl):
+    """A pure pointwise chain (the map-chain row): y = tanh(x * 0.5 + b) - c, broadcast params."""
+    from pdum.dsl.ir import Builder, Region
+    from pdum.dsl.types import f64
+    from pdum.tl.fusion import plan_region
+
+    from pdum_dsl_b200.tile import compile_tile
+
+    rng = np.random.default_rng(5)
+    X, bvec, cmat = rng.standard_normal((37, 50)), rng.standard_normal(50), rng.standard_normal((37, 50))
+    b = Builder(_ops())
+    px, pb, pc = b.param(0, _ptype(X, ("r", "c"))), b.param(1, _ptype(bvec, ("c",))), b.param(2, _ptype(cmat, ("r", "c")))
+    y = b.emit("tl.pointwise", px, b.emit("core.const", type=f64, value=0.5), f="mul")
+    y = b.emit("tl.pointwise", y, b.emit("tl.repeat_like", pb, y), f="add")
+    y = b.emit("tl.pointwise", y, f="tanh")
+    y = b.emit("tl.pointwise", y, pc, f="sub")
+    region = Region(params=(px, pb, pc), body=(b.emit("core.yield", y),))
+    (g,) = plan_region(region).groups
+    assert g.template == "map-chain"
+    run = compile_tile(g.kernel)
+    assert "pointwise" in run.source
+    assert_f32(run([X, bvec, cmat]), np.tanh(X * 0.5 + bvec) - cmat)

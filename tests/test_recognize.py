@@ -62,7 +62,7 @@ def test_refusals_name_the_reason(dsl):
     b = Builder({**CORE_OPS, **TL_OPS})
     x = Tensor.from_numpy(np.zeros((4, 5)), ("m", "k"))
     px = b.param(0, tensor_type_of_layout(x.layout))
-    y = b.emit("tl.pointwise", px, f="exp")
+    y = b.emit("tl.pointwise", px, f="sin")  # no lowered template has sin
     region = Region(params=(px,), body=(b.emit("core.yield", y),))
     with pytest.raises(Untranslatable, match="no sm_100a template"):
         recognize(region)
@@ -156,3 +156,19 @@ def test_contraction_epilogue_naive_and_tile(dsl):
     (g,) = plan_region(r).groups
     assert g.template == "contraction-epilogue"
     assert recognize(g.kernel) == s  # the generated fold reads the same
+
+
+def test_map_chain_spec(dsl):
+    from pdum.dsl.ir import Builder, Region
+    from pdum.dsl.ops import CORE_OPS
+    from pdum.dsl.types import f64
+    from pdum.tl.dialect import TL_OPS, tensor_type_of_layout
+    from pdum.tl.tensor import Tensor
+
+    from pdum_dsl_b200.recognize import MapSpec
+
+    b = Builder({**CORE_OPS, **TL_OPS})
+    px = b.param(0, tensor_type_of_layout(Tensor.from_numpy(np.zeros((3, 4)), ("r", "c")).layout))
+    y = b.emit("tl.pointwise", b.emit("tl.pointwise", px, f="exp"), b.emit("core.const", type=f64, value=2.0), f="mul")
+    s = recognize(Region(params=(px,), body=(b.emit("core.yield", y),)))
+    assert isinstance(s, MapSpec) and [e[0] for e in s.steps] == ["exp", "mul"]
