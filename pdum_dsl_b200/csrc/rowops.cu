@@ -17,8 +17,11 @@
 namespace pdb {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kMaxVec = 8;  // float4 per thread: 8192 columns resident
+#ifndef PDB_ROW_THREADS
+#define PDB_ROW_THREADS 256
+#endif
+constexpr int kThreads = PDB_ROW_THREADS;
+constexpr int kMaxVec = 8 * 256 / kThreads;  // float4 per thread: 8192 columns resident
 
 template <typename Op>
 __device__ __forceinline__ float block_reduce(float v, float* red, Op op, float ident) {
@@ -198,12 +201,13 @@ extern "C" int pdb_rowsoftmax_f32(const pdb_rowsoftmax_desc* d, void* stream) {
   const bool vec = (d->cols & 3) == 0 && vec_ok(d->x, d->x_row_stride) && vec_ok(d->y, d->y_row_stride);
   const int64_t v4 = (d->cols / 4 + kThreads - 1) / kThreads;
   if (vec && v4 <= kMaxVec) {
-    switch (v4) {
-      case 1: softmax_vec_kernel<1><<<grid, block, 0, s>>>(d->x, d->y, d->cols, d->x_row_stride, d->y_row_stride); break;
-      case 2: softmax_vec_kernel<2><<<grid, block, 0, s>>>(d->x, d->y, d->cols, d->x_row_stride, d->y_row_stride); break;
-      case 3: case 4: softmax_vec_kernel<4><<<grid, block, 0, s>>>(d->x, d->y, d->cols, d->x_row_stride, d->y_row_stride); break;
-      default: softmax_vec_kernel<8><<<grid, block, 0, s>>>(d->x, d->y, d->cols, d->x_row_stride, d->y_row_stride); break;
-    }
+#define PDB_SM(V) softmax_vec_kernel<V><<<grid, block, 0, s>>>(d->x, d->y, d->cols, d->x_row_stride, d->y_row_stride)
+    if (v4 <= 1) PDB_SM(1);
+    else if (v4 <= 2) PDB_SM(2);
+    else if (v4 <= 4) PDB_SM(4);
+    else if (v4 <= 8) PDB_SM(8);
+    else PDB_SM(16);
+#undef PDB_SM
   } else {
     softmax_loop_kernel<<<grid, block, 0, s>>>(d->x, d->y, d->cols, d->x_row_stride, d->y_row_stride);
   }
@@ -225,12 +229,11 @@ extern "C" int pdb_layernorm_f32(const pdb_layernorm_desc* d, void* stream) {
   layernorm_vec_kernel<V><<<grid, block, 0, s>>>(d->x, d->gamma, d->beta, d->y, d->cols, d->x_row_stride, \
                                                  d->y_row_stride, eps)
   if (vec && v4 <= kMaxVec) {
-    switch (v4) {
-      case 1: PDB_LN(1); break;
-      case 2: PDB_LN(2); break;
-      case 3: case 4: PDB_LN(4); break;
-      default: PDB_LN(8); break;
-    }
+    if (v4 <= 1) PDB_LN(1);
+    else if (v4 <= 2) PDB_LN(2);
+    else if (v4 <= 4) PDB_LN(4);
+    else if (v4 <= 8) PDB_LN(8);
+    else PDB_LN(16);
   } else {
     layernorm_loop_kernel<<<grid, block, 0, s>>>(d->x, d->gamma, d->beta, d->y, d->cols, d->x_row_stride,
                                                  d->y_row_stride, eps);
