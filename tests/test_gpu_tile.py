@@ -186,3 +186,16 @@ def test_the_first_measurement_greens_the_group(cuda, dsl):
         again = sm100_ms(g.kernel, machine=machine)
     assert again.key == fact.key
     assert replace(g, confidence="green").confidence == "green"
+
+
+def test_the_tile_flagships_run(cuda, dsl):
+    """The reference's hand-written tile flagships (zoo/tiles.py) through compile_tile,
+    against their numpy oracles (conformance/test_triton_tile.py:27-35)."""
+    from pdum.tl.zoo.tiles import flash_tile, gemm_tile
+
+    from pdum_dsl_b200.tile import compile_tile
+
+    for f in (flash_tile(), gemm_tile()):
+        run = compile_tile(f.region)
+        got = run([v.to_numpy() for v in f.inputs.values()])
+        assert_f32(got, f.oracle(f.numpy_inputs()))
