@@ -184,12 +184,16 @@ __global__ void __launch_bounds__(GTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
   volatile int* abort = &bar->abort;
-  // tile t -> (batch, m-tile, n-tile), n fastest: consecutive CTAs share the A row-block in L2
+  // tile t -> (batch, m-tile, n-tile) in groups of 8 m-tile rows, m fastest inside a group, so
+  // the tiles in flight at once touch ~8 A row-blocks and ~20 B column-blocks (fits in L2)
   auto coords = [&](int t, int& bi, int& m0, int& n0) {
     bi = t / (tm * tn);
     const int r = t % (tm * tn);
-    m0 = (r / tn) * GM;
-    n0 = (r % tn) * GN;
+    const int gsz = 8 * tn;  // tiles per group of 8 m-tile rows
+    const int grp = r / gsz, in = r % gsz;
+    const int rows = (tm - grp * 8) < 8 ? (tm - grp * 8) : 8;
+    m0 = (grp * 8 + in % rows) * GM;
+    n0 = (in / rows) * GN;
   };
 
   if (warp == 0 && lane == 0) {
