@@ -16,6 +16,7 @@
 //                             next tile's K loop), stored as bf16;
 //   * pointwise_f32_kernel -- the map-chain template over a strided tensor.
 #include <cfloat>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "tma.h"
@@ -76,6 +77,51 @@ __device__ __forceinline__ float ew_apply(const EwProgram& pg, float v, int64_t 
   }
   return v;
 }
+
+// The epilogue program over 32 consecutive columns of one output row, step by
+// step: a tensor operand's 32 values are loaded together (independent loads,
+// one memory latency per step instead of one per element), then the step's
+// op runs over the row.  Same arithmetic as ew_apply, element for element.
+#define PDB_EW_ROW(EXPR)                       \
+  _Pragma("unroll") for (int c = 0; c < 32; ++c) { \
+    const float x = sw ? w[c] : v[c];          \
+    const float y = sw ? v[c] : w[c];          \
+    (void)x; (void)y;                          \
+    v[c] = (EXPR);                             \
+  }
+__device__ __forceinline__ void ew_apply_row32(const EwProgram& pg, float (&v)[32], int64_t b, int64_t i, int64_t j0,
+                                               int nvalid) {
+  for (int s = 0; s < pg.n; ++s) {
+    const EwOp& o = pg.ops[s];
+    float w[32];
+    if (o.operand == 2) {
+      const float* base = o.ptr + b * o.stride[0] + i * o.stride[1] + j0 * o.stride[2];
+      const int64_t js = o.stride[2];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) w[c] = c < nvalid ? __ldg(base + c * js) : 0.f;
+    } else {
+      const float cv = o.operand == 1 ? o.value : 0.f;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) w[c] = cv;
+    }
+    const bool sw = o.swap != 0;
+    switch (o.op) {
+      case PDB_EW_ADD: PDB_EW_ROW(x + y) break;
+      case PDB_EW_SUB: PDB_EW_ROW(x - y) break;
+      case PDB_EW_MUL: PDB_EW_ROW(x * y) break;
+      case PDB_EW_DIV: PDB_EW_ROW(x / y) break;
+      case PDB_EW_MAX: PDB_EW_ROW(fmaxf(x, y)) break;
+      case PDB_EW_MIN: PDB_EW_ROW(fminf(x, y)) break;
+      case PDB_EW_EXP: PDB_EW_ROW(expf(v[c])) break;
+      case PDB_EW_LOG: PDB_EW_ROW(logf(v[c])) break;
+      case PDB_EW_SQRT: PDB_EW_ROW(sqrtf(v[c])) break;
+      case PDB_EW_TANH: PDB_EW_ROW(tanhf(v[c])) break;
+      case PDB_EW_NEG: PDB_EW_ROW(-v[c]) break;
+      default: break;
+    }
+  }
+}
+#undef PDB_EW_ROW
 
 struct ContractParams {
   const void* a;
@@ -254,13 +300,13 @@ __global__ void __launch_bounds__(GTHREADS, 1)
         tmem_wait_ld();
         const int64_t c0 = n0 + ch * 32;
         if (gm >= p.m || c0 >= p.n) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+        ew_apply_row32(p.pg, v, bi, gm, c0, (int)(p.n - c0 < 32 ? p.n - c0 : 32));
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float v0 = ew_apply(p.pg, __uint_as_float(r[2 * i]) * p.alpha, bi, gm, c0 + 2 * i);
-          const float v1 = ew_apply(p.pg, __uint_as_float(r[2 * i + 1]) * p.alpha, bi, gm, c0 + 2 * i + 1);
-          pk[i] = pack_bf16(v0, v1);
-        }
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
         if (vec && c0 + 32 <= p.n) {
           uint4* dst = reinterpret_cast<uint4*>(C + c0);
 #pragma unroll
@@ -278,6 +324,163 @@ __global__ void __launch_bounds__(GTHREADS, 1)
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------ bf16 path, CTA pair
+// Same schedule on a cluster of two CTAs (one per SM) and 256 x 256 output
+// tiles: each CTA stages 128 rows of A and 128 rows of B per k-block, the
+// pair's rank-0 thread issues cta_group::2 M256 N256 K16 MMAs that read both
+// CTAs' shared memory and write 128 accumulator rows into each CTA's TMEM.
+// Per SM that halves the B bytes fetched per MMA cycle (64 instead of 96 B per
+// cycle at the full tensor rate).  Barriers: full[] of rank 0 counts both
+// CTAs' TMA bytes; empty[] and acc_full[] of each CTA receive the pair
+// commits; acc_empty[] of rank 0 counts the 8 epilogue warps of the pair.
+constexpr int PM = 256, PN = 256, PSTAGES = 6;
+constexpr int kPairStage = 128 * GK * 2;  // A or B half tile per CTA per k-block
+
+struct __align__(8) PairBars {
+  uint64_t full[PSTAGES], empty[PSTAGES];
+  uint64_t acc_full[2], acc_empty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GTHREADS, 1)
+    contract_bf16_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                              const ContractParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + PSTAGES * kPairStage;
+  PairBars* bar = reinterpret_cast<PairBars*>(sB + PSTAGES * kPairStage);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int nk = (int)((p.k + GK - 1) / GK);
+  const int tm = (int)((p.m + PM - 1) / PM), tn = (int)((p.n + PN - 1) / PN);
+  const int num_tiles = (int)p.batch * tm * tn;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PSTAGES; ++i) {
+      mbar_init(&bar->full[i], 1);
+      mbar_init(&bar->empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->acc_full[i], 1);
+      mbar_init(&bar->acc_empty[i], 8);  // one arrival per epilogue warp of the pair
+    }
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(&bar->tmem_base, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+  auto coords = [&](int t, int& bi, int& m0, int& n0) {
+    bi = t / (tm * tn);
+    const int r = t % (tm * tn);
+    const int gsz = 4 * tn;  // groups of 4 m-tile rows (1024 rows of A)
+    const int grp = r / gsz, in = r % gsz;
+    const int rows = (tm - grp * 4) < 4 ? (tm - grp * 4) : 4;
+    m0 = (grp * 4 + in % rows) * PM;
+    n0 = (in / rows) * PN;
+  };
+
+  if (warp == 0 && lane == 0) {
+    uint32_t g = 0;
+    bool ok = true;
+    for (int t = pair; ok && t < num_tiles; t += npairs) {
+      int bi, m0, n0;
+      coords(t, bi, m0, n0);
+      for (int kb = 0; kb < nk; ++kb, ++g) {
+        const int st = g % PSTAGES;
+        if (!(ok = mbar_wait_cluster(&bar->empty[st], ((g / PSTAGES) & 1) ^ 1, abort, p.err))) break;
+        if (rank == 0) mbar_expect_tx(&bar->full[st], 4 * kPairStage);
+        const uint32_t full0 = mapa_shared(smem_u32(&bar->full[st]), 0);
+        tma_load_4d_pair(sA + st * kPairStage, &tm_a, full0, kb * GK, m0 + (int)rank * 128, bi, 0);
+        tma_load_4d_pair(sB + st * kPairStage, &tm_b, full0, kb * GK, n0 + (int)rank * 128, bi, 0);
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    constexpr uint32_t idesc = idesc_bf16(PM, PN, 0, 0);
+    uint32_t g = 0, tt = 0;
+    bool ok = true;
+    for (int t = pair; ok && t < num_tiles; t += npairs, ++tt) {
+      const int buf = tt & 1;
+      if (!(ok = mbar_wait_cluster(&bar->acc_empty[buf], ((tt >> 1) & 1) ^ 1, abort, p.err))) break;
+      tc_fence_after();
+      const uint32_t acc = tmem + buf * PN;
+      for (int kb = 0; kb < nk; ++kb, ++g) {
+        const int st = g % PSTAGES;
+        if (!(ok = mbar_wait_cluster(&bar->full[st], (g / PSTAGES) & 1, abort, p.err))) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + st * kPairStage), b0 = smem_u32(sB + st * kPairStage);
+#pragma unroll
+        for (int kk = 0; kk < GK / 16; ++kk)
+          mma_ss_pair(acc, sdesc_sw128(a0 + kk * 32, 16, 1024), sdesc_sw128(b0 + kk * 32, 16, 1024), idesc,
+                      (kb > 0 || kk > 0) ? 1u : 0u);
+        const uint32_t e = smem_u32(&bar->empty[st]);
+        tc_commit_pair(e);
+        tc_commit_pair(mapa_shared(e, 1));
+      }
+      if (ok) {
+        const uint32_t f = smem_u32(&bar->acc_full[buf]);
+        tc_commit_pair(f);
+        tc_commit_pair(mapa_shared(f, 1));
+      }
+    }
+  } else if (warp >= 4) {
+    const int q4 = warp & 3;
+    const int row = (int)rank * 128 + q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const bool vec = p.cs[2] == 1 && (p.cs[1] & 7) == 0 && (p.cs[0] & 7) == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.c) & 15) == 0;
+    uint32_t tt = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++tt) {
+      int bi, m0, n0;
+      coords(t, bi, m0, n0);
+      const int buf = tt & 1;
+      if (!mbar_wait_cluster(&bar->acc_full[buf], (tt >> 1) & 1, abort, p.err)) break;
+      tc_fence_after();
+      const int64_t gm = m0 + row;
+      __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.c) + (int64_t)bi * p.cs[0] + gm * p.cs[1];
+#pragma unroll 1
+      for (int ch = 0; ch < PN / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + buf * PN + ch * 32, r);
+        tmem_wait_ld();
+        const int64_t c0 = n0 + ch * 32;
+        if (gm >= p.m || c0 >= p.n) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+        ew_apply_row32(p.pg, v, bi, gm, c0, (int)(p.n - c0 < 32 ? p.n - c0 : 32));
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+        if (vec && c0 + 32 <= p.n) {
+          uint4* dst = reinterpret_cast<uint4*>(C + c0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        } else {
+          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(pk);
+          for (int i = 0; i < 32 && c0 + i < p.n; ++i) C[(c0 + i) * p.cs[2]] = h[i];
+        }
+      }
+      warp_arrive_cluster_after_tc(mapa_shared(smem_u32(&bar->acc_empty[buf]), 0));
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -348,12 +551,16 @@ extern "C" int pdb_contract(const pdb_contract_desc* d, void* stream) {
   if (d->dtype != PDB_BF16) return set_error(PDB_ERR_UNSUPPORTED, "contract: unknown dtype %d", d->dtype);
   if (d->a_stride[2] != 1 || d->b_stride[2] != 1)
     return set_error(PDB_ERR_ALIGN, "contract bf16: the contracted dim must be contiguous in a and b");
+  // 256 x 256 tiles on CTA pairs when both output dims fill one; PDB_CONTRACT_PAIR=0 forces single CTAs
+  const char* pair_env = getenv("PDB_CONTRACT_PAIR");
+  const bool pair = d->m >= PM && d->n >= PN && !(pair_env && pair_env[0] == '0');
+  const uint32_t rows_a = pair ? 128 : GM, rows_b = pair ? 128 : GN;
   CUtensorMap ta, tb;
   {
     const uint64_t dims[4] = {(uint64_t)d->k, (uint64_t)d->m, (uint64_t)d->batch, 1};
     const uint64_t str[3] = {(uint64_t)d->a_stride[1] * 2, (uint64_t)(d->batch > 1 ? d->a_stride[0] : d->m * d->a_stride[1]) * 2,
                              (uint64_t)(d->batch * (d->batch > 1 ? d->a_stride[0] : d->m * d->a_stride[1])) * 2};
-    const uint32_t box[4] = {GK, GM, 1, 1};
+    const uint32_t box[4] = {GK, rows_a, 1, 1};
     if (int st = encode_tma_4d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return st;
   }
@@ -361,17 +568,41 @@ extern "C" int pdb_contract(const pdb_contract_desc* d, void* stream) {
     const uint64_t dims[4] = {(uint64_t)d->k, (uint64_t)d->n, (uint64_t)d->batch, 1};
     const uint64_t str[3] = {(uint64_t)d->b_stride[1] * 2, (uint64_t)(d->batch > 1 ? d->b_stride[0] : d->n * d->b_stride[1]) * 2,
                              (uint64_t)(d->batch * (d->batch > 1 ? d->b_stride[0] : d->n * d->b_stride[1])) * 2};
-    const uint32_t box[4] = {GK, GN, 1, 1};
+    const uint32_t box[4] = {GK, rows_b, 1, 1};
     if (int st = encode_tma_4d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return st;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (pair) {
+    const int smem = PSTAGES * 2 * kPairStage + 256 + 1024;
+    cudaError_t e = cudaFuncSetAttribute(contract_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_status(e, "contract bf16 pair: smem attribute");
+    const int64_t tiles = d->batch * ((d->m + PM - 1) / PM) * ((d->n + PN - 1) / PN);
+    if (tiles > 0x7fffffffLL) return set_error(PDB_ERR_SHAPE, "contract bf16: too many tiles");
+    static int max_pairs[64] = {};
+    if (dev < 64 && max_pairs[dev] == 0) {
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(2 * (unsigned)(sm_count(dev) / 2));
+      cfg.blockDim = dim3(GTHREADS);
+      cfg.dynamicSmemBytes = smem;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, contract_bf16_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = sm_count(dev) / 2;
+      }
+      max_pairs[dev] = n;
+    }
+    const int cap = dev < 64 ? max_pairs[dev] : sm_count(dev) / 2;
+    const int64_t pairs = tiles < cap ? tiles : cap;
+    contract_bf16_pair_kernel<<<(unsigned)(2 * pairs), GTHREADS, smem, s>>>(ta, tb, p);
+    return cuda_status(cudaGetLastError(), "contract bf16 pair launch");
   }
   const int smem = GSTAGES * (kStageA + kStageB) + 256 + 1024;
   cudaError_t e = cudaFuncSetAttribute(contract_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_status(e, "contract bf16: smem attribute");
   const int64_t tiles = d->batch * ((d->m + GM - 1) / GM) * ((d->n + GN - 1) / GN);
   if (tiles > 0x7fffffffLL) return set_error(PDB_ERR_SHAPE, "contract bf16: too many tiles");
-  int dev = 0;
-  cudaGetDevice(&dev);
   const int64_t grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
   contract_bf16_kernel<<<(unsigned)grid, GTHREADS, smem, s>>>(ta, tb, p);
   return cuda_status(cudaGetLastError(), "contract bf16 launch");

@@ -123,6 +123,32 @@ def test_batched_bf16_contract_kernel(cuda):
     assert (c.double().cpu() - want).abs().max() <= 2 ** -7
 
 
+@pytest.mark.parametrize("shape", [(2, 600, 520, 200), (1, 1024, 768, 512), (1, 256, 256, 64)])
+def test_pair_bf16_contract_kernel(cuda, monkeypatch, shape):
+    """256 x 256 tiles on CTA pairs (cta_group::2): ragged M / N / K, a batch, the
+    single-tile case; the single-CTA kernel on the same inputs must agree bit for bit
+    (same k-order of the fp32 accumulation)."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    bsz, m, n, k = shape
+    g = torch.Generator(device="cpu").manual_seed(11)
+    a = torch.randn(bsz, m, k, generator=g).to(torch.bfloat16).to(cuda)
+    b = torch.randn(bsz, n, k, generator=g).to(torch.bfloat16).to(cuda)
+    bias = torch.randn(bsz, 1, n, generator=g).to(cuda)
+    ep = [("add", bias, False), ("maximum", 0.0, False)]
+    monkeypatch.setenv("PDB_CONTRACT_PAIR", "1")
+    c_pair = kernels.contract(a, b, epilogue=ep)
+    monkeypatch.setenv("PDB_CONTRACT_PAIR", "0")
+    c_one = kernels.contract(a, b, epilogue=ep)
+    kernels.check_device_errors()
+    want = torch.relu(torch.einsum("bmk,bnk->bmn", a.double(), b.double()) + bias.double()).cpu()
+    err = (c_pair.double().cpu() - want).abs().max().item()
+    assert err <= 2 ** -7 * max(1.0, want.abs().max().item())
+    assert torch.equal(c_pair, c_one)
+
+
 def test_map_chain(cuda, dsl):
     """A pure pointwise chain (the map-chain row): y = tanh(x * 0.5 + b) - c, broadcast params."""
     from pdum.dsl.ir import Builder, Region
