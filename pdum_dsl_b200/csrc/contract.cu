@@ -335,8 +335,9 @@ __global__ void __launch_bounds__(GTHREADS, 1)
 // Per SM that halves the B bytes fetched per MMA cycle (64 instead of 96 B per
 // cycle at the full tensor rate).  Barriers: full[] of rank 0 counts both
 // CTAs' TMA bytes; empty[] and acc_full[] of each CTA receive the pair
-// commits; acc_empty[] of rank 0 counts the 8 epilogue warps of the pair.
-constexpr int PM = 256, PN = 256, PSTAGES = 6;
+// commits; acc_empty[] of rank 0 counts the 16 epilogue warps of the pair
+// (warps 4..11 of each CTA: TMEM lane quarter warp % 4, column half (warp - 4) / 4).
+constexpr int PM = 256, PN = 256, PSTAGES = 6, PTHREADS = 384;
 constexpr int kPairStage = 128 * GK * 2;  // A or B half tile per CTA per k-block
 
 struct __align__(8) PairBars {
@@ -346,7 +347,7 @@ struct __align__(8) PairBars {
   int abort;
 };
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GTHREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PTHREADS, 1)
     contract_bf16_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                               const ContractParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -368,7 +369,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GTHREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar->acc_full[i], 1);
-      mbar_init(&bar->acc_empty[i], 8);  // one arrival per epilogue warp of the pair
+      mbar_init(&bar->acc_empty[i], 16);  // one arrival per epilogue warp of the pair
     }
     bar->abort = 0;
     fence_barrier_init();
@@ -436,7 +437,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GTHREADS, 1)
       }
     }
   } else if (warp >= 4) {
-    const int q4 = warp & 3;
+    const int q4 = warp & 3, half = (warp - 4) >> 2;  // TMEM lane quarter, column half
     const int row = (int)rank * 128 + q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const bool vec = p.cs[2] == 1 && (p.cs[1] & 7) == 0 && (p.cs[0] & 7) == 0 &&
@@ -451,7 +452,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GTHREADS, 1)
       const int64_t gm = m0 + row;
       __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.c) + (int64_t)bi * p.cs[0] + gm * p.cs[1];
 #pragma unroll 1
-      for (int ch = 0; ch < PN / 32; ++ch) {
+      for (int ch = half * (PN / 64); ch < (half + 1) * (PN / 64); ++ch) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_off + buf * PN + ch * 32, r);
         tmem_wait_ld();
@@ -584,7 +585,7 @@ extern "C" int pdb_contract(const pdb_contract_desc* d, void* stream) {
     if (dev < 64 && max_pairs[dev] == 0) {
       cudaLaunchConfig_t cfg{};
       cfg.gridDim = dim3(2 * (unsigned)(sm_count(dev) / 2));
-      cfg.blockDim = dim3(GTHREADS);
+      cfg.blockDim = dim3(PTHREADS);
       cfg.dynamicSmemBytes = smem;
       int n = 0;
       if (cudaOccupancyMaxActiveClusters(&n, contract_bf16_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
@@ -595,7 +596,7 @@ extern "C" int pdb_contract(const pdb_contract_desc* d, void* stream) {
     }
     const int cap = dev < 64 ? max_pairs[dev] : sm_count(dev) / 2;
     const int64_t pairs = tiles < cap ? tiles : cap;
-    contract_bf16_pair_kernel<<<(unsigned)(2 * pairs), GTHREADS, smem, s>>>(ta, tb, p);
+    contract_bf16_pair_kernel<<<(unsigned)(2 * pairs), PTHREADS, smem, s>>>(ta, tb, p);
     return cuda_status(cudaGetLastError(), "contract bf16 pair launch");
   }
   const int smem = GSTAGES * (kStageA + kStageB) + 256 + 1024;
