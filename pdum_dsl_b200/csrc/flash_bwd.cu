@@ -7,12 +7,12 @@
 // carves that re-derive P inside their sweep (partition.py:354-455).  This
 // file executes that plan as three kernels:
 //
-//   bwd_prep     D[t] = sum_o dO[t,o] O[t,o] and lse2[t] = lse[t] * log2 e
-//                (rows padded to a multiple of 128 with lse2 = +inf, D = 0,
+//   bwd_prep     D[t] = sum_o dO[t,o] O[t,o] and nlse2[t] = -lse[t] * log2 e
+//                (rows padded to a multiple of 128 with nlse2 = -inf, D = 0,
 //                so padded query rows carry P = 0 without masks)
 //   bwd_dkdv     one CTA per (batch, KV head, 128-key block): for every query
 //                tile of every query head of the group it forms
-//                S^T = K Q^T and dP^T = V dO^T in TMEM, P^T = exp2(S^T c - lse2),
+//                S^T = K Q^T and dP^T = V dO^T in TMEM, P^T = exp2(S^T c + nlse2),
 //                dS^T = P^T (dP^T - D) (one thread per key row), writes both
 //                back to TMEM as bf16 and accumulates dV += P^T dO,
 //                dK += dS^T Q in TMEM; GQA sums over the group in place.
@@ -38,7 +38,7 @@ constexpr int kThreads = 384;  // warp0 TMA, warp1 MMA, warp2 TMEM, warps 4..11 
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdParams {
-  const float* lse2;  // [B*H*Tpad]
+  const float* nlse2;  // -lse * log2 e, [B*H*Tpad]
   const float* dsum;  // [B*H*Tpad]
   void* out0;         // dkdv: dk ; dq: dq
   void* out1;         // dkdv: dv
@@ -100,8 +100,8 @@ __device__ __forceinline__ void store_cols_bf16(uint32_t t_src, float mul, __nv_
   }
 }
 
-// P, dS for 64 score columns held by one thread: p = exp2(s c - l2), ds = p (dp - dsum).
-// `valid(col)` masks causal positions; l2 / dsum per column (dK/dV) or per row (dQ).
+// P, dS for 64 score columns held by one thread: p = exp2(s c + nl2), ds = p (dp - dsum).
+// `valid(col)` masks causal positions; nl2 / dsum per column (dK/dV) or per row (dQ).
 template <class ColL2, class ColDs, class Valid>
 __device__ __forceinline__ void p_ds_64(const uint32_t (&sr)[64], const uint32_t (&dr)[64], float c, ColL2 l2,
                                         ColDs ds_of, Valid valid, uint32_t (&pp)[32], uint32_t (&dd)[32]) {
@@ -111,7 +111,7 @@ __device__ __forceinline__ void p_ds_64(const uint32_t (&sr)[64], const uint32_t
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int col = 2 * i + u;
-      float pr = ex2(fmaf(__uint_as_float(sr[col]), c, -l2(col)));
+      float pr = ex2(fmaf(__uint_as_float(sr[col]), c, l2(col)));
       pr = valid(col) ? pr : 0.f;
       pv[u] = pr;
       dv[u] = pr * (__uint_as_float(dr[col]) - ds_of(col));
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + kKV;
   uint8_t* sQ = smem + 2 * kKV;                 // kStages
   uint8_t* sDO = sQ + kStages * kQ;             // kStages
-  float* sVec = reinterpret_cast<float*>(sDO + kStages * kQ);  // kStages x (lse2[64], dsum[64])
+  float* sVec = reinterpret_cast<float*>(sDO + kStages * kQ);  // kStages x (nlse2[64], dsum[64])
   BarsKV* bar = reinterpret_cast<BarsKV*>(reinterpret_cast<uint8_t*>(sVec) + kStages * 2 * QT * 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_4d(sDO + st * kQ + i * kBoxQ, &tm_do, &bar->q_full[st], i * 64, t0, h, b);
         }
         const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
-        bulk_load(sVec + st * 2 * QT, p.lse2 + vrow, QT * 4, &bar->q_full[st]);
+        bulk_load(sVec + st * 2 * QT, p.nlse2 + vrow, QT * 4, &bar->q_full[st]);
         bulk_load(sVec + st * 2 * QT + QT, p.dsum + vrow, QT * 4, &bar->q_full[st]);
       }
     } else if (warp == 1 && lane == 0) {
@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* lse2 = sVec + st * 2 * QT;
       const float* dsum = lse2 + QT;
       const int lo = p.causal ? s - p.q_start - t0 : -1;  // query columns below lo cannot see key s
-      // two halves of 32 query columns; per-column lse2 / D read as float4 from shared memory
+      // two halves of 32 query columns; per-column nlse2 / D read as float4 from shared memory
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         uint32_t sr[32], dr[32];
@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int col = hf * 32 + 4 * q + u;
-            float pr = ex2(fmaf(__uint_as_float(sr[4 * q + u]), c, -lv[u]));
+            float pr = ex2(fmaf(__uint_as_float(sr[4 * q + u]), c, lv[u]));
             pr = col >= lo ? pr : 0.f;
             pv[u] = pr;
             gv[u] = pr * (__uint_as_float(dr[4 * q + u]) - dv4[u]);
@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tb = tmem + lane_off + x * 128;
     const float c = p.scale_log2;
     const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t;
-    const float l2 = p.lse2[vrow];  // +inf on padded rows -> P = 0
+    const float l2 = p.nlse2[vrow];  // -inf on padded rows -> P = 0
     const float dsum = p.dsum[vrow];
     bool ok = true;
     for (int j = x; j < n_kv; j += 2) {
@@ -486,12 +486,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // (dV, dK, dQ: N = 64) are not, so the schedule overlaps them with the
 // next item's score math: P / dS of item i are copied to a TMEM staging area,
 // which frees the S / dP columns for item i+1's score MMAs; those are issued
+// as soon as every compute warp holds item i's S / dP in registers (s_free),
 // before the accumulations of item i, and the compute warpgroups work on item
 // i+1 while the tensor core accumulates item i.
 struct __align__(8) Bars64 {
   uint64_t fixed_full;                 // K/V (dK/dV kernel) or Q/dO (dQ kernel)
   uint64_t op_full[kStages], op_empty[kStages];  // streamed operand ring
-  uint64_t s_full, p_full, stage_free, o_full;
+  uint64_t s_full, s_free, p_full, stage_free, o_full;
   uint32_t tmem_base;
   int abort;
 };
@@ -513,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + kT;
   uint8_t* sQ = smem + 2 * kT;         // kStages
   uint8_t* sDO = sQ + kStages * kT;    // kStages
-  float* sVec = reinterpret_cast<float*>(sDO + kStages * kT);  // kStages x (lse2[128], dsum[128])
+  float* sVec = reinterpret_cast<float*>(sDO + kStages * kT);  // kStages x (nlse2[128], dsum[128])
   Bars64* bar = reinterpret_cast<Bars64*>(reinterpret_cast<uint8_t*>(sVec) + kStages * 2 * 128 * 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -538,6 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->op_empty[i], 1);
     }
     mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->s_free, 8);  // one arrival per compute warp: S / dP read into registers
     mbar_init(&bar->p_full, 8);  // one arrival per compute warp
     mbar_init(&bar->stage_free, 1);
     mbar_init(&bar->o_full, 1);
@@ -571,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(sQ + st * kT, &tm_q, &bar->op_full[st], 0, t0, h, b);
         tma_load_4d(sDO + st * kT, &tm_do, &bar->op_full[st], 0, t0, h, b);
         const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
-        bulk_load(sVec + st * 256, p.lse2 + vrow, 512, &bar->op_full[st]);
+        bulk_load(sVec + st * 256, p.nlse2 + vrow, 512, &bar->op_full[st]);
         bulk_load(sVec + st * 256 + 128, p.dsum + vrow, 512, &bar->op_full[st]);
       }
     } else if (warp == 1 && lane == 0) {
@@ -588,9 +590,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && n_items > 0) ok = issue_s(0);
       for (int it = 0; ok && it < n_items; ++it) {
         const int st = it % kStages;
+        // the next item's scores as soon as this item's S / dP sit in registers: they overlap the compute
+        if (!(ok = mbar_wait(&bar->s_free, it & 1, abort, p.err))) break;
+        tc_fence_after();
+        if (it + 1 < n_items && !(ok = issue_s(it + 1))) break;
         if (!(ok = mbar_wait(&bar->p_full, it & 1, abort, p.err))) break;
         tc_fence_after();
-        if (it + 1 < n_items && !(ok = issue_s(it + 1))) break;  // next scores first: the compute overlaps below
         mma_tmem_a<128>(tmem + 384, tmem + 256, smem_u32(sDO + st * kT), kBox, idG, it > 0);  // dV += P^T dO
         mma_tmem_a<128>(tmem + 448, tmem + 320, smem_u32(sQ + st * kT), kBox, idG, it > 0);   // dK += dS^T Q
         tc_commit(&bar->op_empty[st]);
@@ -614,20 +619,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = mbar_wait(&bar->op_full[st], (it / kStages) & 1, abort, p.err))) break;
       if (!(ok = mbar_wait(&bar->s_full, it & 1, abort, p.err))) break;
       tc_fence_after();
-      const float* lse2 = sVec + st * 256 + w * 64;
+      const float* nlse2 = sVec + st * 256 + w * 64;
       const float* dsum = sVec + st * 256 + 128 + w * 64;
       const int lo = p.causal ? s - p.q_start - t0 - w * 64 : -(1 << 30);  // columns below lo are masked
       uint32_t pp[32], dd[32];
       // packed f32x2 math; the causal select only on items that cross the diagonal
       const bool need_mask = __any_sync(0xffffffffu, lo > 0);
       const uint64_t c2 = f2_pack(c, c);
-      const uint32_t sl = smem_u32(lse2), sd = smem_u32(dsum);
+      const uint32_t sl = smem_u32(nlse2), sd = smem_u32(dsum);
+      uint32_t srr[64], drr[64];
+      tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(srr));
+      tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(srr + 32));
+      tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(drr));
+      tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(drr + 32));
+      tmem_wait_ld();
+      warp_arrive_after_tc(&bar->s_free);  // S^T / dP^T are in registers: the next item's scores may overwrite them
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {  // two halves of 32 columns keep the live registers low
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tl + w * 64 + hf * 32, sr);
-        tmem_ld32(tl + 128 + w * 64 + hf * 32, dr);
-        tmem_wait_ld();
+      for (int hf = 0; hf < 2; ++hf) {
+        const uint32_t* sr = srr + 32 * hf;
+        const uint32_t* dr = drr + 32 * hf;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float4 l4 = lds128(sl + 128 * hf + 16 * q);
@@ -640,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t l2 = h2 ? f2_pack(l4.z, l4.w) : f2_pack(l4.x, l4.y);
             const uint64_t dd2 = h2 ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y);
             float x0, x1;
-            f2_unpack(f2_sub(f2_mul(s2, c2), l2), x0, x1);
+            f2_unpack(f2_fma(s2, c2, l2), x0, x1);
             float p0 = ex2(x0), p1 = ex2(x1);
             if (need_mask) {
               p0 = col >= lo ? p0 : 0.f;
@@ -723,6 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->op_empty[i], 1);
     }
     mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->s_free, 8);  // one arrival per compute warp: S / dP read into registers
     mbar_init(&bar->p_full, 8);  // one arrival per compute warp
     mbar_init(&bar->stage_free, 1);
     mbar_init(&bar->o_full, 1);
@@ -768,9 +779,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && n_kv > 0) ok = issue_s(0);
       for (int j = 0; ok && j < n_kv; ++j) {
         const int st = j % kStages;
-        if (!(ok = mbar_wait(&bar->p_full, j & 1, abort, p.err))) break;
+        if (!(ok = mbar_wait(&bar->s_free, j & 1, abort, p.err))) break;
         tc_fence_after();
         if (j + 1 < n_kv && !(ok = issue_s(j + 1))) break;
+        if (!(ok = mbar_wait(&bar->p_full, j & 1, abort, p.err))) break;
+        tc_fence_after();
         mma_tmem_a<128>(tmem + 320, tmem + 256, smem_u32(sK + st * kT), kBox, idG, j > 0);  // dQ += dS K
         tc_commit(&bar->op_empty[st]);
         tc_commit(&bar->stage_free);
@@ -787,7 +800,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tl = tmem + lane_off;
     const float c = p.scale_log2;
     const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t;
-    const float l2 = p.lse2[vrow];  // +inf on padded rows -> P = 0
+    const float l2 = p.nlse2[vrow];  // -inf on padded rows -> P = 0
     const float dsum = p.dsum[vrow];
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -800,9 +813,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
       tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
       tmem_wait_ld();
+      warp_arrive_after_tc(&bar->s_free);
       uint32_t dd[32];
       const bool need_mask = __any_sync(0xffffffffu, lim < 64);
-      const uint64_t c2 = f2_pack(c, c), nl2 = f2_pack(-l2, -l2), ds2 = f2_pack(dsum, dsum);
+      const uint64_t c2 = f2_pack(c, c), nl2 = f2_pack(l2, l2), ds2 = f2_pack(dsum, dsum);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int col = 2 * i;
@@ -841,7 +855,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- prologue
-// D = sum(dO * O) and lse2 = lse * log2(e) per (b, h, padded row).  `tpr`
+// D = sum(dO * O) and nlse2 = -lse * log2(e) per (b, h, padded row).  `tpr`
 // threads share a row, each reading 16-byte chunks (8 bf16) of O and dO.
 __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                 const float* __restrict__ lse, float* __restrict__ lse2, float* __restrict__ dsum,
@@ -876,7 +890,7 @@ __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_
   for (int off = tpr / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (sub == 0) {
     dsum[r] = t < T ? acc : 0.f;
-    lse2[r] = t < T ? lse[bh * T + t] * kLog2e : INFINITY;
+    lse2[r] = t < T ? -lse[bh * T + t] * kLog2e : -INFINITY;
   }
 }
 
@@ -947,7 +961,7 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
   if (int st = map_bf16(&tk64, d.k, D, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, KT)) return st;
   if (int st = map_bf16(&tv64, d.v, D, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, KT)) return st;
   BwdParams p{};
-  p.lse2 = lse2;
+  p.nlse2 = lse2;
   p.dsum = dsum;
   p.T = (int)d.seqlen_q;
   p.S = (int)d.seqlen_k;
