@@ -39,6 +39,10 @@ sys.path.insert(0, str(REPO))
 
 B, H, S, D = 8, 32, 4096, 128
 FLOP_FULL = 4.0 * B * H * S * S * D / 2  # causal: half of 4*B*H*S^2*D
+# NVLink 5 peer copy measured on this pool (per direction) and a typical NCCL
+# launch-to-completion latency: the alpha-beta link model for the gather prediction
+NVLINK_BPS = 770e9
+NCCL_LATENCY_S = 10e-6
 
 
 def _peaks():
@@ -243,8 +247,14 @@ def run_ours(args):
         full = torch.empty((world * units, S, D), dtype=o.dtype, device=dev)
         g_ms, _ = _timed(lambda: dist.all_gather_into_tensor(full, o.reshape(units, S, D)), 5, 2, stream, world)
         nbytes = o.numel() * o.element_size()
-        gather = {"ms": g_ms / 5, "bytes_in_per_rank": nbytes * (world - 1),
-                  "GB/s_in_per_rank": nbytes * (world - 1) / (g_ms / 5 * 1e-3) / 1e9,
+        from pdum_dsl_b200.partition import alpha_beta_seconds, gather_bytes
+
+        moved = gather_bytes(nbytes * world, world)  # what placement.traffic charges the merge
+        gather = {"ms": g_ms / 5, "bytes_in_per_rank": moved,
+                  "GB/s_in_per_rank": moved / (g_ms / 5 * 1e-3) / 1e9,
+                  "predicted_ms": 1e3 * alpha_beta_seconds(moved, NVLINK_BPS, NCCL_LATENCY_S),
+                  "model": "placement.traffic all-gather ((p-1)/p x output bytes), alpha-beta at "
+                           f"{NVLINK_BPS / 1e9:.0f} GB/s per direction + {NCCL_LATENCY_S * 1e6:.0f} us",
                   "note": "all_gather_into_tensor of o shards over NCCL; outside `value`"}
         del full
     if args.kernel_only:

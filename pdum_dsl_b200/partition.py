@@ -16,6 +16,15 @@ inside the computation:
 
 Sequence is never split (the reference refuses split-K over the carried s dim,
 ``docs/design/340_grid-launch.md:162-171``).
+
+A partition can also be read off a placed region instead of the fixed rule:
+``placement_of`` finds the rider dim the region binds to a machine level (the
+global-view spelling ``(w, <rider>l)`` with ``w`` bound, ``zoo/megatron.py``),
+``sharded_attention(..., placement=...)`` gives each rank its index along that
+dim, and ``gather_bytes`` / ``alpha_beta_seconds`` restate what
+``placement.traffic`` and ``TrafficReport.time`` charge for the final merge
+(``tl/placement.py:91-101,170-181``), so the measured NCCL gather can be set
+beside the model's prediction.
 """
 
 from __future__ import annotations
@@ -57,6 +66,57 @@ def gather_bytes(out_bytes: int, world: int) -> int:
     return out_bytes * (world - 1) // world
 
 
+def alpha_beta_seconds(nbytes: int, bandwidth: float, latency: float = 0.0) -> float:
+    """The reference's alpha-beta estimate of one collective: latency + bytes over
+    the link bandwidth (``TrafficReport.time``, placement.py:91-101)."""
+    return latency + (nbytes / bandwidth if bandwidth else 0.0)
+
+
+@dataclass(frozen=True)
+class Placement:
+    dim: str    # the rider dim split over the mesh: "b", "h", or "g" (GQA KV groups)
+    level: str  # machine level the mesh dim is bound to
+    world: int  # extent of the bound mesh dim = number of devices
+    local: int  # extent of `dim` held by each device
+
+
+_NOT_RIDERS = ("t", "s", "e", "o", "r")
+
+
+def placement_of(region) -> Placement:
+    """The partition a placed attention region declares.
+
+    Exactly one dim may be bound to a machine level, the same one in every
+    param; it must be immediately followed by the per-device part of a rider
+    dim (``<rider>l``).  Binding a sequence / feature dim (or ``r``, which
+    would replicate K/V) is refused: that placement implies a cross-device
+    reduction or a split-K the reference does not model."""
+    bound = set()
+    locs = set()
+    for prm in region.params:
+        dims = prm.type.layout.dims
+        for i, d in enumerate(dims):
+            if d.level is None:
+                continue
+            if i + 1 >= len(dims):
+                raise ValueError(f"bound dim {d.name!r} has no per-device part after it")
+            nxt = dims[i + 1]
+            rider = nxt.name[:-1] if nxt.name.endswith("l") else None
+            if rider is None or rider in _NOT_RIDERS:
+                raise ValueError(f"bound dim {d.name!r} must split a batch / head rider, found {nxt.name!r}")
+            bound.add((d.name, d.level, d.size))
+            locs.add((rider, nxt.size))
+    if not bound:
+        raise ValueError("region binds no dim to a machine level")
+    if len(bound) != 1 or len(locs) != 1:
+        raise ValueError(f"expected one bound rider shared by every param, found {sorted(bound)} / {sorted(locs)}")
+    (_, level, world), = bound
+    (rider, local), = locs
+    if len(region.params) != sum(1 for p in region.params if any(d.level for d in p.type.layout.dims)):
+        raise ValueError("every param must carry the bound dim (K/V would otherwise be replicated)")
+    return Placement(rider, level, world, local)
+
+
 def local_slices(shard: Shard, batch: int, heads_kv: int):
     """Units -> list of (b, hk_lo, hk_hi) runs covered by this shard."""
     runs = []
@@ -69,15 +129,57 @@ def local_slices(shard: Shard, batch: int, heads_kv: int):
     return runs
 
 
-def sharded_attention(q, k, v, *, world: int, rank: int, attend, gather: bool = False, group=None):
+def _placed_attention(q, k, v, pl: Placement, *, world, rank, attend, gather, group):
+    import torch
+
+    if pl.world != world:
+        raise ValueError(f"placement is over {pl.world} devices, running on {world}")
+    B, Hq = q.shape[:2]
+    Hkv = k.shape[1]
+    r = Hq // Hkv
+    lo, hi = rank * pl.local, (rank + 1) * pl.local
+    if pl.dim == "b":
+        if B != world * pl.local:
+            raise ValueError(f"b={B} does not match placement {pl}")
+        qs, ks, vs = q[lo:hi], k[lo:hi], v[lo:hi]
+    elif pl.dim in ("h", "g"):
+        if Hkv != world * pl.local or (pl.dim == "h" and r != 1):
+            raise ValueError(f"heads {Hq}/{Hkv} do not match placement {pl}")
+        qs, ks, vs = q[:, lo * r:hi * r], k[:, lo:hi], v[:, lo:hi]
+    else:
+        raise ValueError(f"cannot place attention on {pl.dim!r}")
+    o = attend(qs, ks, vs)
+    if not gather:
+        return o
+    import torch.distributed as dist
+
+    T, Dv = o.shape[2], o.shape[3]
+    full = torch.empty((world, *o.shape), dtype=o.dtype, device=o.device)
+    dist.all_gather_into_tensor(full.reshape(-1, T, Dv), o.contiguous().reshape(-1, T, Dv), group=group)
+    if pl.dim == "b":
+        return full.reshape(B, Hq, T, Dv)
+    return full.permute(1, 0, 2, 3, 4).reshape(B, Hq, T, Dv)  # (w, b, hl, t, o) -> (b, h, t, o)
+
+
+def sharded_attention(q, k, v, *, world: int, rank: int, attend, gather: bool = False, group=None,
+                      placement: Placement | None = None):
     """Run ``attend(q_s, k_s, v_s)`` on this rank's units; optionally all-gather.
 
     q (B, Hq, T, D), k/v (B, Hkv, S, D) hold the FULL problem (or at least this
     rank's units).  The shard's units are flattened to one (1, units*r, T, D)
     job so a single kernel launch covers them.  Returns this rank's output
     shard, or with ``gather`` the full (B, Hq, T, Dv) output on every rank
-    (``torch.distributed.all_gather_into_tensor``; ``group`` as in torch)."""
+    (``torch.distributed.all_gather_into_tensor``; ``group`` as in torch).
+
+    With ``placement`` (from ``placement_of`` on a placed region) rank ``i``
+    takes index ``i`` of the bound mesh dim instead: its block of batches, of
+    heads of every batch, or of KV groups of every batch; the gathered output
+    is put back in (b, h, t, o) order."""
     import torch
+
+    if placement is not None:
+        return _placed_attention(q, k, v, placement, world=world, rank=rank, attend=attend, gather=gather,
+                                 group=group)
 
     B, Hq, T, D = q.shape
     Hkv = k.shape[1]

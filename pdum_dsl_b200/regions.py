@@ -101,6 +101,50 @@ def attention_region(B=None, H=None, T=6, S=None, D=3, DV=None, *, causal=True, 
     return Region(params=(pq, pk, pv), body=(b.emit("core.yield", out),))
 
 
+def placed_attention_region(B, H, T, D, *, world, bind="h", level="gpu", causal=True, scale=None,
+                            group=None, gather=True, S=None, DV=None):
+    """Attention with one rider dim split over a machine level, in the reference's
+    global-view placement spelling (``pdum/tl/zoo/megatron.py:1-14,45-50``): the
+    rider ``bind`` ("b", "h", or "g" for GQA KV groups) of extent X becomes
+    ``(w, <bind>l)`` with ``w`` (extent ``world``) bound to ``level`` and
+    ``<bind>l = X / world`` per device.  With ``gather`` the output merges
+    ``(w, <bind>l)`` back into ``<bind>`` -- the merge of a bound part that
+    ``placement.traffic`` prices as an all-gather (``tl/placement.py:170-181``).
+    The denotation is the unplaced region's (placement is metadata)."""
+    Builder, Region, OPS, f64, ttl, Tensor = _dsl()
+    S = T if S is None else S
+    DV = D if DV is None else DV
+    (qn, qs), (kn, ks), (vn, vs) = attention_shapes(B, H, T, S, D, DV, group)
+    if bind not in qn or bind not in kn or bind in ("t", "s", "e", "o", "r"):
+        raise ValueError(f"bind must name a rider dim shared by q and k/v (b, h or g), got {bind!r}")
+    loc = f"{bind}l"
+
+    def placed(names, shape):
+        i = names.index(bind)
+        if shape[i] % world:
+            raise ValueError(f"{bind}={shape[i]} is not a multiple of world={world}")
+        n2 = names[:i] + ("w", loc) + names[i + 1:]
+        s2 = shape[:i] + (world, shape[i] // world) + shape[i + 1:]
+        t = Tensor.from_numpy(np.zeros(s2), n2).bind(w=level)
+        return ttl(t.layout)
+
+    b = Builder(OPS)
+    pq = b.param(0, placed(qn, qs))
+    pk = b.param(1, placed(kn, ks))
+    pv = b.param(2, placed(vn, vs))
+    sc = _contract(b, pq, pk, "e")
+    if scale is not None:
+        sc = b.emit("tl.pointwise", sc, b.emit("core.const", type=f64, value=float(scale)), f="mul")
+    if causal:
+        mask = b.emit("tl.pointwise", b.emit("tl.iota", sc, name="s"), b.emit("tl.iota", sc, name="t"), f="le")
+        sc = b.emit("tl.pointwise", mask, sc, b.emit("core.const", type=f64, value=-1e9), f="where")
+    pr, _, _ = _softmax(b, sc, "s")
+    out = _contract(b, pr, pv, "s")
+    if gather:
+        out = b.emit("tl.merge", out, parts=("w", loc), name=bind)
+    return Region(params=(pq, pk, pv), body=(b.emit("core.yield", out),))
+
+
 def row_softmax_region(R, C):
     """softmax over the column dim ``c`` of X(r, c) (``zoo_common.py:79-82``)."""
     Builder, Region, OPS, *_ = _dsl()
