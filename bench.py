@@ -281,6 +281,12 @@ def run_ours(args):
     cpu_base = None
     if world == 1 and not args.no_extra:
         extra = secondary(args, dev, stream, peaks)
+    elif world > 1 and not args.no_extra:
+        del qh, kh, vh, oh
+        torch.cuda.empty_cache()
+        gq = _gqa_sharded(world, rank, dev, stream)
+        if gq is not None:
+            extra["gqa_fwd_sharded"] = gq
     if rank == 0 and world == 1 and not args.no_cpu:
         tf, dt, desc = cpu_attention_sample()
         cpu_base = {"value": tf, "unit": "TFLOP/s", "cores": _cpu_threads(), "kind": "port", "sample": desc,
@@ -384,6 +390,42 @@ def _gqa(out, kernels, dev, stream, g):
     fl = 4.0 * Bq * Hq * Sq * Sq * D / 2
     out["gqa_fwd"] = {"TFLOP/s": fl / (sum(per) / len(per) * 1e-3) / 1e12, "ms": sum(per) / len(per),
                       "config": "B4 Hq64 Hkv8 S8192 D128 causal (config 4)"}
+
+
+def _gqa_sharded(world, rank, dev, stream):
+    """Config 4 over `world` GPUs: the KV groups split by the placement rule
+    (b, w, gl) with w bound to the GPU level, each rank computing its block of
+    KV heads of every batch, then the NCCL all-gather of the output shards.
+    Strong scaling (the problem is fixed); device time, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from pdum_dsl_b200 import kernels
+    from pdum_dsl_b200.partition import Placement, alpha_beta_seconds, gather_bytes
+
+    Bq, Hq, Hk, Sq = 4, 64, 8, 8192
+    if Hk % world:
+        return None
+    pl = Placement("g", "gpu", world, Hk // world)
+    r = Hq // Hk
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    # this rank's shard only: query heads of its KV groups, and those K/V heads
+    q = torch.randn((Bq, pl.local * r, Sq, D), device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn((Bq, pl.local, Sq, D), device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn((Bq, pl.local, Sq, D), device=dev, generator=g).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    ms, _ = _timed(lambda: kernels.flash_attention(q, k, v, causal=True, out=o), 5, 2, stream, world)
+    fl = 4.0 * Bq * Hq * Sq * Sq * D / 2
+    full = torch.empty((world, *o.shape), dtype=o.dtype, device=dev)
+    g_ms, _ = _timed(lambda: dist.all_gather_into_tensor(full.reshape(-1, Sq, D), o.reshape(-1, Sq, D)), 5, 2,
+                     stream, world)
+    moved = gather_bytes(o.numel() * o.element_size() * world, world)
+    del full
+    return {"TFLOP/s": fl / (ms / 5 * 1e-3) / 1e12, "ms": ms / 5, "n_gpus": world,
+            "partition": f"KV groups over {world} GPUs (placement g -> (w, gl), {pl.local} KV heads per GPU)",
+            "gather": {"ms": g_ms / 5, "bytes_in_per_rank": moved, "GB/s_in_per_rank": moved / (g_ms / 5 * 1e-3) / 1e9,
+                       "predicted_ms": 1e3 * alpha_beta_seconds(moved, NVLINK_BPS, NCCL_LATENCY_S)},
+            "config": "B4 Hq64 Hkv8 S8192 D128 causal (config 4), strong scaling"}
 
 
 def _bwd(out, kernels, dev, stream, g):
