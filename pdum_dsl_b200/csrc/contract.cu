@@ -17,6 +17,7 @@
 //   * pointwise_f32_kernel -- the map-chain template over a strided tensor.
 #include <cfloat>
 #include <cstdlib>
+#include <mutex>
 
 #include "common.cuh"
 #include "tma.h"
@@ -581,8 +582,11 @@ extern "C" int pdb_contract(const pdb_contract_desc* d, void* stream) {
     if (e != cudaSuccess) return cuda_status(e, "contract bf16 pair: smem attribute");
     const int64_t tiles = d->batch * ((d->m + PM - 1) / PM) * ((d->n + PN - 1) / PN);
     if (tiles > 0x7fffffffLL) return set_error(PDB_ERR_SHAPE, "contract bf16: too many tiles");
+    // clusters of two that fit at once, per device (queried once, under a lock)
+    static std::mutex mu;
     static int max_pairs[64] = {};
-    if (dev < 64 && max_pairs[dev] == 0) {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= 0 && dev < 64 && max_pairs[dev] == 0) {
       cudaLaunchConfig_t cfg{};
       cfg.gridDim = dim3(2 * (unsigned)(sm_count(dev) / 2));
       cfg.blockDim = dim3(PTHREADS);
@@ -594,7 +598,7 @@ extern "C" int pdb_contract(const pdb_contract_desc* d, void* stream) {
       }
       max_pairs[dev] = n;
     }
-    const int cap = dev < 64 ? max_pairs[dev] : sm_count(dev) / 2;
+    const int cap = dev >= 0 && dev < 64 ? max_pairs[dev] : sm_count(dev) / 2;
     const int64_t pairs = tiles < cap ? tiles : cap;
     contract_bf16_pair_kernel<<<(unsigned)(2 * pairs), PTHREADS, smem, s>>>(ta, tb, p);
     return cuda_status(cudaGetLastError(), "contract bf16 pair launch");
