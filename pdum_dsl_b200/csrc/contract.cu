@@ -585,20 +585,23 @@ extern "C" int pdb_contract(const pdb_contract_desc* d, void* stream) {
     // clusters of two that fit at once, per device (queried once, under a lock)
     static std::mutex mu;
     static int max_pairs[64] = {};
-    std::lock_guard<std::mutex> lk(mu);
-    if (dev >= 0 && dev < 64 && max_pairs[dev] == 0) {
-      cudaLaunchConfig_t cfg{};
-      cfg.gridDim = dim3(2 * (unsigned)(sm_count(dev) / 2));
-      cfg.blockDim = dim3(PTHREADS);
-      cfg.dynamicSmemBytes = smem;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, contract_bf16_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
-        cudaGetLastError();
-        n = sm_count(dev) / 2;
+    int cap = sm_count(dev) / 2;
+    if (dev >= 0 && dev < 64) {
+      std::lock_guard<std::mutex> lk(mu);
+      if (max_pairs[dev] == 0) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(2 * (unsigned)(sm_count(dev) / 2));
+        cfg.blockDim = dim3(PTHREADS);
+        cfg.dynamicSmemBytes = smem;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, contract_bf16_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+          cudaGetLastError();
+          n = sm_count(dev) / 2;
+        }
+        max_pairs[dev] = n;
       }
-      max_pairs[dev] = n;
+      cap = max_pairs[dev];
     }
-    const int cap = dev >= 0 && dev < 64 ? max_pairs[dev] : sm_count(dev) / 2;
     const int64_t pairs = tiles < cap ? tiles : cap;
     contract_bf16_pair_kernel<<<(unsigned)(2 * pairs), PTHREADS, smem, s>>>(ta, tb, p);
     return cuda_status(cudaGetLastError(), "contract bf16 pair launch");
