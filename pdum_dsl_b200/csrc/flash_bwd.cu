@@ -47,6 +47,8 @@ struct BwdParams {
   int q_start, causal;
   float scale, scale_log2;
   int n_blocks;  // key blocks (dkdv) or query blocks (dq) per head
+  int B;
+  int* ctr;      // work-unit counter of a persistent kernel (zeroed by the prologue)
   int* err;
 };
 
@@ -489,18 +491,50 @@ __global__ void __launch_bounds__(kThreads, 1)
 // as soon as every compute warp holds item i's S / dP in registers (s_free),
 // before the accumulations of item i, and the compute warpgroups work on item
 // i+1 while the tensor core accumulates item i.
-struct __align__(8) Bars64 {
-  uint64_t fixed_full;                 // K/V (dK/dV kernel) or Q/dO (dQ kernel)
+// Persistent scheduling of the D = 64 kernels.  The work units (a 128-key
+// block for dK/dV, a 128-row query block for dQ) differ in size under the
+// causal mask (1 to n items); one CTA per unit left SMs idle ~40 % of the time
+// (CTA start / drain gaps and the uneven tail).  Here one CTA per SM takes units
+// from a global counter in descending size order (the counter lives in the
+// workspace and is zeroed by the prologue kernel), and the producer hands each
+// unit to the MMA thread and the compute warps through a two-slot queue in
+// shared memory.  K/V (or Q/dO) of the next unit load while the current one
+// runs; barrier phases follow running counters across units.
+struct __align__(8) UnitQueue {
+  uint64_t full[2], empty[2];  // producer -> consumers (1 MMA thread + 8 compute warps)
+  int unit[2];
+};
+
+__device__ __forceinline__ int fetch_unit(UnitQueue* uq, uint32_t n, int u, volatile int* abort, int* err) {
+  const int slot = n & 1;
+  if (!mbar_wait(&uq->empty[slot], ((n >> 1) & 1) ^ 1, abort, err)) return -2;
+  uq->unit[slot] = u;
+  mbar_arrive(&uq->full[slot]);
+  return u;
+}
+// consumer side: every compute warp (lane 0 after the warp converged) or the MMA thread
+__device__ __forceinline__ int take_unit(UnitQueue* uq, uint32_t n, volatile int* abort, int* err, bool warp_wide) {
+  const int slot = n & 1;
+  if (!mbar_wait(&uq->full[slot], (n >> 1) & 1, abort, err)) return -2;
+  const int u = *reinterpret_cast<volatile int*>(&uq->unit[slot]);
+  if (warp_wide) __syncwarp();
+  if (!warp_wide || (threadIdx.x & 31) == 0) mbar_arrive(&uq->empty[slot]);
+  return u;
+}
+
+struct __align__(8) Bars64P {
+  uint64_t fixed_full[2], fixed_empty[2];  // K/V (dK/dV kernel) or Q/dO (dQ kernel), per buffer
   uint64_t op_full[kStages], op_empty[kStages];  // streamed operand ring
-  uint64_t s_full, s_free, p_full, stage_free, o_full;
+  uint64_t s_full, s_free, p_full, stage_free, o_full, acc_free;
+  UnitQueue uq;
   uint32_t tmem_base;
   int abort;
 };
 
-// dK/dV, D = 64.  CTA = 128 keys; items = (query head, 128-row query tile).
-// TMEM: S^T [0,128)  dP^T [128,256)  staging P^T [256,320) dS^T [320,384)
-//       dV [384,448)  dK [448,512).  Compute warpgroup w owns query columns
-// [64w, 64w+64) of each item.
+// dK/dV, D = 64.  Unit = 128 keys of one (batch, KV head); items = (query head,
+// 128-row query tile).  TMEM: S^T [0,128)  dP^T [128,256)  staging P^T
+// [256,320) dS^T [320,384)  dV [384,448)  dK [448,512).  Compute warpgroup w
+// owns query columns [64w, 64w+64) of each item.
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_dkdv64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -510,30 +544,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kT = 128 * D * 2;  // any 128-row tile (16 KB)
   constexpr uint32_t kBox = 128 * 128;
-  uint8_t* sK = smem;
-  uint8_t* sV = smem + kT;
-  uint8_t* sQ = smem + 2 * kT;         // kStages
-  uint8_t* sDO = sQ + kStages * kT;    // kStages
+  uint8_t* sKV = smem;                   // 2 buffers x (K, V)
+  uint8_t* sQ = smem + 4 * kT;           // kStages
+  uint8_t* sDO = sQ + kStages * kT;      // kStages
   float* sVec = reinterpret_cast<float*>(sDO + kStages * kT);  // kStages x (nlse2[128], dsum[128])
-  Bars64* bar = reinterpret_cast<Bars64*>(reinterpret_cast<uint8_t*>(sVec) + kStages * 2 * 128 * 4);
+  Bars64P* bar = reinterpret_cast<Bars64P*>(reinterpret_cast<uint8_t*>(sVec) + kStages * 2 * 128 * 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  const int bhk = blockIdx.x / p.n_blocks;
-  const int nblk = blockIdx.x % p.n_blocks;
-  const int b = bhk / p.HKV, hk = bhk % p.HKV;
   const int group = p.H / p.HKV;
-  const int s0 = nblk * 128;
   const int n_qt = p.Tpad / 128;
-  int qt0 = 0;
-  if (p.causal) {
-    const int first = s0 - p.q_start;
-    qt0 = first > 0 ? first / 128 : 0;
-  }
-  const int per_head = n_qt - qt0 > 0 ? n_qt - qt0 : 0;
-  const int n_items = per_head * group;
+  const int n_bh = p.B * p.HKV;
+  const int n_units = p.n_blocks * n_bh;
+  // unit u: key block u / n_bh (ascending block = descending work under the causal mask)
+  auto unit_info = [&](int u, int& b, int& hk, int& s0, int& qt0, int& per_head) {
+    const int nblk = u / n_bh, bhk = u % n_bh;
+    b = bhk / p.HKV;
+    hk = bhk % p.HKV;
+    s0 = nblk * 128;
+    qt0 = 0;
+    if (p.causal) {
+      const int first = s0 - p.q_start;
+      qt0 = first > 0 ? first / 128 : 0;
+    }
+    per_head = n_qt - qt0 > 0 ? n_qt - qt0 : 0;
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar->fixed_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->fixed_full[i], 1);
+      mbar_init(&bar->fixed_empty[i], 1);
+      mbar_init(&bar->uq.full[i], 1);
+      mbar_init(&bar->uq.empty[i], 9);  // the MMA thread + 8 compute warps
+    }
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&bar->op_full[i], 1);
       mbar_init(&bar->op_empty[i], 1);
@@ -543,6 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bar->p_full, 8);  // one arrival per compute warp
     mbar_init(&bar->stage_free, 1);
     mbar_init(&bar->o_full, 1);
+    mbar_init(&bar->acc_free, 8);  // dK / dV read out of TMEM
     bar->abort = 0;
     fence_barrier_init();
   }
@@ -561,118 +603,165 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
     if (warp == 0 && lane == 0) {
-      mbar_expect_tx(&bar->fixed_full, 2 * kT);
-      tma_load_4d(sK, &tm_k, &bar->fixed_full, 0, s0, hk, b);
-      tma_load_4d(sV, &tm_v, &bar->fixed_full, 0, s0, hk, b);
-      for (int it = 0; it < n_items; ++it) {
-        const int st = it % kStages;
-        const int h = hk * group + it / per_head;
-        const int t0 = (qt0 + it % per_head) * 128;
-        if (!mbar_wait(&bar->op_empty[st], ((it / kStages) & 1) ^ 1, abort, p.err)) break;
-        mbar_expect_tx(&bar->op_full[st], 2 * kT + 2 * 128 * 4);
-        tma_load_4d(sQ + st * kT, &tm_q, &bar->op_full[st], 0, t0, h, b);
-        tma_load_4d(sDO + st * kT, &tm_do, &bar->op_full[st], 0, t0, h, b);
-        const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
-        bulk_load(sVec + st * 256, p.nlse2 + vrow, 512, &bar->op_full[st]);
-        bulk_load(sVec + st * 256 + 128, p.dsum + vrow, 512, &bar->op_full[st]);
+      // ---------------------------------------------------------- producer
+      uint32_t gi = 0, nu = 0, nkv = 0;  // items loaded, units handed out, K/V buffers filled
+      for (;; ++nu) {
+        int u = atomicAdd(p.ctr, 1);
+        if (u >= n_units) u = -1;
+        if (fetch_unit(&bar->uq, nu, u, abort, p.err) < 0) break;
+        int b, hk, s0, qt0, per_head;
+        unit_info(u, b, hk, s0, qt0, per_head);
+        const int n_items = per_head * group;
+        if (n_items == 0) continue;
+        const int kb = nkv & 1;
+        if (!mbar_wait(&bar->fixed_empty[kb], ((nkv >> 1) & 1) ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->fixed_full[kb], 2 * kT);
+        tma_load_4d(sKV + kb * 2 * kT, &tm_k, &bar->fixed_full[kb], 0, s0, hk, b);
+        tma_load_4d(sKV + kb * 2 * kT + kT, &tm_v, &bar->fixed_full[kb], 0, s0, hk, b);
+        ++nkv;
+        bool ok = true;
+        for (int it = 0; it < n_items; ++it, ++gi) {
+          const int st = gi % kStages;
+          const int h = hk * group + it / per_head;
+          const int t0 = (qt0 + it % per_head) * 128;
+          if (!(ok = mbar_wait(&bar->op_empty[st], ((gi / kStages) & 1) ^ 1, abort, p.err))) break;
+          mbar_expect_tx(&bar->op_full[st], 2 * kT + 2 * 128 * 4);
+          tma_load_4d(sQ + st * kT, &tm_q, &bar->op_full[st], 0, t0, h, b);
+          tma_load_4d(sDO + st * kT, &tm_do, &bar->op_full[st], 0, t0, h, b);
+          const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
+          bulk_load(sVec + st * 256, p.nlse2 + vrow, 512, &bar->op_full[st]);
+          bulk_load(sVec + st * 256 + 128, p.dsum + vrow, 512, &bar->op_full[st]);
+        }
+        if (!ok) break;
       }
     } else if (warp == 1 && lane == 0) {
-      bool ok = mbar_wait(&bar->fixed_full, 0, abort, p.err);
-      auto issue_s = [&](int it) -> bool {
-        const int st = it % kStages;
-        if (!mbar_wait(&bar->op_full[st], (it / kStages) & 1, abort, p.err)) return false;
-        tc_fence_after();
-        mma_kmajor<D>(tmem + 0, smem_u32(sK), kBox, smem_u32(sQ + st * kT), kBox, idS);     // S^T = K Q^T
-        mma_kmajor<D>(tmem + 128, smem_u32(sV), kBox, smem_u32(sDO + st * kT), kBox, idS);  // dP^T = V dO^T
-        tc_commit(&bar->s_full);
-        return true;
-      };
-      if (ok && n_items > 0) ok = issue_s(0);
-      for (int it = 0; ok && it < n_items; ++it) {
-        const int st = it % kStages;
-        // the next item's scores as soon as this item's S / dP sit in registers: they overlap the compute
-        if (!(ok = mbar_wait(&bar->s_free, it & 1, abort, p.err))) break;
-        tc_fence_after();
-        if (it + 1 < n_items && !(ok = issue_s(it + 1))) break;
-        if (!(ok = mbar_wait(&bar->p_full, it & 1, abort, p.err))) break;
-        tc_fence_after();
-        mma_tmem_a<128>(tmem + 384, tmem + 256, smem_u32(sDO + st * kT), kBox, idG, it > 0);  // dV += P^T dO
-        mma_tmem_a<128>(tmem + 448, tmem + 320, smem_u32(sQ + st * kT), kBox, idG, it > 0);   // dK += dS^T Q
-        tc_commit(&bar->op_empty[st]);
-        tc_commit(&bar->stage_free);
+      // -------------------------------------------------------- MMA issuer
+      uint32_t gi = 0, nu = 0, nkv = 0;  // items issued, units taken, units with items
+      bool ok = true;
+      for (;; ++nu) {
+        const int u = take_unit(&bar->uq, nu, abort, p.err, false);
+        if (u < 0) break;
+        int b, hk, s0, qt0, per_head;
+        unit_info(u, b, hk, s0, qt0, per_head);
+        const int n_items = per_head * group;
+        if (n_items == 0) continue;
+        const int kb = nkv & 1;
+        const uint32_t sK = smem_u32(sKV + kb * 2 * kT), sV = sK + kT;
+        if (!(ok = mbar_wait(&bar->fixed_full[kb], (nkv >> 1) & 1, abort, p.err))) break;
+        auto issue_s = [&](uint32_t g) -> bool {
+          const int st = g % kStages;
+          if (!mbar_wait(&bar->op_full[st], (g / kStages) & 1, abort, p.err)) return false;
+          tc_fence_after();
+          mma_kmajor<D>(tmem + 0, sK, kBox, smem_u32(sQ + st * kT), kBox, idS);     // S^T = K Q^T
+          mma_kmajor<D>(tmem + 128, sV, kBox, smem_u32(sDO + st * kT), kBox, idS);  // dP^T = V dO^T
+          tc_commit(&bar->s_full);
+          return true;
+        };
+        // S^T of the unit's first item overwrites the previous unit's last one: its
+        // compute warps must hold that in registers (s_free of item gi - 1)
+        if (gi > 0 && !(ok = mbar_wait(&bar->s_free, (gi - 1) & 1, abort, p.err))) break;
+        if (!(ok = issue_s(gi))) break;
+        for (int it = 0; ok && it < n_items; ++it) {
+          const uint32_t g = gi + it;
+          const int st = g % kStages;
+          if (it + 1 < n_items) {
+            // the next item's scores as soon as this item's S / dP sit in registers
+            if (!(ok = mbar_wait(&bar->s_free, g & 1, abort, p.err))) break;
+            tc_fence_after();
+            if (!(ok = issue_s(g + 1))) break;
+          }
+          if (!(ok = mbar_wait(&bar->p_full, g & 1, abort, p.err))) break;
+          // dV / dK of the previous unit must be read out before this unit's first accumulation
+          if (it == 0 && nkv > 0 && !(ok = mbar_wait(&bar->acc_free, (nkv - 1) & 1, abort, p.err))) break;
+          tc_fence_after();
+          mma_tmem_a<128>(tmem + 384, tmem + 256, smem_u32(sDO + st * kT), kBox, idG, it > 0);  // dV += P^T dO
+          mma_tmem_a<128>(tmem + 448, tmem + 320, smem_u32(sQ + st * kT), kBox, idG, it > 0);   // dK += dS^T Q
+          tc_commit(&bar->op_empty[st]);
+          tc_commit(&bar->stage_free);
+        }
+        if (!ok) break;
+        tc_commit(&bar->fixed_empty[kb]);  // every MMA reading this K/V buffer has been issued
+        tc_commit(&bar->o_full);
+        gi += n_items;
+        ++nkv;
       }
-      if (ok) tc_commit(&bar->o_full);
+      // the last unit's s_free arrivals are never waited on: nothing reads S^T after them
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
     const int w = warp >= 8 ? 1 : 0;  // query-column half
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;
-    const int s = s0 + row;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const uint32_t tl = tmem + lane_off;
     const float c = p.scale_log2;
+    const uint64_t c2 = f2_pack(c, c);
+    uint32_t gi = 0, nu = 0, nkv = 0;  // items computed, units taken, units with items
     bool ok = true;
-    for (int it = 0; it < n_items; ++it) {
-      const int st = it % kStages;
-      const int t0 = (qt0 + it % per_head) * 128;
-      if (!(ok = mbar_wait(&bar->op_full[st], (it / kStages) & 1, abort, p.err))) break;
-      if (!(ok = mbar_wait(&bar->s_full, it & 1, abort, p.err))) break;
-      tc_fence_after();
-      const float* nlse2 = sVec + st * 256 + w * 64;
-      const float* dsum = sVec + st * 256 + 128 + w * 64;
-      const int lo = p.causal ? s - p.q_start - t0 - w * 64 : -(1 << 30);  // columns below lo are masked
-      uint32_t pp[32], dd[32];
-      // packed f32x2 math; the causal select only on items that cross the diagonal
-      const bool need_mask = __any_sync(0xffffffffu, lo > 0);
-      const uint64_t c2 = f2_pack(c, c);
-      const uint32_t sl = smem_u32(nlse2), sd = smem_u32(dsum);
-      uint32_t srr[64], drr[64];
-      tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(srr));
-      tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(srr + 32));
-      tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(drr));
-      tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(drr + 32));
-      tmem_wait_ld();
-      warp_arrive_after_tc(&bar->s_free);  // S^T / dP^T are in registers: the next item's scores may overwrite them
+    for (;; ++nu) {
+      const int u = take_unit(&bar->uq, nu, abort, p.err, true);
+      if (u < 0) break;
+      int b, hk, s0, qt0, per_head;
+      unit_info(u, b, hk, s0, qt0, per_head);
+      const int n_items = per_head * group;
+      const int s = s0 + row;
+      for (int it = 0; it < n_items; ++it) {
+        const uint32_t g = gi + it;
+        const int st = g % kStages;
+        const int t0 = (qt0 + it % per_head) * 128;
+        if (!(ok = mbar_wait(&bar->op_full[st], (g / kStages) & 1, abort, p.err))) break;
+        if (!(ok = mbar_wait(&bar->s_full, g & 1, abort, p.err))) break;
+        tc_fence_after();
+        const int lo = p.causal ? s - p.q_start - t0 - w * 64 : -(1 << 30);  // columns below lo are masked
+        uint32_t pp[32], dd[32];
+        // packed f32x2 math; the causal select only on items that cross the diagonal
+        const bool need_mask = __any_sync(0xffffffffu, lo > 0);
+        const uint32_t sl = smem_u32(sVec + st * 256 + w * 64), sd = smem_u32(sVec + st * 256 + 128 + w * 64);
+        uint32_t srr[64], drr[64];
+        tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(srr));
+        tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(srr + 32));
+        tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(drr));
+        tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(drr + 32));
+        tmem_wait_ld();
+        warp_arrive_after_tc(&bar->s_free);  // S^T / dP^T are in registers: the next scores may overwrite them
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const uint32_t* sr = srr + 32 * hf;
-        const uint32_t* dr = drr + 32 * hf;
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint32_t* sr = srr + 32 * hf;
+          const uint32_t* dr = drr + 32 * hf;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 l4 = lds128(sl + 128 * hf + 16 * q);
-          const float4 d4 = lds128(sd + 128 * hf + 16 * q);
+          for (int q = 0; q < 8; ++q) {
+            const float4 l4 = lds128(sl + 128 * hf + 16 * q);
+            const float4 d4 = lds128(sd + 128 * hf + 16 * q);
 #pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            const int cc = 4 * q + 2 * h2, col = 32 * hf + cc;
-            const uint64_t s2 = (uint64_t)sr[cc] | ((uint64_t)sr[cc + 1] << 32);
-            const uint64_t g2 = (uint64_t)dr[cc] | ((uint64_t)dr[cc + 1] << 32);
-            const uint64_t l2 = h2 ? f2_pack(l4.z, l4.w) : f2_pack(l4.x, l4.y);
-            const uint64_t dd2 = h2 ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y);
-            float x0, x1;
-            f2_unpack(f2_fma(s2, c2, l2), x0, x1);
-            float p0 = ex2(x0), p1 = ex2(x1);
-            if (need_mask) {
-              p0 = col >= lo ? p0 : 0.f;
-              p1 = col + 1 >= lo ? p1 : 0.f;
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int cc = 4 * q + 2 * h2, col = 32 * hf + cc;
+              const uint64_t s2 = (uint64_t)sr[cc] | ((uint64_t)sr[cc + 1] << 32);
+              const uint64_t g2 = (uint64_t)dr[cc] | ((uint64_t)dr[cc + 1] << 32);
+              const uint64_t l2 = h2 ? f2_pack(l4.z, l4.w) : f2_pack(l4.x, l4.y);
+              const uint64_t dd2 = h2 ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y);
+              float x0, x1;
+              f2_unpack(f2_fma(s2, c2, l2), x0, x1);
+              float p0 = ex2(x0), p1 = ex2(x1);
+              if (need_mask) {
+                p0 = col >= lo ? p0 : 0.f;
+                p1 = col + 1 >= lo ? p1 : 0.f;
+              }
+              float g0, g1;
+              f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(g2, dd2)), g0, g1);
+              pp[16 * hf + 2 * q + h2] = pack_bf16(p0, p1);
+              dd[16 * hf + 2 * q + h2] = pack_bf16(g0, g1);
             }
-            float g0, g1;
-            f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(g2, dd2)), g0, g1);
-            pp[16 * hf + 2 * q + h2] = pack_bf16(p0, p1);
-            dd[16 * hf + 2 * q + h2] = pack_bf16(g0, g1);
           }
         }
+        // the staging area must be free of the previous item's accumulations
+        if (g > 0 && !(ok = mbar_wait(&bar->stage_free, (g - 1) & 1, abort, p.err))) break;
+        tc_fence_after();
+        tmem_st32(tl + 256 + w * 32, pp);
+        tmem_st32(tl + 320 + w * 32, dd);
+        tmem_wait_st();
+        warp_arrive_after_tc(&bar->p_full);
       }
-      // S^T / dP^T fully read: the staging area must be free of item it-1's accumulations
-      if (it > 0 && !(ok = mbar_wait(&bar->stage_free, (it - 1) & 1, abort, p.err))) break;
-      tc_fence_after();
-      tmem_st32(tl + 256 + w * 32, pp);
-      tmem_st32(tl + 320 + w * 32, dd);
-      tmem_wait_st();
-      warp_arrive_after_tc(&bar->p_full);
-    }
-    if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
-      tc_fence_after();
+      if (!ok) break;
       const bool store = s < p.S;
       __nv_bfloat16* dst = w == 0
           ? static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] + (int64_t)s * p.s1[2]
@@ -680,9 +769,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (n_items == 0) {
         if (store)
           for (int i = 0; i < D; i += 8) *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
-      } else {
-        store_cols_bf16<D>(tl + 384 + w * 64, w == 0 ? 1.0f : p.scale, dst, store);
+        continue;
       }
+      if (!(ok = mbar_wait(&bar->o_full, nkv & 1, abort, p.err))) break;
+      tc_fence_after();
+      store_cols_bf16<D>(tl + 384 + w * 64, w == 0 ? 1.0f : p.scale, dst, store);
+      warp_arrive_after_tc(&bar->acc_free);
+      gi += n_items;
+      ++nkv;
     }
   }
   tc_fence_before();
@@ -693,8 +787,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// dQ, D = 64.  CTA = 128 query rows; items = 128-key tiles.
-// TMEM: S [0,128)  dP [128,256)  staging dS [256,320)  dQ [320,384).
+// dQ, D = 64.  Unit = 128 query rows of one (batch, head); items = 128-key
+// tiles.  TMEM: S [0,128)  dP [128,256)  staging dS [256,320)  dQ [320,384).
 // Compute warpgroup w owns key columns [64w, 64w+64).
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_dq64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -705,29 +799,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kT = 128 * D * 2;
   constexpr uint32_t kBox = 128 * 128;
-  uint8_t* sQ = smem;
-  uint8_t* sDO = smem + kT;
-  uint8_t* sK = smem + 2 * kT;        // kStages
+  uint8_t* sQD = smem;                // 2 buffers x (Q, dO)
+  uint8_t* sK = smem + 4 * kT;        // kStages
   uint8_t* sV = sK + kStages * kT;    // kStages
-  Bars64* bar = reinterpret_cast<Bars64*>(sV + kStages * kT);
+  Bars64P* bar = reinterpret_cast<Bars64P*>(sV + kStages * kT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  const int bh = blockIdx.x / p.n_blocks;
-  const int mblk = p.n_blocks - 1 - (blockIdx.x % p.n_blocks);
-  const int b = bh / p.H, h = bh % p.H;
-  const int hk = h / (p.H / p.HKV);
-  const int t0 = mblk * 128;
+  const int n_bh = p.B * p.H;
+  const int n_units = p.n_blocks * n_bh;
   const int n_all = (p.S + 127) / 128;
-  int n_kv = n_all;
-  if (p.causal) {
-    int last = t0 + 127;
-    if (last > p.T - 1) last = p.T - 1;
-    const int n = (last + p.q_start) / 128 + 1;
-    n_kv = n < n_all ? n : n_all;
-  }
+  // unit u: query block n_blocks - 1 - u / n_bh (the heaviest blocks first under the causal mask)
+  auto unit_info = [&](int u, int& b, int& h, int& t0, int& n_kv) {
+    const int mblk = p.n_blocks - 1 - u / n_bh, bh = u % n_bh;
+    b = bh / p.H;
+    h = bh % p.H;
+    t0 = mblk * 128;
+    n_kv = n_all;
+    if (p.causal) {
+      int last = t0 + 127;
+      if (last > p.T - 1) last = p.T - 1;
+      const int n = (last + p.q_start) / 128 + 1;
+      n_kv = n < n_all ? (n > 0 ? n : 0) : n_all;
+    }
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar->fixed_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->fixed_full[i], 1);
+      mbar_init(&bar->fixed_empty[i], 1);
+      mbar_init(&bar->uq.full[i], 1);
+      mbar_init(&bar->uq.empty[i], 9);  // the MMA thread + 8 compute warps
+    }
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&bar->op_full[i], 1);
       mbar_init(&bar->op_empty[i], 1);
@@ -737,6 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bar->p_full, 8);  // one arrival per compute warp
     mbar_init(&bar->stage_free, 1);
     mbar_init(&bar->o_full, 1);
+    mbar_init(&bar->acc_free, 8);  // dQ read out of TMEM
     bar->abort = 0;
     fence_barrier_init();
   }
@@ -755,95 +857,148 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
     if (warp == 0 && lane == 0) {
-      mbar_expect_tx(&bar->fixed_full, 2 * kT);
-      tma_load_4d(sQ, &tm_q, &bar->fixed_full, 0, t0, h, b);
-      tma_load_4d(sDO, &tm_do, &bar->fixed_full, 0, t0, h, b);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % kStages;
-        if (!mbar_wait(&bar->op_empty[st], ((j / kStages) & 1) ^ 1, abort, p.err)) break;
-        mbar_expect_tx(&bar->op_full[st], 2 * kT);
-        tma_load_4d(sK + st * kT, &tm_k, &bar->op_full[st], 0, j * 128, hk, b);
-        tma_load_4d(sV + st * kT, &tm_v, &bar->op_full[st], 0, j * 128, hk, b);
+      // ---------------------------------------------------------- producer
+      uint32_t gi = 0, nu = 0, nqd = 0;  // items loaded, units handed out, Q/dO buffers filled
+      for (;; ++nu) {
+        int u = atomicAdd(p.ctr + 1, 1);
+        if (u >= n_units) u = -1;
+        if (fetch_unit(&bar->uq, nu, u, abort, p.err) < 0) break;
+        int b, h, t0, n_kv;
+        unit_info(u, b, h, t0, n_kv);
+        if (n_kv == 0) continue;
+        const int hk = h / (p.H / p.HKV);
+        const int qb = nqd & 1;
+        if (!mbar_wait(&bar->fixed_empty[qb], ((nqd >> 1) & 1) ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->fixed_full[qb], 2 * kT);
+        tma_load_4d(sQD + qb * 2 * kT, &tm_q, &bar->fixed_full[qb], 0, t0, h, b);
+        tma_load_4d(sQD + qb * 2 * kT + kT, &tm_do, &bar->fixed_full[qb], 0, t0, h, b);
+        ++nqd;
+        bool ok = true;
+        for (int j = 0; j < n_kv; ++j, ++gi) {
+          const int st = gi % kStages;
+          if (!(ok = mbar_wait(&bar->op_empty[st], ((gi / kStages) & 1) ^ 1, abort, p.err))) break;
+          mbar_expect_tx(&bar->op_full[st], 2 * kT);
+          tma_load_4d(sK + st * kT, &tm_k, &bar->op_full[st], 0, j * 128, hk, b);
+          tma_load_4d(sV + st * kT, &tm_v, &bar->op_full[st], 0, j * 128, hk, b);
+        }
+        if (!ok) break;
       }
     } else if (warp == 1 && lane == 0) {
-      bool ok = mbar_wait(&bar->fixed_full, 0, abort, p.err);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % kStages;
-        if (!mbar_wait(&bar->op_full[st], (j / kStages) & 1, abort, p.err)) return false;
-        tc_fence_after();
-        mma_kmajor<D>(tmem + 0, smem_u32(sQ), kBox, smem_u32(sK + st * kT), kBox, idS);     // S = Q K^T
-        mma_kmajor<D>(tmem + 128, smem_u32(sDO), kBox, smem_u32(sV + st * kT), kBox, idS);  // dP = dO V^T
-        tc_commit(&bar->s_full);
-        return true;
-      };
-      if (ok && n_kv > 0) ok = issue_s(0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % kStages;
-        if (!(ok = mbar_wait(&bar->s_free, j & 1, abort, p.err))) break;
-        tc_fence_after();
-        if (j + 1 < n_kv && !(ok = issue_s(j + 1))) break;
-        if (!(ok = mbar_wait(&bar->p_full, j & 1, abort, p.err))) break;
-        tc_fence_after();
-        mma_tmem_a<128>(tmem + 320, tmem + 256, smem_u32(sK + st * kT), kBox, idG, j > 0);  // dQ += dS K
-        tc_commit(&bar->op_empty[st]);
-        tc_commit(&bar->stage_free);
+      // -------------------------------------------------------- MMA issuer
+      uint32_t gi = 0, nu = 0, nqd = 0;  // items issued, units taken, units with items
+      bool ok = true;
+      for (;; ++nu) {
+        const int u = take_unit(&bar->uq, nu, abort, p.err, false);
+        if (u < 0) break;
+        int b, h, t0, n_kv;
+        unit_info(u, b, h, t0, n_kv);
+        if (n_kv == 0) continue;
+        const int qb = nqd & 1;
+        const uint32_t sQ = smem_u32(sQD + qb * 2 * kT), sDO = sQ + kT;
+        if (!(ok = mbar_wait(&bar->fixed_full[qb], (nqd >> 1) & 1, abort, p.err))) break;
+        auto issue_s = [&](uint32_t g) -> bool {
+          const int st = g % kStages;
+          if (!mbar_wait(&bar->op_full[st], (g / kStages) & 1, abort, p.err)) return false;
+          tc_fence_after();
+          mma_kmajor<D>(tmem + 0, sQ, kBox, smem_u32(sK + st * kT), kBox, idS);     // S = Q K^T
+          mma_kmajor<D>(tmem + 128, sDO, kBox, smem_u32(sV + st * kT), kBox, idS);  // dP = dO V^T
+          tc_commit(&bar->s_full);
+          return true;
+        };
+        if (gi > 0 && !(ok = mbar_wait(&bar->s_free, (gi - 1) & 1, abort, p.err))) break;
+        if (!(ok = issue_s(gi))) break;
+        for (int j = 0; ok && j < n_kv; ++j) {
+          const uint32_t g = gi + j;
+          const int st = g % kStages;
+          if (j + 1 < n_kv) {
+            if (!(ok = mbar_wait(&bar->s_free, g & 1, abort, p.err))) break;
+            tc_fence_after();
+            if (!(ok = issue_s(g + 1))) break;
+          }
+          if (!(ok = mbar_wait(&bar->p_full, g & 1, abort, p.err))) break;
+          if (j == 0 && nqd > 0 && !(ok = mbar_wait(&bar->acc_free, (nqd - 1) & 1, abort, p.err))) break;
+          tc_fence_after();
+          mma_tmem_a<128>(tmem + 320, tmem + 256, smem_u32(sK + st * kT), kBox, idG, j > 0);  // dQ += dS K
+          tc_commit(&bar->op_empty[st]);
+          tc_commit(&bar->stage_free);
+        }
+        if (!ok) break;
+        tc_commit(&bar->fixed_empty[qb]);
+        tc_commit(&bar->o_full);
+        gi += n_kv;
+        ++nqd;
       }
-      if (ok) tc_commit(&bar->o_full);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
     const int w = warp >= 8 ? 1 : 0;
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;
-    const int t = t0 + row;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const uint32_t tl = tmem + lane_off;
     const float c = p.scale_log2;
-    const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t;
-    const float l2 = p.nlse2[vrow];  // -inf on padded rows -> P = 0
-    const float dsum = p.dsum[vrow];
+    uint32_t gi = 0, nu = 0, nqd = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!(ok = mbar_wait(&bar->s_full, j & 1, abort, p.err))) break;
-      tc_fence_after();
-      const int lim = p.causal ? t + p.q_start + 1 - j * 128 - w * 64 : (1 << 30);  // key columns >= lim masked
-      uint32_t sr[64], dr[64];
-      tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(sr));
-      tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-      tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
-      tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
-      tmem_wait_ld();
-      warp_arrive_after_tc(&bar->s_free);
-      uint32_t dd[32];
-      const bool need_mask = __any_sync(0xffffffffu, lim < 64);
-      const uint64_t c2 = f2_pack(c, c), nl2 = f2_pack(l2, l2), ds2 = f2_pack(dsum, dsum);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int col = 2 * i;
-        const uint64_t s2 = (uint64_t)sr[col] | ((uint64_t)sr[col + 1] << 32);
-        const uint64_t g2 = (uint64_t)dr[col] | ((uint64_t)dr[col + 1] << 32);
-        float x0, x1;
-        f2_unpack(f2_fma(s2, c2, nl2), x0, x1);
-        float p0 = ex2(x0), p1 = ex2(x1);
-        if (need_mask) {
-          p0 = col < lim ? p0 : 0.f;
-          p1 = col + 1 < lim ? p1 : 0.f;
-        }
-        float g0, g1;
-        f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(g2, ds2)), g0, g1);
-        dd[i] = pack_bf16(g0, g1);
-      }
-      if (j > 0 && !(ok = mbar_wait(&bar->stage_free, (j - 1) & 1, abort, p.err))) break;
-      tc_fence_after();
-      tmem_st32(tl + 256 + w * 32, dd);
-      tmem_wait_st();
-      warp_arrive_after_tc(&bar->p_full);
-    }
-    if (ok && mbar_wait(&bar->o_full, 0, abort, p.err)) {
-      tc_fence_after();
+    for (;; ++nu) {
+      const int u = take_unit(&bar->uq, nu, abort, p.err, true);
+      if (u < 0) break;
+      int b, h, t0, n_kv;
+      unit_info(u, b, h, t0, n_kv);
+      const int t = t0 + row;
       __nv_bfloat16* dq = static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)h * p.s0[1] +
                           (int64_t)t * p.s0[2];
+      if (n_kv == 0) {  // no key is visible to these rows: dQ = 0
+        if (t < p.T)
+          for (int i = 0; i < 32; i += 8) *reinterpret_cast<uint4*>(dq + w * 32 + i) = make_uint4(0, 0, 0, 0);
+        continue;
+      }
+      const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t;
+      const float l2 = p.nlse2[vrow];  // -inf on padded rows -> P = 0
+      const float dsum = p.dsum[vrow];
+      const uint64_t c2 = f2_pack(c, c), nl2 = f2_pack(l2, l2), ds2 = f2_pack(dsum, dsum);
+      for (int j = 0; j < n_kv; ++j) {
+        const uint32_t g = gi + j;
+        if (!(ok = mbar_wait(&bar->s_full, g & 1, abort, p.err))) break;
+        tc_fence_after();
+        const int lim = p.causal ? t + p.q_start + 1 - j * 128 - w * 64 : (1 << 30);  // key columns >= lim masked
+        uint32_t sr[64], dr[64];
+        tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(sr));
+        tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+        tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
+        tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
+        tmem_wait_ld();
+        warp_arrive_after_tc(&bar->s_free);
+        uint32_t dd[32];
+        const bool need_mask = __any_sync(0xffffffffu, lim < 64);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = 2 * i;
+          const uint64_t s2 = (uint64_t)sr[col] | ((uint64_t)sr[col + 1] << 32);
+          const uint64_t g2 = (uint64_t)dr[col] | ((uint64_t)dr[col + 1] << 32);
+          float x0, x1;
+          f2_unpack(f2_fma(s2, c2, nl2), x0, x1);
+          float p0 = ex2(x0), p1 = ex2(x1);
+          if (need_mask) {
+            p0 = col < lim ? p0 : 0.f;
+            p1 = col + 1 < lim ? p1 : 0.f;
+          }
+          float g0, g1;
+          f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(g2, ds2)), g0, g1);
+          dd[i] = pack_bf16(g0, g1);
+        }
+        if (g > 0 && !(ok = mbar_wait(&bar->stage_free, (g - 1) & 1, abort, p.err))) break;
+        tc_fence_after();
+        tmem_st32(tl + 256 + w * 32, dd);
+        tmem_wait_st();
+        warp_arrive_after_tc(&bar->p_full);
+      }
+      if (!ok) break;
+      if (!(ok = mbar_wait(&bar->o_full, nqd & 1, abort, p.err))) break;
+      tc_fence_after();
       store_cols_bf16<32>(tl + 320 + w * 32, p.scale, dq + w * 32, t < p.T);
+      warp_arrive_after_tc(&bar->acc_free);
+      gi += n_kv;
+      ++nqd;
     }
   }
   tc_fence_before();
@@ -856,11 +1011,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------- prologue
 // D = sum(dO * O) and nlse2 = -lse * log2(e) per (b, h, padded row).  `tpr`
-// threads share a row, each reading 16-byte chunks (8 bf16) of O and dO.
+// threads share a row, each reading 16-byte chunks (8 bf16) of O and dO.  Also
+// zeroes the work-unit counters of the persistent kernels that follow.
 __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                 const float* __restrict__ lse, float* __restrict__ lse2, float* __restrict__ dsum,
                                 int64_t so0, int64_t so1, int64_t so2, int64_t sd0, int64_t sd1, int64_t sd2, int H,
-                                int T, int Tpad, int DV, int64_t rows, int tpr, int vec) {
+                                int T, int Tpad, int DV, int64_t rows, int tpr, int vec, int* ctr) {
+  if (blockIdx.x == 0 && threadIdx.x < 2) ctr[threadIdx.x] = 0;
   const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / tpr;
   const int sub = threadIdx.x % tpr;
   if (r >= rows) return;
@@ -897,7 +1054,7 @@ __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct WsLayout {
-  size_t lse2, dsum, lse, o_scratch, total;
+  size_t lse2, dsum, ctr, lse, o_scratch, total;
 };
 
 WsLayout ws_layout(const pdb_flash_bwd_desc& d) {
@@ -909,6 +1066,8 @@ WsLayout ws_layout(const pdb_flash_bwd_desc& d) {
   off = align256(off + rows * 4);
   w.dsum = off;
   off = align256(off + rows * 4);
+  w.ctr = off;  // two work-unit counters
+  off = align256(off + 8);
   if (d.lse == nullptr) {  // recompute variant: the forward's lse and a scratch output
     w.lse = off;
     off = align256(off + (size_t)(d.batch * d.heads_q * d.seqlen_q) * 4);
@@ -933,6 +1092,7 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
   const int64_t tpad = (d.seqlen_q + BT - 1) / BT * BT;
   float* lse2 = reinterpret_cast<float*>(ws + w.lse2);
   float* dsum = reinterpret_cast<float*>(ws + w.dsum);
+  int* ctr = reinterpret_cast<int*>(ws + w.ctr);
   {
     const int64_t rows = d.batch * d.heads_q * tpad;
     const bool vec = (d.head_dim_v % 8 == 0) && ((d.o_stride[0] | d.o_stride[1] | d.o_stride[2]) % 8 == 0) &&
@@ -947,7 +1107,7 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(d.o), static_cast<const __nv_bfloat16*>(d.dout), lse, lse2, dsum,
         d.o_stride[0], d.o_stride[1], d.o_stride[2], d.do_stride[0], d.do_stride[1], d.do_stride[2],
-        (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (int)d.head_dim_v, rows, tpr, vec ? 1 : 0);
+        (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (int)d.head_dim_v, rows, tpr, vec ? 1 : 0, ctr);
     if (int st = cuda_status(cudaGetLastError(), "bwd prep launch")) return st;
   }
   // dK/dV kernel: 64-row query tiles, 128-key blocks; dQ kernel: 128-row query blocks, 64-key tiles
@@ -972,7 +1132,10 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
   p.causal = d.causal ? 1 : 0;
   p.scale = (float)d.scale;
   p.scale_log2 = (float)(d.scale * 1.4426950408889634);
+  p.B = (int)d.batch;
   p.err = device_error_flag();
+  int dev = 0;
+  cudaGetDevice(&dev);
   // >= 120 KB keeps one CTA per SM, so the 512-column TMEM allocation never waits
   const int need_kv = 2 * (128 * D * 2) + kStages * 2 * (QT * D * 2) + kStages * 2 * QT * 4 + 256 + 1024;
   const int need_q = 2 * (128 * D * 2) + kStages * 2 * (KT * D * 2) + 256 + 1024;
@@ -987,11 +1150,13 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     }
     p.n_blocks = (int)((d.seqlen_k + 127) / 128);
     const int64_t grid = (int64_t)p.n_blocks * d.heads_kv * d.batch;
-    if (D == 64) {
-      const int smem = 2 * 16384 + kStages * 2 * 16384 + kStages * 1024 + 256 + 1024;
+    if (D == 64) {  // persistent: one CTA per SM takes key blocks from ctr[0]
+      const int smem = 4 * 16384 + kStages * 2 * 16384 + kStages * 1024 + (int)sizeof(Bars64P) + 1024;
       cudaError_t e = cudaFuncSetAttribute(bwd_dkdv64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return cuda_status(e, "bwd dkdv64 smem attribute");
-      bwd_dkdv64_kernel<<<(unsigned)grid, kThreads, smem, stream>>>(tq128, tk128, tv128, tdo128, p);
+      p.ctr = ctr;
+      const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
+      bwd_dkdv64_kernel<<<(unsigned)pgrid, kThreads, smem, stream>>>(tq128, tk128, tv128, tdo128, p);
     } else {
       cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
       if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
@@ -1005,11 +1170,13 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     for (int i = 0; i < 3; ++i) p.s0[i] = d.dq_stride[i];
     p.n_blocks = (int)(tpad / 128);
     const int64_t grid = (int64_t)p.n_blocks * d.heads_q * d.batch;
-    if (D == 64) {
-      const int smem = 2 * 16384 + kStages * 2 * 16384 + 256 + 1024;
+    if (D == 64) {  // persistent: one CTA per SM takes query blocks from ctr[1]
+      const int smem = 4 * 16384 + kStages * 2 * 16384 + (int)sizeof(Bars64P) + 1024;
       cudaError_t e = cudaFuncSetAttribute(bwd_dq64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return cuda_status(e, "bwd dq64 smem attribute");
-      bwd_dq64_kernel<<<(unsigned)grid, kThreads, smem, stream>>>(tq128, tk128, tv128, tdo128, p);
+      p.ctr = ctr;
+      const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
+      bwd_dq64_kernel<<<(unsigned)pgrid, kThreads, smem, stream>>>(tq128, tk128, tv128, tdo128, p);
     } else {
       cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
       if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
