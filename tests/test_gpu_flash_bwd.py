@@ -105,3 +105,36 @@ def test_bwd_query_offset(cuda):
     assert_bf16(_np(gq), rq, what="dq")
     assert_bf16(_np(gk), rk, what="dk")
     assert_bf16(_np(gv), rv, what="dv")
+
+
+@pytest.mark.parametrize("B,H,HKV,T,S,D", [(4, 16, 16, 1100, 1100, 128), (4, 32, 8, 1100, 1100, 128),
+                                           (4, 16, 4, 1100, 1100, 64), (2, 8, 8, 300, 1100, 128)])
+def test_bwd_persistent_units_vs_oracle(cuda, B, H, HKV, T, S, D):
+    """More work units than SMs (each persistent CTA takes several, light and heavy,
+    across heads and KV groups), ragged tails, and key blocks no query row can see
+    (S > T: those units write dK = dV = 0); sampled KV groups vs the oracle."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device=cuda).manual_seed(T + S + D + H)
+    q = torch.randn(B, H, T, D, device=cuda, generator=g).to(torch.bfloat16)
+    k, v = (torch.randn(B, HKV, S, D, device=cuda, generator=g).to(torch.bfloat16) for _ in range(2))
+    r = H // HKV
+    # dK / dV sum over the r query heads of a KV group: dO drawn at 1 / r keeps them O(1),
+    # where the absolute bf16 bar is meaningful (bf16 spacing is 2^-5 at 4..8)
+    do = (torch.randn(B, H, T, D, device=cuda, generator=g) / r).to(torch.bfloat16)
+    scale = 1 / math.sqrt(D)
+    o, lse = kernels.flash_attention(q, k, v, scale=scale, causal=True, return_lse=True)
+    gq, gk, gv = kernels.flash_attention_backward(q, k, v, o, do, lse, scale=scale, causal=True)
+    kernels.check_device_errors()
+    for b, hk in ((0, 0), (B - 1, HKV - 1)):
+        sl = slice(hk * r, (hk + 1) * r)
+        rq, rk, rv = OA.attention_bwd(*(x.double().cpu().numpy() for x in (q[b:b + 1, sl], k[b:b + 1, hk:hk + 1],
+                                                                             v[b:b + 1, hk:hk + 1], do[b:b + 1, sl])),
+                                      scale=scale, causal=True)
+        assert_bf16(_np(gq[b:b + 1, sl]), rq, what=f"dq ({b},{hk})")
+        assert_bf16(_np(gk[b:b + 1, hk:hk + 1]), rk, what=f"dk ({b},{hk})")
+        assert_bf16(_np(gv[b:b + 1, hk:hk + 1]), rv, what=f"dv ({b},{hk})")
+    if S > T:
+        assert gk[:, :, T:].abs().max().item() == 0 and gv[:, :, T:].abs().max().item() == 0
