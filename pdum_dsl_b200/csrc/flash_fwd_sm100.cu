@@ -406,6 +406,292 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// D = 64: P in its own TMEM columns.  With D = 128 the 512 TMEM columns hold
+// S_A, S_B, O_A, O_B and P must alias S, so a tile's next score MMA waits for
+// its PV (softmax, PV and QK form one chain per tile).  With D = 64 the O
+// accumulators take 64 columns each, which leaves room for P_A, P_B:
+//   S_A [0,128) S_B [128,256) O_A [256,320) O_B [320,384) P_A [384,448) P_B [448,512)
+// so S_x(j+1) is issued as soon as softmax x holds S_x(j) in registers
+// (s_free) and runs under the exponentials of step j; PV_x(j) releases P_x
+// (p_free) for step j+1.  K and V have their own producer threads and the
+// score and PV MMAs their own issuing threads, so no in-order wait of one
+// stream holds up the other.
+struct __align__(8) BarriersD64 {
+  uint64_t q_full, q_empty;
+  uint64_t k_full[2], k_empty[2];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[2];   // score MMA done -> softmax x
+  uint64_t s_free[2];   // softmax x holds S in registers -> next score MMA (4 warp arrivals)
+  uint64_t p_full[2];   // P_x written -> PV (4 warp arrivals)
+  uint64_t p_free[2];   // PV_x done: P_x may be rewritten, O_x is quiescent
+  uint64_t o_full[2], o_empty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_fwd_d64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+  constexpr int D = 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using L = Smem<D>;  // Q_A, Q_B, K x 2, V x 2
+  BarriersD64* bar = reinterpret_cast<BarriersD64*>(smem + L::kBar);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = p.num_mblocks * p.H * p.B;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 1);
+    mbar_init(&bar->q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->k_full[i], 1);
+      mbar_init(&bar->k_empty[i], 1);
+      mbar_init(&bar->v_full[i], 1);
+      mbar_init(&bar->v_empty[i], 1);
+      mbar_init(&bar->s_full[i], 1);
+      mbar_init(&bar->s_free[i], BM / 32);
+      mbar_init(&bar->p_full[i], BM / 32);
+      mbar_init(&bar->p_free[i], 1);
+      mbar_init(&bar->o_full[i], 1);
+      mbar_init(&bar->o_empty[i], BM / 32);
+    }
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+  const uint32_t sQ[2] = {smem_u32(smem + L::kQ0), smem_u32(smem + L::kQ1)};
+  const uint32_t sK = smem_u32(smem + L::kK), sV = smem_u32(smem + L::kV);
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+    if (warp == 0 && lane == 0) {
+      // -------------------------------------------------- Q and K producer
+      prefetch_tensormap(&tm_q);
+      prefetch_tensormap(&tm_k);
+      uint32_t gk = 0, tt = 0;
+      bool ok = true;
+      for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+        const TileInfo ti = tile_info(tile, p);
+        if (!(ok = mbar_wait(&bar->q_empty, (tt & 1) ^ 1, abort, p.err))) break;
+        mbar_expect_tx(&bar->q_full, 2 * L::kTileBytes);
+        tma_load_4d(smem + L::kQ0, &tm_q, &bar->q_full, 0, ti.t0, ti.h, ti.b);
+        tma_load_4d(smem + L::kQ1, &tm_q, &bar->q_full, 0, ti.t0 + BM, ti.h, ti.b);
+        for (int j = 0; j < ti.nB; ++j, ++gk) {
+          const int st = gk & 1;
+          if (!(ok = mbar_wait(&bar->k_empty[st], ((gk >> 1) & 1) ^ 1, abort, p.err))) break;
+          mbar_expect_tx(&bar->k_full[st], L::kTileBytes);
+          tma_load_4d(smem + L::kK + st * L::kTileBytes, &tm_k, &bar->k_full[st], 0, j * BN, ti.hk, ti.b);
+        }
+      }
+    } else if (warp == 2 && lane == 0) {
+      // -------------------------------------------------------- V producer
+      prefetch_tensormap(&tm_v);
+      uint32_t gv = 0;
+      bool ok = true;
+      for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k)) {
+        const TileInfo ti = tile_info(tile, p);
+        for (int j = 0; j < ti.nB; ++j, ++gv) {
+          const int st = gv & 1;
+          if (!(ok = mbar_wait(&bar->v_empty[st], ((gv >> 1) & 1) ^ 1, abort, p.err))) break;
+          mbar_expect_tx(&bar->v_full[st], L::kTileBytes);
+          tma_load_4d(smem + L::kV + st * L::kTileBytes, &tm_v, &bar->v_full[st], 0, j * BN, ti.hk, ti.b);
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      // ------------------------------------------ score MMA issuer (QK)
+      const uint32_t tS[2] = {tmem + 0, tmem + 128};
+      uint32_t gk = 0, tt = 0, nqk[2] = {0, 0};
+      bool ok = true;
+      auto issue_qk = [&](int x) -> bool {
+        // S_x may only be overwritten once softmax x holds the previous one in registers
+        if (nqk[x] > 0 && !mbar_wait(&bar->s_free[x], (nqk[x] - 1) & 1, abort, p.err)) return false;
+        tc_fence_after();
+        mma_qk<D>(tS[x], sQ[x], sK + (gk & 1) * L::kTileBytes);
+        tc_commit(&bar->s_full[x]);
+        ++nqk[x];
+        return true;
+      };
+      for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+        const TileInfo ti = tile_info(tile, p);
+        if (!(ok = mbar_wait(&bar->q_full, tt & 1, abort, p.err))) break;
+        for (int j = 0; ok && j < ti.nB; ++j) {
+          if (!(ok = mbar_wait(&bar->k_full[gk & 1], (gk >> 1) & 1, abort, p.err))) break;
+          if (j < ti.nA && !(ok = issue_qk(0))) break;
+          if (!(ok = issue_qk(1))) break;
+          tc_commit(&bar->k_empty[gk & 1]);
+          ++gk;
+        }
+        if (ok) tc_commit(&bar->q_empty);  // every score MMA of this tile has been issued
+      }
+    } else if (warp == 3 && lane == 0) {
+      // ------------------------------------------------ PV MMA issuer
+      const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
+      const uint32_t tP[2] = {tmem + 384, tmem + 448};
+      uint32_t gv = 0, tt = 0, npf[2] = {0, 0};
+      bool ok = true;
+      for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+        const TileInfo ti = tile_info(tile, p);
+        for (int j = 0; ok && j < ti.nB; ++j) {
+          const int st = gv & 1;
+          if (!(ok = mbar_wait(&bar->v_full[st], (gv >> 1) & 1, abort, p.err))) break;
+          for (int x = 0; x < 2; ++x) {
+            if (x == 0 && j >= ti.nA) continue;
+            if (!(ok = mbar_wait(&bar->p_full[x], npf[x] & 1, abort, p.err))) break;
+            ++npf[x];
+            if (j == 0 && !(ok = mbar_wait(&bar->o_empty[x], (tt & 1) ^ 1, abort, p.err))) break;
+            tc_fence_after();
+            mma_pv<D>(tO[x], tP[x], sV + st * L::kTileBytes, j > 0);
+            tc_commit(&bar->p_free[x]);
+            if (j + 1 == (x ? ti.nB : ti.nA)) tc_commit(&bar->o_full[x]);
+          }
+          if (!ok) break;
+          tc_commit(&bar->v_empty[st]);
+          ++gv;
+        }
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
+    // ------------------------------------------------------------- softmax
+    const int x = (warp >= 8) ? 1 : 0;  // tile A / B
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tS = tmem + lane_off + x * 128;
+    const uint32_t tO = tmem + lane_off + 256 + x * D;
+    const uint32_t tP = tmem + lane_off + 384 + x * 64;
+    const float c = p.scale_log2;
+    uint32_t cs = 0, tt = 0, pw = 0;  // S tiles read, work tiles, P tiles written
+    bool ok = true;
+    for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+      const TileInfo ti = tile_info(tile, p);
+      const int t = ti.t0 + x * BM + row;
+      const int n = x ? ti.nB : ti.nA;
+      float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j, ++cs) {
+        if (!(ok = mbar_wait(&bar->s_full[x], cs & 1, abort, p.err))) break;
+        tc_fence_after();
+        int lim = p.S - j * BN;
+        if (p.causal) {
+          const int lc = t + p.q_start + 1 - j * BN;
+          lim = lc < lim ? lc : lim;
+        }
+        const bool need_mask = __any_sync(0xffffffffu, lim < BN);
+        uint32_t sr[BN];
+#pragma unroll
+        for (int ch = 0; ch < BN / 32; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
+        tmem_wait_ld();
+        warp_arrive_after_tc(&bar->s_free[x]);  // the next score MMA of this tile may overwrite S_x
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < BN; ++i)
+            if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
+        }
+        float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < BN; i += 8) {
+          mxa = max3(mxa, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+          mxb = max3(mxb, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
+          mxc = max3(mxc, __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
+          mxd = max3(mxd, __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
+        }
+        const float mt = fmaxf(max3(mxa, mxb, mxc), mxd) * c;
+        m_true = fmaxf(m_true, mt);
+        // PV_x(j-1) must be done before P_x is rewritten or O_x rescaled
+        if (pw > 0 && !(ok = mbar_wait(&bar->p_free[x], (pw - 1) & 1, abort, p.err))) break;
+        tc_fence_after();
+        if (j == 0) {
+          m_used = mt;
+        } else if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
+          const float m_new = fmaxf(m_used, mt);
+          const float alpha = ex2(m_used - m_new);
+          m_used = m_new;
+          l *= alpha;
+          uint32_t r[32];
+#pragma unroll
+          for (int ch = 0; ch < D / 32; ++ch) {
+            tmem_ld32(tO + ch * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tO + ch * 32, r);
+          }
+        }
+        const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+        const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(neg_m, neg_m);
+        uint64_t sum_a = 0, sum_b = 0;
+#pragma unroll
+        for (int ch = 0; ch < BN / 32; ++ch) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint64_t sv = (uint64_t)sr[ch * 32 + 2 * i] | ((uint64_t)sr[ch * 32 + 2 * i + 1] << 32);
+            float x0, x1;
+            f2_unpack(f2_fma(sv, c2, nm2), x0, x1);
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            const uint64_t pv = f2_pack(p0, p1);
+            if (i & 1) sum_b = f2_add(sum_b, pv); else sum_a = f2_add(sum_a, pv);
+            pk[i] = pack_bf16(p0, p1);
+          }
+          tmem_st16(tP + ch * 16, pk);
+        }
+        float sa0, sa1, sb0, sb1;
+        f2_unpack(sum_a, sa0, sa1);
+        f2_unpack(sum_b, sb0, sb1);
+        l += (sa0 + sa1) + (sb0 + sb1);
+        tmem_wait_st();
+        warp_arrive_after_tc(&bar->p_full[x]);
+        ++pw;
+      }
+      if (!ok || !(ok = mbar_wait(&bar->o_full[x], tt & 1, abort, p.err))) break;
+      tc_fence_after();
+      const float inv_l = 1.0f / l;
+      const bool store = t < p.T;
+      const int64_t bhq = (int64_t)ti.b * p.H + ti.h;
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.o) + (int64_t)ti.b * p.o_stride[0] +
+                            (int64_t)ti.h * p.o_stride[1] + (int64_t)t * p.o_stride[2];
+#pragma unroll
+      for (int ch = 0; ch < D / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(tO + ch * 32, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
+        if (store) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+      warp_arrive_after_tc(&bar->o_empty[x]);
+      if (store) {
+        const int64_t idx = bhq * p.T + t;
+        constexpr float kLn2 = 0.6931471805599453f;
+        if (p.lse) p.lse[idx] = (m_used + __log2f(l)) * kLn2;
+        if (p.m) p.m[idx] = m_true * kLn2;
+        if (p.den) p.den[idx] = l * ex2(m_used - m_true);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 template <int D>
 int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   CUtensorMap tq, tk, tv;
@@ -448,6 +734,12 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   const int64_t units = (nblk + 1) / 2;  // tile pairs
   const int64_t grid = units < sm_count(dev) ? units : sm_count(dev);  // persistent: one CTA per SM
   const int smem = Smem<D>::kTotal;
+  if (D == 64) {  // P in its own TMEM columns (656 vs 610 TFLOP/s at B8 H32 S4096 causal)
+    cudaError_t e = cudaFuncSetAttribute(flash_fwd_d64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_status(e, "bf16 flash: set smem attribute");
+    flash_fwd_d64_kernel<<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, p);
+    return cuda_status(cudaGetLastError(), "bf16 flash launch");
+  }
   cudaError_t e = cudaFuncSetAttribute(flash_fwd_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_status(e, "bf16 flash: set smem attribute");
   flash_fwd_sm100_kernel<D><<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, p);
