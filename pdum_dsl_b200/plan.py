@@ -65,3 +65,90 @@ def plan_region(region, machine=None, floor: int = 1024):
               ("backend", B200_FP))
     arts = ("m", "den") if spec.artifacts else ()
     return fusion.Plan((fusion.Group("flash", region, cert, "yellow", params=params, artifacts=arts),))
+
+
+_CHART_OPS = ("tl.with_charts", "tl.strip_charts", "tl.simplify")
+
+
+def _bare(node):
+    while node.op in _CHART_OPS:
+        node = node.args[0]
+    return node
+
+
+def _kernel_of(carve):
+    return carve.group.kernel if carve.group.kernel is not None else carve.kernel
+
+
+def device_assignment(plan) -> list[str]:
+    """Per carve of a ``plan_model`` ModelPlan (``pdum/tl/partition.py:586``):
+    ``"device"`` when ``compile_tile`` lowers its kernel to the sm_100a library,
+    ``"reference"`` when the group is red or the kernel has no template here (the
+    reference doctrine: red groups are served by ``run_region``)."""
+    from .tile import compile_tile
+
+    out = []
+    for c in plan.carves:
+        where = "reference"
+        if c.root is not None and c.group.confidence != "red":
+            try:
+                compile_tile(_kernel_of(c))
+                where = "device"
+            except Untranslatable:
+                pass
+        out.append(where)
+    return out
+
+
+def execute_model_plan(plan, region, values, *, device: bool = True):
+    """Execute a carved plan carve by carve, the way the reference executes one
+    (``tests/test_partition.py:124-193``): a carve runs once every boundary value
+    it reads is known; its kernel runs on the sm_100a library when
+    ``device_assignment`` says so (f32 IEEE column, numpy in / out), else through
+    ``run_region``.  ``values`` are ``Tensor``s per region param; returns the
+    yielded values (``Tensor``s) and the per-carve assignment."""
+    import numpy as np
+    from pdum.tl.dialect import run_region
+    from pdum.tl.tensor import Tensor
+
+    from .tile import compile_tile
+
+    assign = device_assignment(plan) if device else ["reference"] * len(plan.carves)
+    vals = {id(p): v for p, v in zip(region.params, values)}
+
+    def known(b):
+        while id(b) not in vals and b.op in _CHART_OPS:
+            b = b.args[0]
+        return b
+
+    pending = [(i, c) for i, c in enumerate(plan.carves) if c.root is not None]
+    progressed = True
+    while pending and progressed:
+        progressed = False
+        for i, c in list(pending):
+            bounds = [known(b) for b in c.bounds]
+            if not all(id(b) in vals for b in bounds):
+                continue
+            kernel = _kernel_of(c)
+            ins = [vals[id(b)] for b in bounds]
+            if assign[i] == "device":
+                arrs = [t.to_numpy(order=tuple(d.name for d in p.type.dims)) for t, p in zip(ins, kernel.params)]
+                got = compile_tile(kernel)(arrs)
+                got = got if isinstance(got, tuple) else (got,)
+                y = kernel.body[-1].args[0]
+                ynodes = y.args if y.op == "core.tuple" else (y,)
+                outs = tuple(Tensor.from_numpy(np.asarray(a, dtype=np.float64), tuple(d.name for d in n.type.dims))
+                             for a, n in zip(got, ynodes))
+            else:
+                got = run_region(kernel, ins)
+                outs = tuple(got) if isinstance(got, (tuple, list)) else (got,)
+            for node, val in zip((c.root, *c.artifacts), outs):
+                vals[id(node)] = val
+                vals[id(_bare(node))] = val  # chart roots alias their bare value
+            pending.remove((i, c))
+            progressed = True
+    if pending:
+        raise RuntimeError("plan stalled: a carve reads a boundary value no carve produces")
+    y = region.body[-1].args[0]
+    targets = y.args if y.op == "core.tuple" else (y,)
+    return tuple(vals[id(known(t))] for t in targets), assign

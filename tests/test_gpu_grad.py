@@ -54,3 +54,30 @@ def test_scaled_rider_gqa_joint_vs_run_region(cuda, dsl):
     got = compile_grad(rg)(arrs)
     for g, w in zip(got, want):
         assert_bf16(g, w.to_numpy(order=w.names))
+
+
+def test_model_plan_executes_carve_by_carve(cuda, dsl):
+    """The carved backward plan run carve by carve, device carves on the sm_100a library
+    (f32 IEEE column) and the rest through run_region, reproduces run_region of the
+    whole joint."""
+    from pdum.tl.dialect import run_region
+    from pdum.tl.partition import plan_model
+    from pdum.tl.tensor import Tensor
+    from pdum.tl.zoo.tiles import flash_tile
+
+    from pdum_dsl_b200.plan import execute_model_plan
+    from tests.tolerances import assert_f32
+
+    rg = _joint(flash_tile(T=64, E=8, OD=8, SI=2).naive)
+    plan = plan_model(rg.region)
+    rng = np.random.default_rng(5)
+    ins = []
+    for p in rg.region.params:
+        dims = p.type.dims
+        ins.append(Tensor.from_numpy(rng.standard_normal(tuple(d.stop - d.start for d in dims)),
+                                     tuple(d.name for d in dims)))
+    want = run_region(rg.region, list(ins))
+    got, assign = execute_model_plan(plan, rg.region, ins)
+    assert assign.count("device") >= 3
+    for g, w in zip(got, want):
+        assert_f32(g.to_numpy(order=w.names), w.to_numpy(order=w.names))

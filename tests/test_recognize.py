@@ -172,3 +172,30 @@ def test_map_chain_spec(dsl):
     y = b.emit("tl.pointwise", b.emit("tl.pointwise", px, f="exp"), b.emit("core.const", type=f64, value=2.0), f="mul")
     s = recognize(Region(params=(px,), body=(b.emit("core.yield", y),)))
     assert isinstance(s, MapSpec) and [e[0] for e in s.steps] == ["exp", "mul"]
+
+
+def _flash_joint(T=64, E=8, OD=8):
+    from pdum.tl.autodiff import grad
+    from pdum.tl.zoo.tiles import flash_tile
+
+    region = flash_tile(T=T, E=E, OD=OD, SI=2).naive
+    out = region.body[-1].args[0]
+    names = {id(p): f"p{i}" for i, p in enumerate(region.params)}
+    names[id(out)] = "out"
+    return grad(region, "out", seed="dO", names=names)
+
+
+def test_model_plan_carves_assigned_to_the_device(dsl):
+    """plan_model's carves of the flash joint (reference tests/test_partition.py:124-193):
+    the flash-with-artifacts carve and the plain contraction carves lower to the sm_100a
+    library; red groups and the carves whose operands re-derive P stay with run_region."""
+    from pdum.tl.partition import plan_model
+
+    from pdum_dsl_b200.plan import device_assignment
+
+    plan = plan_model(_flash_joint().region)
+    assign = device_assignment(plan)
+    by = list(zip((c.group.template for c in plan.carves), assign))
+    assert ("flash", "device") in by
+    assert sum(1 for t, a in by if t == "contraction-epilogue" and a == "device") >= 2
+    assert all(a == "reference" for c, a in zip(plan.carves, assign) if c.group.confidence == "red")
