@@ -387,10 +387,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PTHREADS, 1)
   auto coords = [&](int t, int& bi, int& m0, int& n0) {
     bi = t / (tm * tn);
     const int r = t % (tm * tn);
-    const int gsz = 4 * tn;  // groups of 4 m-tile rows (1024 rows of A)
+    constexpr int G = 8;  // m-tile rows per group (2048 rows of A); 4-16 measured alike
+    const int gsz = G * tn;
     const int grp = r / gsz, in = r % gsz;
-    const int rows = (tm - grp * 4) < 4 ? (tm - grp * 4) : 4;
-    m0 = (grp * 4 + in % rows) * PM;
+    const int rows = (tm - grp * G) < G ? (tm - grp * G) : G;
+    m0 = (grp * G + in % rows) * PM;
     n0 = (in / rows) * PN;
   };
 
