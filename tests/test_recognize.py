@@ -199,3 +199,25 @@ def test_model_plan_carves_assigned_to_the_device(dsl):
     assert ("flash", "device") in by
     assert sum(1 for t, a in by if t == "contraction-epilogue" and a == "device") >= 2
     assert all(a == "reference" for c, a in zip(plan.carves, assign) if c.group.confidence == "red")
+
+
+def test_model_plan_executor_on_the_reference(dsl):
+    """The carve-by-carve executor itself (every carve through run_region) reproduces
+    run_region of the whole joint, as the reference's own executor test does."""
+    import numpy as np
+    from pdum.tl.dialect import run_region
+    from pdum.tl.partition import plan_model
+    from pdum.tl.tensor import Tensor
+
+    from pdum_dsl_b200.plan import execute_model_plan
+
+    rg = _flash_joint(T=8, E=4, OD=4)
+    plan = plan_model(rg.region)
+    rng = np.random.default_rng(5)
+    ins = [Tensor.from_numpy(rng.standard_normal(tuple(d.stop - d.start for d in p.type.dims)),
+                             tuple(d.name for d in p.type.dims)) for p in rg.region.params]
+    want = run_region(rg.region, list(ins))
+    got, assign = execute_model_plan(plan, rg.region, ins, device=False)
+    assert set(assign) == {"reference"}
+    for g, w in zip(got, want):
+        np.testing.assert_allclose(g.to_numpy(order=w.names), w.to_numpy(order=w.names), rtol=1e-9, atol=1e-12)
