@@ -199,3 +199,23 @@ def test_the_tile_flagships_run(cuda, dsl):
         run = compile_tile(f.region)
         got = run([v.to_numpy() for v in f.inputs.values()])
         assert_f32(got, f.oracle(f.numpy_inputs()))
+
+
+def test_ledger_measures_and_greens_planned_groups(cuda, dsl):
+    """pdum_dsl_b200.ledger: the device time of each lowered group as a ledger fact
+    (CUDA-event microseconds), the plan's groups green, and no re-measurement warm."""
+    import torch
+    from pdum.tl.analysis import no_reanalysis
+    from pdum.tl.fusion import plan_region
+    from pdum.tl.zoo.tiles import flash_tile
+
+    from pdum_dsl_b200 import ledger
+
+    plan = plan_region(flash_tile(T=256, E=64, OD=64, SI=2).naive)
+    machine = torch.cuda.get_device_name(0)
+    green, facts = ledger.green_plan(plan, machine=machine, reps=5)
+    assert [g.confidence for g in green.groups] == ["green"]
+    assert 0 < facts[0].value["us"] < 1e5
+    with no_reanalysis():
+        again = ledger.sm100_us(plan.groups[0].kernel, machine=machine, dtype="bf16", reps=5)
+    assert again.key == facts[0].key
