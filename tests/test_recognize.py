@@ -221,3 +221,41 @@ def test_model_plan_executor_on_the_reference(dsl):
     assert set(assign) == {"reference"}
     for g, w in zip(got, want):
         np.testing.assert_allclose(g.to_numpy(order=w.names), w.to_numpy(order=w.names), rtol=1e-9, atol=1e-12)
+
+
+def test_backend_record_for_the_seam(dsl):
+    """The reference's backend capability record (dsl/registry.py:56-70): the
+    fingerprint carries the library version, render names the launch, compile returns
+    the compile_tile runner, and the record registers in a registry."""
+    from pdum.dsl.registry import Backend, Registry
+    from pdum.tl.zoo.tiles import flash_tile
+
+    from pdum_dsl_b200._lib import version
+    from pdum_dsl_b200.backend import b200_backend
+
+    be = b200_backend()
+    assert isinstance(be, Backend) and be.fp == ("b200_sm100a", version())
+    region = flash_tile(T=64, E=8, OD=8, SI=2).naive
+    src = be.render(region)
+    assert "pdb_flash_fwd" in src
+    run = be.compile(src, "flash")
+    assert isinstance(run.spec, AttentionSpec)
+    reg = Registry()
+    reg.register_backend(be)
+    assert reg.backends["b200_sm100a"] is be
+    with pytest.raises(Untranslatable):
+        be.render(_rows_only_unsupported())
+
+
+def _rows_only_unsupported():
+    """A region with no template here: a plain sum over a single param."""
+    import numpy as np
+    from pdum.dsl.ir import Builder, Region
+    from pdum.dsl.ops import CORE_OPS
+    from pdum.tl.dialect import TL_OPS, tensor_type_of_layout
+    from pdum.tl.tensor import Tensor
+
+    b = Builder({**CORE_OPS, **TL_OPS})
+    x = b.param(0, tensor_type_of_layout(Tensor.from_numpy(np.zeros((3, 4)), ("r", "c")).layout))
+    y = b.emit("tl.reduce", x, dims=("c",), f="sum")
+    return Region(params=(x,), body=(b.emit("core.yield", y),))
