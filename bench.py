@@ -152,24 +152,31 @@ def _timed(fn, steps, warmup, stream, world):
     return total, per
 
 
-def cpu_attention_sample(head_seq=S, rows=S):
-    """Time the oracle (numpy f64) on one causal head: `rows` query rows at the END
-    of a head of length head_seq (the heaviest rows); returns (tflops, seconds, desc)."""
+def cpu_attention_sample(head_seq=S, rows=S, min_seconds=0.0):
+    """Time the oracle (numpy f64) on whole causal heads of config 3: `rows` query rows
+    at the END of a head of length head_seq (the heaviest rows), repeated over fresh
+    seeded heads until at least `min_seconds` of CPU time have been spent (a bounded
+    sample of the workload); returns (tflops, seconds, desc)."""
     import numpy as np
 
     from oracle import attention as OA
 
-    rng = np.random.default_rng(0)
-    q = rng.standard_normal((rows, D))
-    k = rng.standard_normal((head_seq, D))
-    v = rng.standard_normal((head_seq, D))
-    t0 = time.perf_counter()
-    OA.attention_fwd(q, k, v, scale=1 / math.sqrt(D), causal=True, q_start=head_seq - rows, row_block=256)
-    dt = time.perf_counter() - t0
     # causal work of those rows: sum over rows of (t+1) keys, 4*D flops per (row, key)
     t_abs = np.arange(head_seq - rows, head_seq) + 1
-    flops = 4.0 * D * float(t_abs.sum())
-    return flops / dt / 1e12, dt, f"{rows} query rows x {head_seq} keys of one causal head (D={D}), numpy f64"
+    flops_head = 4.0 * D * float(t_abs.sum())
+    heads, dt = 0, 0.0
+    while heads == 0 or dt < min_seconds:
+        rng = np.random.default_rng(heads)
+        q = rng.standard_normal((rows, D))
+        k = rng.standard_normal((head_seq, D))
+        v = rng.standard_normal((head_seq, D))
+        t0 = time.perf_counter()
+        OA.attention_fwd(q, k, v, scale=1 / math.sqrt(D), causal=True, q_start=head_seq - rows, row_block=256)
+        dt += time.perf_counter() - t0
+        heads += 1
+    desc = (f"{heads} causal head(s) of {rows} query rows x {head_seq} keys (D={D}) of config 3's "
+            f"{B * H}, numpy f64, {dt:.1f} s")
+    return flops_head * heads / dt / 1e12, dt, desc
 
 
 def _cpu_threads():
@@ -193,7 +200,7 @@ def run_reference(args):
     t_all = 0.0
     desc = ""
     for _ in range(args.steps_ref):
-        tf, dt, desc = cpu_attention_sample()
+        tf, dt, desc = cpu_attention_sample(min_seconds=6.0)
         vals.append(tf)
         t_all += dt
     v = sorted(vals)[len(vals) // 2]
@@ -288,7 +295,7 @@ def run_ours(args):
         if gq is not None:
             extra["gqa_fwd_sharded"] = gq
     if rank == 0 and world == 1 and not args.no_cpu:
-        tf, dt, desc = cpu_attention_sample()
+        tf, dt, desc = cpu_attention_sample(min_seconds=10.0)
         cpu_base = {"value": tf, "unit": "TFLOP/s", "cores": _cpu_threads(), "kind": "port", "sample": desc,
                     "seconds": round(dt, 2)}
     if world > 1:
