@@ -31,6 +31,13 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   return t;
 }
 
+// Programmatic dependent launch.  grid_dep_wait: block until the grids this one
+// was launched behind (with programmatic stream serialization) have completed and
+// their memory is visible; a no-op for an ordinary launch.  grid_dep_launch: let
+// the next such grid be scheduled once every CTA of this one has signalled or exited.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

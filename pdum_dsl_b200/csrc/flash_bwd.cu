@@ -22,6 +22,7 @@
 // and is rounded to bf16 once.  No atomics: the result is deterministic.
 #include <cfloat>
 #include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "tma.h"
@@ -236,6 +237,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_wait();    // the prologue (D, nlse2, zeroed counters) has completed
+  grid_dep_launch();  // the dQ grid may take SMs as this grid's CTAs retire
   const uint32_t tmem = bar->tmem_base;
   volatile int* abort = &bar->abort;
   constexpr int kNB = D / 64;
@@ -608,6 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  grid_dep_wait();  // complete only after the dK/dV grid this one overlapped has completed
 }
 
 // ---------------------------------------------------------------------------
@@ -692,6 +696,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_wait();    // the prologue (D, nlse2, zeroed counters) has completed
+  grid_dep_launch();  // the dQ grid may take SMs as this grid's CTAs retire
   const uint32_t tmem = bar->tmem_base;
   volatile int* abort = &bar->abort;
   constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
@@ -1104,6 +1110,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  grid_dep_wait();  // complete only after the dK/dV grid this one overlapped has completed
 }
 
 // ---------------------------------------------------------------- prologue
@@ -1183,6 +1190,25 @@ int map_bf16(CUtensorMap* m, const void* base, int D, int64_t rows, int64_t head
   return encode_tma_4d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Launch behind the previous kernel of the stream with programmatic stream
+// serialization: the grid may start (set-up: barriers, TMEM, tensor maps) while
+// the previous one drains; the kernel orders its reads with grid_dep_wait.
+template <class... KArgs, class... Args>
+cudaError_t launch_overlapped(void (*kernel)(KArgs...), int64_t grid, int smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <int D>
 int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w, cudaStream_t stream) {
   uint8_t* ws = static_cast<uint8_t*>(d.workspace);
@@ -1254,13 +1280,15 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       if (e != cudaSuccess) return cuda_status(e, "bwd dkdv64 smem attribute");
       p.ctr = ctr;
       const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      bwd_dkdv64_kernel<<<(unsigned)pgrid, kThreads, smem, stream>>>(tq128, tk128, tv128, tdo128, p);
+      e = launch_overlapped(bwd_dkdv64_kernel, pgrid, smem, stream, tq128, tk128, tv128, tdo128, p);
+      if (e != cudaSuccess) return cuda_status(e, "bwd dkdv64 launch");
     } else {
       cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
       if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
       p.ctr = ctr;
       const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      bwd_dkdv_kernel<D><<<(unsigned)pgrid, kThreads, smem_kv, stream>>>(tq64, tk128, tv128, tdo64, p);
+      e = launch_overlapped(bwd_dkdv_kernel<D>, pgrid, smem_kv, stream, tq64, tk128, tv128, tdo64, p);
+      if (e != cudaSuccess) return cuda_status(e, "bwd dkdv launch");
     }
     if (int st = cuda_status(cudaGetLastError(), "bwd dkdv launch")) return st;
   }
@@ -1276,13 +1304,15 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       if (e != cudaSuccess) return cuda_status(e, "bwd dq64 smem attribute");
       p.ctr = ctr;
       const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      bwd_dq64_kernel<<<(unsigned)pgrid, kThreads, smem, stream>>>(tq128, tk128, tv128, tdo128, p);
+      e = launch_overlapped(bwd_dq64_kernel, pgrid, smem, stream, tq128, tk128, tv128, tdo128, p);
+      if (e != cudaSuccess) return cuda_status(e, "bwd dq64 launch");
     } else {
       cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
       if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
       p.ctr = ctr;
       const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      bwd_dq_kernel<D><<<(unsigned)pgrid, kThreads, smem_q, stream>>>(tq128, tk64, tv64, tdo128, p);
+      e = launch_overlapped(bwd_dq_kernel<D>, pgrid, smem_q, stream, tq128, tk64, tv64, tdo128, p);
+      if (e != cudaSuccess) return cuda_status(e, "bwd dq launch");
     }
     if (int st = cuda_status(cudaGetLastError(), "bwd dq launch")) return st;
   }
