@@ -1113,18 +1113,418 @@ __global__ void __launch_bounds__(kThreads, 1)
   grid_dep_wait();  // complete only after the dK/dV grid this one overlapped has completed
 }
 
+// ---------------------------------------------------------------------------
+// Fused D = 64 backward: dK, dV and dQ in one persistent pass.
+// The dK/dV schedule above (unit = 128 keys of one (batch, KV head), items =
+// (query head, 128-row query tile)) plus, per item, the dQ contribution of the
+// unit's keys, dQ_part = dS K, so the scores and exponentials are formed once
+// instead of once per kernel.  dS^T goes to shared memory (bf16, 128-byte
+// swizzled rows of 64 queries per key), where it serves as the K-major A
+// operand of dK += dS^T Q and, read the other way, as the MN-major A operand
+// of dQ_part = dS K.  dQ_part lands in its own TMEM columns; a drain warpgroup
+// reads it out, stages it in shared memory and adds it into an fp32 dQ
+// accumulator in the workspace with TMA bulk reductions (performed in L2; the
+// accumulator of config-5-sized problems fits there).  A final kernel scales
+// and rounds the accumulator to bf16.  dQ then depends on the order of the
+// fp32 additions (not bit-reproducible run to run); dK and dV do not.
+constexpr int kStagesF = 2;
+constexpr int kFusedThreads = 512;  // warps 0..3 control, 4..11 compute, 12..15 dQ drain
+
+struct __align__(8) BarsF {
+  uint64_t fixed_full[2], fixed_empty[2];          // K/V per buffer
+  uint64_t op_full[kStagesF], op_empty[kStagesF];  // Q/dO ring
+  uint64_t s_full, s_free, p_full, stage_free, o_full, acc_free;
+  uint64_t dq_full, dq_free, stg_full, stg_free;   // dQ_part TMEM -> drain -> staging -> bulk reduce
+  UnitQueue uq;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, uint32_t smem_src, int c0, int c1, int c2,
+                                                  int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void sts128(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// TMEM: S^T [0,128)  dP^T [128,256)  staging P^T [256,320)  dQ_part [320,384)
+// dV [384,448)  dK [448,512).  Shared memory: K/V x 2 buffers, Q/dO x
+// kStagesF, nlse2/dsum rows, dS^T (two 16 KB halves of 64 queries), dQ staging
+// (two 16 KB boxes of 32 fp32 columns).
+__global__ void __launch_bounds__(kFusedThreads, 1)
+    bwd_fused64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                       const __grid_constant__ CUtensorMap tm_dqacc, const BwdParams p) {
+  constexpr int D = 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kT = 128 * D * 2;  // any 128-row bf16 tile (16 KB)
+  constexpr uint32_t kBox = 128 * 128;
+  uint8_t* sKV = smem;                       // 2 buffers x (K, V)
+  uint8_t* sQ = smem + 4 * kT;               // kStagesF
+  uint8_t* sDO = sQ + kStagesF * kT;         // kStagesF
+  uint8_t* sDS = sDO + kStagesF * kT;        // dS^T, 2 x 16 KB
+  uint8_t* sDQ = sDS + 2 * kT;               // dQ staging, 2 x 16 KB
+  float* sVec = reinterpret_cast<float*>(sDQ + 2 * kT);  // kStagesF x (nlse2[128], dsum[128])
+  BarsF* bar = reinterpret_cast<BarsF*>(reinterpret_cast<uint8_t*>(sVec) + kStagesF * 2 * 128 * 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = p.H / p.HKV;
+  const int n_qt = p.Tpad / 128;
+  const int n_bh = p.B * p.HKV;
+  const int n_units = p.n_blocks * n_bh;
+  auto unit_info = [&](int u, int& b, int& hk, int& s0, int& qt0, int& per_head) {
+    const int nblk = u / n_bh, bhk = u % n_bh;
+    b = bhk / p.HKV;
+    hk = bhk % p.HKV;
+    s0 = nblk * 128;
+    qt0 = 0;
+    if (p.causal) {
+      const int first = s0 - p.q_start;
+      qt0 = first > 0 ? first / 128 : 0;
+    }
+    per_head = n_qt - qt0 > 0 ? n_qt - qt0 : 0;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->fixed_full[i], 1);
+      mbar_init(&bar->fixed_empty[i], 1);
+      mbar_init(&bar->uq.full[i], 1);
+      mbar_init(&bar->uq.empty[i], 13);  // the MMA thread + 8 compute warps + 4 drain warps
+    }
+    for (int i = 0; i < kStagesF; ++i) {
+      mbar_init(&bar->op_full[i], 1);
+      mbar_init(&bar->op_empty[i], 1);
+    }
+    mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->s_free, 8);
+    mbar_init(&bar->p_full, 8);
+    mbar_init(&bar->stage_free, 1);
+    mbar_init(&bar->o_full, 1);
+    mbar_init(&bar->acc_free, 8);
+    mbar_init(&bar->dq_full, 1);
+    mbar_init(&bar->dq_free, 4);   // drain warps: dQ_part in registers
+    mbar_init(&bar->stg_full, 4);  // drain warps: staging written
+    mbar_init(&bar->stg_free, 1);  // the reduction has read the staging
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == 3 && lane == 0) {
+    prefetch_tensormap(&tm_q);
+    prefetch_tensormap(&tm_do);
+    prefetch_tensormap(&tm_k);
+    prefetch_tensormap(&tm_v);
+    prefetch_tensormap(&tm_dqacc);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  grid_dep_wait();  // the prologue (D, nlse2, zeroed counters and dQ accumulator) has completed
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+  constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
+  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);   // dV, dK: A K-major (TMEM / smem), B MN-major
+  constexpr uint32_t idQ = idesc_bf16(128, D, 1, 1);   // dQ: A = dS MN-major (smem), B = K MN-major
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");  // 128 x 80 + 256 x 176 + 128 x 80 = 65536
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- producer
+      uint32_t gi = 0, nu = 0, nkv = 0;
+      for (;; ++nu) {
+        int u = atomicAdd(p.ctr, 1);
+        if (u >= n_units) u = -1;
+        if (fetch_unit(&bar->uq, nu, u, abort, p.err) < 0) break;
+        int b, hk, s0, qt0, per_head;
+        unit_info(u, b, hk, s0, qt0, per_head);
+        const int n_items = per_head * group;
+        if (n_items == 0) continue;
+        const int kb = nkv & 1;
+        if (!mbar_wait(&bar->fixed_empty[kb], ((nkv >> 1) & 1) ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->fixed_full[kb], 2 * kT);
+        tma_load_4d(sKV + kb * 2 * kT, &tm_k, &bar->fixed_full[kb], 0, s0, hk, b);
+        tma_load_4d(sKV + kb * 2 * kT + kT, &tm_v, &bar->fixed_full[kb], 0, s0, hk, b);
+        ++nkv;
+        bool ok = true;
+        for (int it = 0; it < n_items; ++it, ++gi) {
+          const int st = gi % kStagesF;
+          const int h = hk * group + it / per_head;
+          const int t0 = (qt0 + it % per_head) * 128;
+          if (!(ok = mbar_wait(&bar->op_empty[st], ((gi / kStagesF) & 1) ^ 1, abort, p.err))) break;
+          mbar_expect_tx(&bar->op_full[st], 2 * kT + 2 * 128 * 4);
+          tma_load_4d(sQ + st * kT, &tm_q, &bar->op_full[st], 0, t0, h, b);
+          tma_load_4d(sDO + st * kT, &tm_do, &bar->op_full[st], 0, t0, h, b);
+          const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
+          bulk_load(sVec + st * 256, p.nlse2 + vrow, 512, &bar->op_full[st]);
+          bulk_load(sVec + st * 256 + 128, p.dsum + vrow, 512, &bar->op_full[st]);
+        }
+        if (!ok) break;
+      }
+    } else if (warp == 1 && lane == 0) {
+      // -------------------------------------------------------- MMA issuer
+      uint32_t gi = 0, nu = 0, nkv = 0;
+      bool ok = true;
+      const uint32_t sDSa = smem_u32(sDS);
+      for (;; ++nu) {
+        const int u = take_unit(&bar->uq, nu, abort, p.err, false);
+        if (u < 0) break;
+        int b, hk, s0, qt0, per_head;
+        unit_info(u, b, hk, s0, qt0, per_head);
+        const int n_items = per_head * group;
+        if (n_items == 0) continue;
+        const int kb = nkv & 1;
+        const uint32_t sK = smem_u32(sKV + kb * 2 * kT), sV = sK + kT;
+        if (!(ok = mbar_wait(&bar->fixed_full[kb], (nkv >> 1) & 1, abort, p.err))) break;
+        auto issue_s = [&](uint32_t g) -> bool {
+          const int st = g % kStagesF;
+          if (!mbar_wait(&bar->op_full[st], (g / kStagesF) & 1, abort, p.err)) return false;
+          tc_fence_after();
+          mma_kmajor<D>(tmem + 0, sK, kBox, smem_u32(sQ + st * kT), kBox, idS);     // S^T = K Q^T
+          mma_kmajor<D>(tmem + 128, sV, kBox, smem_u32(sDO + st * kT), kBox, idS);  // dP^T = V dO^T
+          tc_commit(&bar->s_full);
+          return true;
+        };
+        if (gi > 0 && !(ok = mbar_wait(&bar->s_free, (gi - 1) & 1, abort, p.err))) break;
+        if (!(ok = issue_s(gi))) break;
+        for (int it = 0; ok && it < n_items; ++it) {
+          const uint32_t g = gi + it;
+          const int st = g % kStagesF;
+          if (it + 1 < n_items) {
+            if (!(ok = mbar_wait(&bar->s_free, g & 1, abort, p.err))) break;
+            tc_fence_after();
+            if (!(ok = issue_s(g + 1))) break;
+          }
+          if (!(ok = mbar_wait(&bar->p_full, g & 1, abort, p.err))) break;
+          if (it == 0 && nkv > 0 && !(ok = mbar_wait(&bar->acc_free, (nkv - 1) & 1, abort, p.err))) break;
+          tc_fence_after();
+          const uint32_t sQst = smem_u32(sQ + st * kT), sDOst = smem_u32(sDO + st * kT);
+          mma_tmem_a<128>(tmem + 384, tmem + 256, sDOst, kBox, idG, it > 0);  // dV += P^T dO
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q  (A: dS^T K-major, two 64-query halves)
+            mma_ss(tmem + 448, sdesc_sw128(sDSa + (kk >> 2) * kT + (kk & 3) * 32, 16, 1024),
+                   sdesc_sw128(sQst + kk * 2048, kBox, 1024), idG, (it > 0 || kk > 0) ? 1u : 0u);
+          // dQ_part = dS K once the drain holds the previous item's part in registers
+          if (g > 0 && !(ok = mbar_wait(&bar->dq_free, (g - 1) & 1, abort, p.err))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // A: dS MN-major (query halves 16 KB apart), B: K MN-major
+            mma_ss(tmem + 320, sdesc_sw128(sDSa + kk * 2048, kT, 1024), sdesc_sw128(sK + kk * 2048, kBox, 1024), idQ,
+                   kk > 0 ? 1u : 0u);
+          tc_commit(&bar->op_empty[st]);
+          tc_commit(&bar->stage_free);
+          tc_commit(&bar->dq_full);
+        }
+        if (!ok) break;
+        tc_commit(&bar->fixed_empty[kb]);
+        tc_commit(&bar->o_full);
+        gi += n_items;
+        ++nkv;
+      }
+    }
+  } else if (warp < 12) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 176;" ::: "memory");
+    const int w = warp >= 8 ? 1 : 0;  // query-column half
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tl = tmem + lane_off;
+    const float c = p.scale_log2;
+    const uint64_t c2 = f2_pack(c, c);
+    const uint32_t ds_row = smem_u32(sDS) + w * kT + row * 128;
+    uint32_t gi = 0, nu = 0, nkv = 0;
+    bool ok = true;
+    for (;; ++nu) {
+      const int u = take_unit(&bar->uq, nu, abort, p.err, true);
+      if (u < 0) break;
+      int b, hk, s0, qt0, per_head;
+      unit_info(u, b, hk, s0, qt0, per_head);
+      const int n_items = per_head * group;
+      const int s = s0 + row;
+      for (int it = 0; it < n_items; ++it) {
+        const uint32_t g = gi + it;
+        const int st = g % kStagesF;
+        const int t0 = (qt0 + it % per_head) * 128;
+        if (!(ok = mbar_wait(&bar->op_full[st], (g / kStagesF) & 1, abort, p.err))) break;
+        if (!(ok = mbar_wait(&bar->s_full, g & 1, abort, p.err))) break;
+        tc_fence_after();
+        const int lo = p.causal ? s - p.q_start - t0 - w * 64 : -(1 << 30);  // columns below lo are masked
+        uint32_t pp[32], dd[32];
+        const bool need_mask = __any_sync(0xffffffffu, lo > 0);
+        const uint32_t sl = smem_u32(sVec + st * 256 + w * 64), sd = smem_u32(sVec + st * 256 + 128 + w * 64);
+        uint32_t srr[64], drr[64];
+        tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(srr));
+        tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(srr + 32));
+        tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(drr));
+        tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(drr + 32));
+        tmem_wait_ld();
+        warp_arrive_after_tc(&bar->s_free);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint32_t* sr = srr + 32 * hf;
+          const uint32_t* dr = drr + 32 * hf;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 l4 = lds128(sl + 128 * hf + 16 * q);
+            const float4 d4 = lds128(sd + 128 * hf + 16 * q);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int cc = 4 * q + 2 * h2, col = 32 * hf + cc;
+              const uint64_t s2 = (uint64_t)sr[cc] | ((uint64_t)sr[cc + 1] << 32);
+              const uint64_t g2 = (uint64_t)dr[cc] | ((uint64_t)dr[cc + 1] << 32);
+              const uint64_t l2 = h2 ? f2_pack(l4.z, l4.w) : f2_pack(l4.x, l4.y);
+              const uint64_t dd2 = h2 ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y);
+              float x0, x1;
+              f2_unpack(f2_fma(s2, c2, l2), x0, x1);
+              float p0 = ex2(x0), p1 = ex2(x1);
+              if (need_mask) {
+                p0 = col >= lo ? p0 : 0.f;
+                p1 = col + 1 >= lo ? p1 : 0.f;
+              }
+              float g0, g1;
+              f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(g2, dd2)), g0, g1);
+              pp[16 * hf + 2 * q + h2] = pack_bf16(p0, p1);
+              dd[16 * hf + 2 * q + h2] = pack_bf16(g0, g1);
+            }
+          }
+        }
+        // the P^T staging columns and the dS^T buffer must be free of the previous item's MMAs
+        if (g > 0 && !(ok = mbar_wait(&bar->stage_free, (g - 1) & 1, abort, p.err))) break;
+        tc_fence_after();
+        tmem_st32(tl + 256 + w * 32, pp);
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)  // 128-byte swizzled row of 64 queries for key `row`
+          sts128(ds_row + ((ch ^ (row & 7)) << 4), dd[4 * ch], dd[4 * ch + 1], dd[4 * ch + 2], dd[4 * ch + 3]);
+        fence_proxy_async_smem();
+        tmem_wait_st();
+        warp_arrive_after_tc(&bar->p_full);
+      }
+      if (!ok) break;
+      const bool store = s < p.S;
+      __nv_bfloat16* dst = w == 0
+          ? static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] + (int64_t)s * p.s1[2]
+          : static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] + (int64_t)s * p.s0[2];
+      if (n_items == 0) {
+        if (store)
+          for (int i = 0; i < D; i += 8) *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
+        continue;
+      }
+      if (!(ok = mbar_wait(&bar->o_full, nkv & 1, abort, p.err))) break;
+      tc_fence_after();
+      store_cols_bf16<D>(tl + 384 + w * 64, w == 0 ? 1.0f : p.scale, dst, store);
+      warp_arrive_after_tc(&bar->acc_free);
+      gi += n_items;
+      ++nkv;
+    }
+  } else {
+    // ------------------------------------------------------------ dQ drain
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;  // query row of the item
+    const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
+    const uint32_t stg = smem_u32(sDQ) + row * 128;
+    const bool issuer = warp == 12 && lane == 0;
+    uint32_t gi = 0, nu = 0;
+    bool ok = true;
+    for (;; ++nu) {
+      const int u = take_unit(&bar->uq, nu, abort, p.err, true);
+      if (u < 0) break;
+      int b, hk, s0, qt0, per_head;
+      unit_info(u, b, hk, s0, qt0, per_head);
+      const int n_items = per_head * group;
+      for (int it = 0; it < n_items; ++it) {
+        const uint32_t g = gi + it;
+        const int h = hk * group + it / per_head;
+        const int t0 = (qt0 + it % per_head) * 128;
+        if (!(ok = mbar_wait(&bar->dq_full, g & 1, abort, p.err))) break;
+        tc_fence_after();
+        // the previous reduction must have read the staging buffer
+        if (!(ok = mbar_wait(&bar->stg_free, (g & 1) ^ 1, abort, p.err))) break;
+#pragma unroll
+        for (int bx = 0; bx < 2; ++bx) {  // 32 columns (one staging box) at a time
+          uint32_t r[32];
+          tmem_ld32(tl + 320 + 32 * bx, r);
+          tmem_wait_ld();
+          if (bx == 1) warp_arrive_after_tc(&bar->dq_free);  // dQ_part is out of TMEM
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch)
+            sts128(stg + bx * kT + ((ch ^ (row & 7)) << 4), r[4 * ch], r[4 * ch + 1], r[4 * ch + 2], r[4 * ch + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->stg_full);
+        if (warp == 12) {  // lane 0 issues the item's two bulk reductions
+          bool good = true;
+          if (issuer && (good = mbar_wait(&bar->stg_full, g & 1, abort, p.err))) {
+            tma_reduce_add_4d(&tm_dqacc, smem_u32(sDQ), 0, t0, h, b);
+            tma_reduce_add_4d(&tm_dqacc, smem_u32(sDQ) + kT, 32, t0, h, b);
+            bulk_commit();
+            bulk_wait_read_all();
+            mbar_arrive(&bar->stg_free);
+          }
+          if (!(ok = __shfl_sync(0xffffffffu, good ? 1 : 0, 0) != 0)) break;
+        }
+      }
+      if (!ok) break;
+      gi += n_items;
+    }
+    if (issuer) bulk_wait_all();  // the reductions are complete before the CTA retires
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dQ (bf16) = scale * the fp32 accumulator of the fused pass, rows t < T.
+// Eight features per thread (two 16-byte loads, one 16-byte store).
+__global__ void bwd_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t s0,
+                                      int64_t s1, int64_t s2, int H, int T, int Tpad, float scale, int64_t n) {
+  grid_dep_wait();  // the fused pass (and its bulk reductions) has completed
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int ch = (int)(i & 7);
+  const int64_t r = i >> 3;
+  const int t = (int)(r % T);
+  const int64_t bh = r / T;
+  const int b = (int)(bh / H), h = (int)(bh % H);
+  const float4* src = reinterpret_cast<const float4*>(acc + (bh * Tpad + t) * 64 + ch * 8);
+  const float4 a = src[0], c = src[1];
+  *reinterpret_cast<uint4*>(dq + b * s0 + h * s1 + t * s2 + ch * 8) =
+      make_uint4(pack_bf16(a.x * scale, a.y * scale), pack_bf16(a.z * scale, a.w * scale),
+                 pack_bf16(c.x * scale, c.y * scale), pack_bf16(c.z * scale, c.w * scale));
+}
+
 // ---------------------------------------------------------------- prologue
 // D = sum(dO * O) and nlse2 = -lse * log2(e) per (b, h, padded row).  `tpr`
 // threads share a row, each reading 16-byte chunks (8 bf16) of O and dO.  Also
-// zeroes the work-unit counters of the persistent kernels that follow.
+// zeroes the work-unit counters of the persistent kernels that follow and, for
+// the fused D = 64 pass, its fp32 dQ accumulator.
 __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                 const float* __restrict__ lse, float* __restrict__ lse2, float* __restrict__ dsum,
                                 int64_t so0, int64_t so1, int64_t so2, int64_t sd0, int64_t sd1, int64_t sd2, int H,
-                                int T, int Tpad, int DV, int64_t rows, int tpr, int vec, int* ctr) {
+                                int T, int Tpad, int DV, int64_t rows, int tpr, int vec, int* ctr,
+                                float* __restrict__ dqacc) {
   if (blockIdx.x == 0 && threadIdx.x < 2) ctr[threadIdx.x] = 0;
   const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / tpr;
   const int sub = threadIdx.x % tpr;
   if (r >= rows) return;
+  if (dqacc)  // the fused D = 64 pass adds its dQ parts into this (rows of 64 fp32)
+    for (int i = sub * 4; i < 64; i += tpr * 4)
+      *reinterpret_cast<float4*>(dqacc + r * 64 + i) = make_float4(0.f, 0.f, 0.f, 0.f);
   const int t = (int)(r % Tpad);
   const int64_t bh = r / Tpad;
   const int b = (int)(bh / H), h = (int)(bh % H);
@@ -1158,7 +1558,7 @@ __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct WsLayout {
-  size_t lse2, dsum, ctr, lse, o_scratch, total;
+  size_t lse2, dsum, ctr, dqacc, lse, o_scratch, total;
 };
 
 WsLayout ws_layout(const pdb_flash_bwd_desc& d) {
@@ -1172,6 +1572,10 @@ WsLayout ws_layout(const pdb_flash_bwd_desc& d) {
   off = align256(off + rows * 4);
   w.ctr = off;  // two work-unit counters
   off = align256(off + 8);
+  if (d.head_dim == 64) {  // fp32 dQ accumulator of the fused pass, rows padded like lse2
+    w.dqacc = off;
+    off = align256(off + rows * 64 * 4);
+  }
   if (d.lse == nullptr) {  // recompute variant: the forward's lse and a scratch output
     w.lse = off;
     off = align256(off + (size_t)(d.batch * d.heads_q * d.seqlen_q) * 4);
@@ -1194,11 +1598,11 @@ int map_bf16(CUtensorMap* m, const void* base, int D, int64_t rows, int64_t head
 // serialization: the grid may start (set-up: barriers, TMEM, tensor maps) while
 // the previous one drains; the kernel orders its reads with grid_dep_wait.
 template <class... KArgs, class... Args>
-cudaError_t launch_overlapped(void (*kernel)(KArgs...), int64_t grid, int smem, cudaStream_t stream,
+cudaError_t launch_overlapped(void (*kernel)(KArgs...), int64_t grid, int threads, int smem, cudaStream_t stream,
                               Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1230,7 +1634,8 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(d.o), static_cast<const __nv_bfloat16*>(d.dout), lse, lse2, dsum,
         d.o_stride[0], d.o_stride[1], d.o_stride[2], d.do_stride[0], d.do_stride[1], d.do_stride[2],
-        (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (int)d.head_dim_v, rows, tpr, vec ? 1 : 0, ctr);
+        (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (int)d.head_dim_v, rows, tpr, vec ? 1 : 0, ctr,
+        D == 64 ? reinterpret_cast<float*>(ws + w.dqacc) : nullptr);
     if (int st = cuda_status(cudaGetLastError(), "bwd prep launch")) return st;
   }
   // dK/dV kernel: 64-row query tiles, 128-key blocks; dQ kernel: 128-row query blocks, 64-key tiles
@@ -1265,6 +1670,40 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
   const int need_q = 2 * (128 * D * 2) + kStages * 2 * (KT * D * 2) + 256 + 1024;
   const int smem_kv = need_kv > 120 * 1024 ? need_kv : 120 * 1024;
   const int smem_q = need_q > 120 * 1024 ? need_q : 120 * 1024;
+  if (D == 64) {  // one fused pass for dK, dV and dQ, then dQ scaled and rounded
+    float* dqacc = reinterpret_cast<float*>(ws + w.dqacc);
+    CUtensorMap tdq;
+    {
+      const uint64_t dims[4] = {64, (uint64_t)tpad, (uint64_t)d.heads_q, (uint64_t)d.batch};
+      const uint64_t str[3] = {64 * 4, (uint64_t)tpad * 64 * 4, (uint64_t)(tpad * d.heads_q) * 64 * 4};
+      const uint32_t box[4] = {32, 128, 1, 1};
+      if (int st = encode_tma_4d(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dqacc, dims, str, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B))
+        return st;
+    }
+    p.out0 = d.dk;
+    p.out1 = d.dv;
+    for (int i = 0; i < 3; ++i) {
+      p.s0[i] = d.dk_stride[i];
+      p.s1[i] = d.dv_stride[i];
+    }
+    p.n_blocks = (int)((d.seqlen_k + 127) / 128);
+    p.ctr = ctr;
+    const int64_t grid = (int64_t)p.n_blocks * d.heads_kv * d.batch;
+    const int smem = 12 * 16384 + kStagesF * 1024 + (int)sizeof(BarsF) + 1024;
+    cudaError_t e = cudaFuncSetAttribute(bwd_fused64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_status(e, "bwd fused64 smem attribute");
+    const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
+    e = launch_overlapped(bwd_fused64_kernel, pgrid, kFusedThreads, smem, stream, tq128, tk128, tv128, tdo128, tdq,
+                          p);
+    if (e != cudaSuccess) return cuda_status(e, "bwd fused64 launch");
+    const int64_t n = d.batch * d.heads_q * d.seqlen_q * 8;
+    e = launch_overlapped(bwd_dq_convert_kernel, (n + 255) / 256, 256, 0, stream, (const float*)dqacc,
+                          static_cast<__nv_bfloat16*>(d.dq), d.dq_stride[0], d.dq_stride[1], d.dq_stride[2],
+                          (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (float)d.scale, n);
+    if (e != cudaSuccess) return cuda_status(e, "bwd dq convert launch");
+    return PDB_OK;
+  }
   {  // dK, dV
     p.out0 = d.dk;
     p.out1 = d.dv;
@@ -1280,14 +1719,14 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       if (e != cudaSuccess) return cuda_status(e, "bwd dkdv64 smem attribute");
       p.ctr = ctr;
       const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      e = launch_overlapped(bwd_dkdv64_kernel, pgrid, smem, stream, tq128, tk128, tv128, tdo128, p);
+      e = launch_overlapped(bwd_dkdv64_kernel, pgrid, kThreads, smem, stream, tq128, tk128, tv128, tdo128, p);
       if (e != cudaSuccess) return cuda_status(e, "bwd dkdv64 launch");
     } else {
       cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
       if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
       p.ctr = ctr;
       const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      e = launch_overlapped(bwd_dkdv_kernel<D>, pgrid, smem_kv, stream, tq64, tk128, tv128, tdo64, p);
+      e = launch_overlapped(bwd_dkdv_kernel<D>, pgrid, kThreads, smem_kv, stream, tq64, tk128, tv128, tdo64, p);
       if (e != cudaSuccess) return cuda_status(e, "bwd dkdv launch");
     }
     if (int st = cuda_status(cudaGetLastError(), "bwd dkdv launch")) return st;
@@ -1304,14 +1743,14 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       if (e != cudaSuccess) return cuda_status(e, "bwd dq64 smem attribute");
       p.ctr = ctr;
       const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      e = launch_overlapped(bwd_dq64_kernel, pgrid, smem, stream, tq128, tk128, tv128, tdo128, p);
+      e = launch_overlapped(bwd_dq64_kernel, pgrid, kThreads, smem, stream, tq128, tk128, tv128, tdo128, p);
       if (e != cudaSuccess) return cuda_status(e, "bwd dq64 launch");
     } else {
       cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
       if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
       p.ctr = ctr;
       const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      e = launch_overlapped(bwd_dq_kernel<D>, pgrid, smem_q, stream, tq128, tk64, tv64, tdo128, p);
+      e = launch_overlapped(bwd_dq_kernel<D>, pgrid, kThreads, smem_q, stream, tq128, tk64, tv64, tdo128, p);
       if (e != cudaSuccess) return cuda_status(e, "bwd dq launch");
     }
     if (int st = cuda_status(cudaGetLastError(), "bwd dq launch")) return st;
