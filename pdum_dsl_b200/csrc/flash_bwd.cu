@@ -5,21 +5,27 @@
 // (partition.py:586-607) into: the flash forward with its (m, den)
 // artifacts, a held-back D = rowsum(dO * O) row statistic, and contraction
 // carves that re-derive P inside their sweep (partition.py:354-455).  This
-// file executes that plan as three kernels:
+// file executes that plan as:
 //
 //   bwd_prep     D[t] = sum_o dO[t,o] O[t,o] and nlse2[t] = -lse[t] * log2 e
 //                (rows padded to a multiple of 128 with nlse2 = -inf, D = 0,
 //                so padded query rows carry P = 0 without masks)
-//   bwd_dkdv     one CTA per (batch, KV head, 128-key block): for every query
-//                tile of every query head of the group it forms
-//                S^T = K Q^T and dP^T = V dO^T in TMEM, P^T = exp2(S^T c + nlse2),
+//   D = 64: bwd_fused64 (dK, dV and dQ in one persistent pass; dQ parts are
+//                added into an fp32 accumulator in L2 by TMA bulk reductions)
+//                and bwd_dq_convert (dQ = scale * accumulator, to bf16)
+//   D = 128: bwd_dkdv and bwd_dq, two persistent passes:
+//   bwd_dkdv     per (batch, KV head, 128-key block): for every query tile of
+//                every query head of the group it forms S^T = K Q^T and
+//                dP^T = V dO^T in TMEM, P^T = exp2(S^T c + nlse2),
 //                dS^T = P^T (dP^T - D) (one thread per key row), writes both
 //                back to TMEM as bf16 and accumulates dV += P^T dO,
 //                dK += dS^T Q in TMEM; GQA sums over the group in place.
-//   bwd_dq       one CTA per (batch, head, 128-row block): S = Q K^T,
-//                dP = dO V^T, dS = P (dP - D), dQ += dS K over the key tiles.
-// dQ = scale dS K, dK = scale dS^T Q; everything accumulates in fp32 (TMEM)
-// and is rounded to bf16 once.  No atomics: the result is deterministic.
+//   bwd_dq       per (batch, head, 128-row block): S = Q K^T, dP = dO V^T,
+//                dS = P (dP - D), dQ += dS K over the key tiles.
+// dQ = scale dS K, dK = scale dS^T Q; everything accumulates in fp32 (TMEM,
+// and for the fused pass's dQ, fp32 in L2) and is rounded to bf16 once.  The
+// D = 128 passes use no atomics (bit-reproducible); the fused pass's dQ sums
+// its per-key-block parts in whatever order the reductions land.
 #include <cfloat>
 #include <mutex>
 #include <utility>
@@ -615,505 +621,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// D = 64 backward with 128-wide score tiles and overlapped accumulation.
-// With D = 64 the score MMAs (N = 128) are full-width; the accumulations
-// (dV, dK, dQ: N = 64) are not, so the schedule overlaps them with the
-// next item's score math: P / dS of item i are copied to a TMEM staging area,
-// which frees the S / dP columns for item i+1's score MMAs; those are issued
-// as soon as every compute warp holds item i's S / dP in registers (s_free),
-// before the accumulations of item i, and the compute warpgroups work on item
-// i+1 while the tensor core accumulates item i.
-struct __align__(8) Bars64P {
-  uint64_t fixed_full[2], fixed_empty[2];  // K/V (dK/dV kernel) or Q/dO (dQ kernel), per buffer
-  uint64_t op_full[kStages], op_empty[kStages];  // streamed operand ring
-  uint64_t s_full, s_free, p_full, stage_free, o_full, acc_free;
-  UnitQueue uq;
-  uint32_t tmem_base;
-  int abort;
-};
-
-// dK/dV, D = 64.  Unit = 128 keys of one (batch, KV head); items = (query head,
-// 128-row query tile).  TMEM: S^T [0,128)  dP^T [128,256)  staging P^T
-// [256,320) dS^T [320,384)  dV [384,448)  dK [448,512).  Compute warpgroup w
-// owns query columns [64w, 64w+64) of each item.
-__global__ void __launch_bounds__(kThreads, 1)
-    bwd_dkdv64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                      const BwdParams p) {
-  constexpr int D = 64;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kT = 128 * D * 2;  // any 128-row tile (16 KB)
-  constexpr uint32_t kBox = 128 * 128;
-  uint8_t* sKV = smem;                   // 2 buffers x (K, V)
-  uint8_t* sQ = smem + 4 * kT;           // kStages
-  uint8_t* sDO = sQ + kStages * kT;      // kStages
-  float* sVec = reinterpret_cast<float*>(sDO + kStages * kT);  // kStages x (nlse2[128], dsum[128])
-  Bars64P* bar = reinterpret_cast<Bars64P*>(reinterpret_cast<uint8_t*>(sVec) + kStages * 2 * 128 * 4);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int group = p.H / p.HKV;
-  const int n_qt = p.Tpad / 128;
-  const int n_bh = p.B * p.HKV;
-  const int n_units = p.n_blocks * n_bh;
-  // unit u: key block u / n_bh (ascending block = descending work under the causal mask)
-  auto unit_info = [&](int u, int& b, int& hk, int& s0, int& qt0, int& per_head) {
-    const int nblk = u / n_bh, bhk = u % n_bh;
-    b = bhk / p.HKV;
-    hk = bhk % p.HKV;
-    s0 = nblk * 128;
-    qt0 = 0;
-    if (p.causal) {
-      const int first = s0 - p.q_start;
-      qt0 = first > 0 ? first / 128 : 0;
-    }
-    per_head = n_qt - qt0 > 0 ? n_qt - qt0 : 0;
-  };
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar->fixed_full[i], 1);
-      mbar_init(&bar->fixed_empty[i], 1);
-      mbar_init(&bar->uq.full[i], 1);
-      mbar_init(&bar->uq.empty[i], 9);  // the MMA thread + 8 compute warps
-    }
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&bar->op_full[i], 1);
-      mbar_init(&bar->op_empty[i], 1);
-    }
-    mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->s_free, 8);  // one arrival per compute warp: S / dP read into registers
-    mbar_init(&bar->p_full, 8);  // one arrival per compute warp
-    mbar_init(&bar->stage_free, 1);
-    mbar_init(&bar->o_full, 1);
-    mbar_init(&bar->acc_free, 8);  // dK / dV read out of TMEM
-    bar->abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == 2) {
-    tmem_alloc(&bar->tmem_base, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  grid_dep_wait();    // the prologue (D, nlse2, zeroed counters) has completed
-  grid_dep_launch();  // the dQ grid may take SMs as this grid's CTAs retire
-  const uint32_t tmem = bar->tmem_base;
-  volatile int* abort = &bar->abort;
-  constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
-  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);
-
-  if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
-    if (warp == 0 && lane == 0) {
-      // ---------------------------------------------------------- producer
-      uint32_t gi = 0, nu = 0, nkv = 0;  // items loaded, units handed out, K/V buffers filled
-      for (;; ++nu) {
-        int u = atomicAdd(p.ctr, 1);
-        if (u >= n_units) u = -1;
-        if (fetch_unit(&bar->uq, nu, u, abort, p.err) < 0) break;
-        int b, hk, s0, qt0, per_head;
-        unit_info(u, b, hk, s0, qt0, per_head);
-        const int n_items = per_head * group;
-        if (n_items == 0) continue;
-        const int kb = nkv & 1;
-        if (!mbar_wait(&bar->fixed_empty[kb], ((nkv >> 1) & 1) ^ 1, abort, p.err)) break;
-        mbar_expect_tx(&bar->fixed_full[kb], 2 * kT);
-        tma_load_4d(sKV + kb * 2 * kT, &tm_k, &bar->fixed_full[kb], 0, s0, hk, b);
-        tma_load_4d(sKV + kb * 2 * kT + kT, &tm_v, &bar->fixed_full[kb], 0, s0, hk, b);
-        ++nkv;
-        bool ok = true;
-        for (int it = 0; it < n_items; ++it, ++gi) {
-          const int st = gi % kStages;
-          const int h = hk * group + it / per_head;
-          const int t0 = (qt0 + it % per_head) * 128;
-          if (!(ok = mbar_wait(&bar->op_empty[st], ((gi / kStages) & 1) ^ 1, abort, p.err))) break;
-          mbar_expect_tx(&bar->op_full[st], 2 * kT + 2 * 128 * 4);
-          tma_load_4d(sQ + st * kT, &tm_q, &bar->op_full[st], 0, t0, h, b);
-          tma_load_4d(sDO + st * kT, &tm_do, &bar->op_full[st], 0, t0, h, b);
-          const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
-          bulk_load(sVec + st * 256, p.nlse2 + vrow, 512, &bar->op_full[st]);
-          bulk_load(sVec + st * 256 + 128, p.dsum + vrow, 512, &bar->op_full[st]);
-        }
-        if (!ok) break;
-      }
-    } else if (warp == 1 && lane == 0) {
-      // -------------------------------------------------------- MMA issuer
-      uint32_t gi = 0, nu = 0, nkv = 0;  // items issued, units taken, units with items
-      bool ok = true;
-      for (;; ++nu) {
-        const int u = take_unit(&bar->uq, nu, abort, p.err, false);
-        if (u < 0) break;
-        int b, hk, s0, qt0, per_head;
-        unit_info(u, b, hk, s0, qt0, per_head);
-        const int n_items = per_head * group;
-        if (n_items == 0) continue;
-        const int kb = nkv & 1;
-        const uint32_t sK = smem_u32(sKV + kb * 2 * kT), sV = sK + kT;
-        if (!(ok = mbar_wait(&bar->fixed_full[kb], (nkv >> 1) & 1, abort, p.err))) break;
-        auto issue_s = [&](uint32_t g) -> bool {
-          const int st = g % kStages;
-          if (!mbar_wait(&bar->op_full[st], (g / kStages) & 1, abort, p.err)) return false;
-          tc_fence_after();
-          mma_kmajor<D>(tmem + 0, sK, kBox, smem_u32(sQ + st * kT), kBox, idS);     // S^T = K Q^T
-          mma_kmajor<D>(tmem + 128, sV, kBox, smem_u32(sDO + st * kT), kBox, idS);  // dP^T = V dO^T
-          tc_commit(&bar->s_full);
-          return true;
-        };
-        // S^T of the unit's first item overwrites the previous unit's last one: its
-        // compute warps must hold that in registers (s_free of item gi - 1)
-        if (gi > 0 && !(ok = mbar_wait(&bar->s_free, (gi - 1) & 1, abort, p.err))) break;
-        if (!(ok = issue_s(gi))) break;
-        for (int it = 0; ok && it < n_items; ++it) {
-          const uint32_t g = gi + it;
-          const int st = g % kStages;
-          if (it + 1 < n_items) {
-            // the next item's scores as soon as this item's S / dP sit in registers
-            if (!(ok = mbar_wait(&bar->s_free, g & 1, abort, p.err))) break;
-            tc_fence_after();
-            if (!(ok = issue_s(g + 1))) break;
-          }
-          if (!(ok = mbar_wait(&bar->p_full, g & 1, abort, p.err))) break;
-          // dV / dK of the previous unit must be read out before this unit's first accumulation
-          if (it == 0 && nkv > 0 && !(ok = mbar_wait(&bar->acc_free, (nkv - 1) & 1, abort, p.err))) break;
-          tc_fence_after();
-          mma_tmem_a<128>(tmem + 384, tmem + 256, smem_u32(sDO + st * kT), kBox, idG, it > 0);  // dV += P^T dO
-          mma_tmem_a<128>(tmem + 448, tmem + 320, smem_u32(sQ + st * kT), kBox, idG, it > 0);   // dK += dS^T Q
-          tc_commit(&bar->op_empty[st]);
-          tc_commit(&bar->stage_free);
-        }
-        if (!ok) break;
-        tc_commit(&bar->fixed_empty[kb]);  // every MMA reading this K/V buffer has been issued
-        tc_commit(&bar->o_full);
-        gi += n_items;
-        ++nkv;
-      }
-      // the last unit's s_free arrivals are never waited on: nothing reads S^T after them
-    }
-  } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
-    const int w = warp >= 8 ? 1 : 0;  // query-column half
-    const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const uint32_t tl = tmem + lane_off;
-    const float c = p.scale_log2;
-    const uint64_t c2 = f2_pack(c, c);
-    uint32_t gi = 0, nu = 0, nkv = 0;  // items computed, units taken, units with items
-    bool ok = true;
-    for (;; ++nu) {
-      const int u = take_unit(&bar->uq, nu, abort, p.err, true);
-      if (u < 0) break;
-      int b, hk, s0, qt0, per_head;
-      unit_info(u, b, hk, s0, qt0, per_head);
-      const int n_items = per_head * group;
-      const int s = s0 + row;
-      for (int it = 0; it < n_items; ++it) {
-        const uint32_t g = gi + it;
-        const int st = g % kStages;
-        const int t0 = (qt0 + it % per_head) * 128;
-        if (!(ok = mbar_wait(&bar->op_full[st], (g / kStages) & 1, abort, p.err))) break;
-        if (!(ok = mbar_wait(&bar->s_full, g & 1, abort, p.err))) break;
-        tc_fence_after();
-        const int lo = p.causal ? s - p.q_start - t0 - w * 64 : -(1 << 30);  // columns below lo are masked
-        uint32_t pp[32], dd[32];
-        // packed f32x2 math; the causal select only on items that cross the diagonal
-        const bool need_mask = __any_sync(0xffffffffu, lo > 0);
-        const uint32_t sl = smem_u32(sVec + st * 256 + w * 64), sd = smem_u32(sVec + st * 256 + 128 + w * 64);
-        uint32_t srr[64], drr[64];
-        tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(srr));
-        tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(srr + 32));
-        tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(drr));
-        tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(drr + 32));
-        tmem_wait_ld();
-        warp_arrive_after_tc(&bar->s_free);  // S^T / dP^T are in registers: the next scores may overwrite them
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const uint32_t* sr = srr + 32 * hf;
-          const uint32_t* dr = drr + 32 * hf;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 l4 = lds128(sl + 128 * hf + 16 * q);
-            const float4 d4 = lds128(sd + 128 * hf + 16 * q);
-#pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-              const int cc = 4 * q + 2 * h2, col = 32 * hf + cc;
-              const uint64_t s2 = (uint64_t)sr[cc] | ((uint64_t)sr[cc + 1] << 32);
-              const uint64_t g2 = (uint64_t)dr[cc] | ((uint64_t)dr[cc + 1] << 32);
-              const uint64_t l2 = h2 ? f2_pack(l4.z, l4.w) : f2_pack(l4.x, l4.y);
-              const uint64_t dd2 = h2 ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y);
-              float x0, x1;
-              f2_unpack(f2_fma(s2, c2, l2), x0, x1);
-              float p0 = ex2(x0), p1 = ex2(x1);
-              if (need_mask) {
-                p0 = col >= lo ? p0 : 0.f;
-                p1 = col + 1 >= lo ? p1 : 0.f;
-              }
-              float g0, g1;
-              f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(g2, dd2)), g0, g1);
-              pp[16 * hf + 2 * q + h2] = pack_bf16(p0, p1);
-              dd[16 * hf + 2 * q + h2] = pack_bf16(g0, g1);
-            }
-          }
-        }
-        // the staging area must be free of the previous item's accumulations
-        if (g > 0 && !(ok = mbar_wait(&bar->stage_free, (g - 1) & 1, abort, p.err))) break;
-        tc_fence_after();
-        tmem_st32(tl + 256 + w * 32, pp);
-        tmem_st32(tl + 320 + w * 32, dd);
-        tmem_wait_st();
-        warp_arrive_after_tc(&bar->p_full);
-      }
-      if (!ok) break;
-      const bool store = s < p.S;
-      __nv_bfloat16* dst = w == 0
-          ? static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] + (int64_t)s * p.s1[2]
-          : static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] + (int64_t)s * p.s0[2];
-      if (n_items == 0) {
-        if (store)
-          for (int i = 0; i < D; i += 8) *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
-        continue;
-      }
-      if (!(ok = mbar_wait(&bar->o_full, nkv & 1, abort, p.err))) break;
-      tc_fence_after();
-      store_cols_bf16<D>(tl + 384 + w * 64, w == 0 ? 1.0f : p.scale, dst, store);
-      warp_arrive_after_tc(&bar->acc_free);
-      gi += n_items;
-      ++nkv;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// dQ, D = 64.  Unit = 128 query rows of one (batch, head); items = 128-key
-// tiles.  TMEM: S [0,128)  dP [128,256)  staging dS [256,320)  dQ [320,384).
-// Compute warpgroup w owns key columns [64w, 64w+64).
-__global__ void __launch_bounds__(kThreads, 1)
-    bwd_dq64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                    const BwdParams p) {
-  constexpr int D = 64;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kT = 128 * D * 2;
-  constexpr uint32_t kBox = 128 * 128;
-  uint8_t* sQD = smem;                // 2 buffers x (Q, dO)
-  uint8_t* sK = smem + 4 * kT;        // kStages
-  uint8_t* sV = sK + kStages * kT;    // kStages
-  Bars64P* bar = reinterpret_cast<Bars64P*>(sV + kStages * kT);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_bh = p.B * p.H;
-  const int n_units = p.n_blocks * n_bh;
-  const int n_all = (p.S + 127) / 128;
-  // unit u: query block n_blocks - 1 - u / n_bh (the heaviest blocks first under the causal mask)
-  auto unit_info = [&](int u, int& b, int& h, int& t0, int& n_kv) {
-    const int mblk = p.n_blocks - 1 - u / n_bh, bh = u % n_bh;
-    b = bh / p.H;
-    h = bh % p.H;
-    t0 = mblk * 128;
-    n_kv = n_all;
-    if (p.causal) {
-      int last = t0 + 127;
-      if (last > p.T - 1) last = p.T - 1;
-      const int n = (last + p.q_start) / 128 + 1;
-      n_kv = n < n_all ? (n > 0 ? n : 0) : n_all;
-    }
-  };
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar->fixed_full[i], 1);
-      mbar_init(&bar->fixed_empty[i], 1);
-      mbar_init(&bar->uq.full[i], 1);
-      mbar_init(&bar->uq.empty[i], 9);  // the MMA thread + 8 compute warps
-    }
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&bar->op_full[i], 1);
-      mbar_init(&bar->op_empty[i], 1);
-    }
-    mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->s_free, 8);  // one arrival per compute warp: S / dP read into registers
-    mbar_init(&bar->p_full, 8);  // one arrival per compute warp
-    mbar_init(&bar->stage_free, 1);
-    mbar_init(&bar->o_full, 1);
-    mbar_init(&bar->acc_free, 8);  // dQ read out of TMEM
-    bar->abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == 2) {
-    tmem_alloc(&bar->tmem_base, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = bar->tmem_base;
-  volatile int* abort = &bar->abort;
-  constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
-  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);
-
-  if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
-    if (warp == 0 && lane == 0) {
-      // ---------------------------------------------------------- producer
-      uint32_t gi = 0, nu = 0, nqd = 0;  // items loaded, units handed out, Q/dO buffers filled
-      for (;; ++nu) {
-        int u = atomicAdd(p.ctr + 1, 1);
-        if (u >= n_units) u = -1;
-        if (fetch_unit(&bar->uq, nu, u, abort, p.err) < 0) break;
-        int b, h, t0, n_kv;
-        unit_info(u, b, h, t0, n_kv);
-        if (n_kv == 0) continue;
-        const int hk = h / (p.H / p.HKV);
-        const int qb = nqd & 1;
-        if (!mbar_wait(&bar->fixed_empty[qb], ((nqd >> 1) & 1) ^ 1, abort, p.err)) break;
-        mbar_expect_tx(&bar->fixed_full[qb], 2 * kT);
-        tma_load_4d(sQD + qb * 2 * kT, &tm_q, &bar->fixed_full[qb], 0, t0, h, b);
-        tma_load_4d(sQD + qb * 2 * kT + kT, &tm_do, &bar->fixed_full[qb], 0, t0, h, b);
-        ++nqd;
-        bool ok = true;
-        for (int j = 0; j < n_kv; ++j, ++gi) {
-          const int st = gi % kStages;
-          if (!(ok = mbar_wait(&bar->op_empty[st], ((gi / kStages) & 1) ^ 1, abort, p.err))) break;
-          mbar_expect_tx(&bar->op_full[st], 2 * kT);
-          tma_load_4d(sK + st * kT, &tm_k, &bar->op_full[st], 0, j * 128, hk, b);
-          tma_load_4d(sV + st * kT, &tm_v, &bar->op_full[st], 0, j * 128, hk, b);
-        }
-        if (!ok) break;
-      }
-    } else if (warp == 1 && lane == 0) {
-      // -------------------------------------------------------- MMA issuer
-      uint32_t gi = 0, nu = 0, nqd = 0;  // items issued, units taken, units with items
-      bool ok = true;
-      for (;; ++nu) {
-        const int u = take_unit(&bar->uq, nu, abort, p.err, false);
-        if (u < 0) break;
-        int b, h, t0, n_kv;
-        unit_info(u, b, h, t0, n_kv);
-        if (n_kv == 0) continue;
-        const int qb = nqd & 1;
-        const uint32_t sQ = smem_u32(sQD + qb * 2 * kT), sDO = sQ + kT;
-        if (!(ok = mbar_wait(&bar->fixed_full[qb], (nqd >> 1) & 1, abort, p.err))) break;
-        auto issue_s = [&](uint32_t g) -> bool {
-          const int st = g % kStages;
-          if (!mbar_wait(&bar->op_full[st], (g / kStages) & 1, abort, p.err)) return false;
-          tc_fence_after();
-          mma_kmajor<D>(tmem + 0, sQ, kBox, smem_u32(sK + st * kT), kBox, idS);     // S = Q K^T
-          mma_kmajor<D>(tmem + 128, sDO, kBox, smem_u32(sV + st * kT), kBox, idS);  // dP = dO V^T
-          tc_commit(&bar->s_full);
-          return true;
-        };
-        if (gi > 0 && !(ok = mbar_wait(&bar->s_free, (gi - 1) & 1, abort, p.err))) break;
-        if (!(ok = issue_s(gi))) break;
-        for (int j = 0; ok && j < n_kv; ++j) {
-          const uint32_t g = gi + j;
-          const int st = g % kStages;
-          if (j + 1 < n_kv) {
-            if (!(ok = mbar_wait(&bar->s_free, g & 1, abort, p.err))) break;
-            tc_fence_after();
-            if (!(ok = issue_s(g + 1))) break;
-          }
-          if (!(ok = mbar_wait(&bar->p_full, g & 1, abort, p.err))) break;
-          if (j == 0 && nqd > 0 && !(ok = mbar_wait(&bar->acc_free, (nqd - 1) & 1, abort, p.err))) break;
-          tc_fence_after();
-          mma_tmem_a<128>(tmem + 320, tmem + 256, smem_u32(sK + st * kT), kBox, idG, j > 0);  // dQ += dS K
-          tc_commit(&bar->op_empty[st]);
-          tc_commit(&bar->stage_free);
-        }
-        if (!ok) break;
-        tc_commit(&bar->fixed_empty[qb]);
-        tc_commit(&bar->o_full);
-        gi += n_kv;
-        ++nqd;
-      }
-    }
-  } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
-    const int w = warp >= 8 ? 1 : 0;
-    const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const uint32_t tl = tmem + lane_off;
-    const float c = p.scale_log2;
-    uint32_t gi = 0, nu = 0, nqd = 0;
-    bool ok = true;
-    for (;; ++nu) {
-      const int u = take_unit(&bar->uq, nu, abort, p.err, true);
-      if (u < 0) break;
-      int b, h, t0, n_kv;
-      unit_info(u, b, h, t0, n_kv);
-      const int t = t0 + row;
-      __nv_bfloat16* dq = static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)h * p.s0[1] +
-                          (int64_t)t * p.s0[2];
-      if (n_kv == 0) {  // no key is visible to these rows: dQ = 0
-        if (t < p.T)
-          for (int i = 0; i < 32; i += 8) *reinterpret_cast<uint4*>(dq + w * 32 + i) = make_uint4(0, 0, 0, 0);
-        continue;
-      }
-      const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t;
-      const float l2 = p.nlse2[vrow];  // -inf on padded rows -> P = 0
-      const float dsum = p.dsum[vrow];
-      const uint64_t c2 = f2_pack(c, c), nl2 = f2_pack(l2, l2), ds2 = f2_pack(dsum, dsum);
-      for (int j = 0; j < n_kv; ++j) {
-        const uint32_t g = gi + j;
-        if (!(ok = mbar_wait(&bar->s_full, g & 1, abort, p.err))) break;
-        tc_fence_after();
-        const int lim = p.causal ? t + p.q_start + 1 - j * 128 - w * 64 : (1 << 30);  // key columns >= lim masked
-        uint32_t sr[64], dr[64];
-        tmem_ld32(tl + w * 64, *reinterpret_cast<uint32_t(*)[32]>(sr));
-        tmem_ld32(tl + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-        tmem_ld32(tl + 128 + w * 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
-        tmem_ld32(tl + 128 + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
-        tmem_wait_ld();
-        warp_arrive_after_tc(&bar->s_free);
-        uint32_t dd[32];
-        const bool need_mask = __any_sync(0xffffffffu, lim < 64);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = 2 * i;
-          const uint64_t s2 = (uint64_t)sr[col] | ((uint64_t)sr[col + 1] << 32);
-          const uint64_t g2 = (uint64_t)dr[col] | ((uint64_t)dr[col + 1] << 32);
-          float x0, x1;
-          f2_unpack(f2_fma(s2, c2, nl2), x0, x1);
-          float p0 = ex2(x0), p1 = ex2(x1);
-          if (need_mask) {
-            p0 = col < lim ? p0 : 0.f;
-            p1 = col + 1 < lim ? p1 : 0.f;
-          }
-          float g0, g1;
-          f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(g2, ds2)), g0, g1);
-          dd[i] = pack_bf16(g0, g1);
-        }
-        if (g > 0 && !(ok = mbar_wait(&bar->stage_free, (g - 1) & 1, abort, p.err))) break;
-        tc_fence_after();
-        tmem_st32(tl + 256 + w * 32, dd);
-        tmem_wait_st();
-        warp_arrive_after_tc(&bar->p_full);
-      }
-      if (!ok) break;
-      if (!(ok = mbar_wait(&bar->o_full, nqd & 1, abort, p.err))) break;
-      tc_fence_after();
-      store_cols_bf16<32>(tl + 320 + w * 32, p.scale, dq + w * 32, t < p.T);
-      warp_arrive_after_tc(&bar->acc_free);
-      gi += n_kv;
-      ++nqd;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-  grid_dep_wait();  // complete only after the dK/dV grid this one overlapped has completed
-}
-
-// ---------------------------------------------------------------------------
 // Fused D = 64 backward: dK, dV and dQ in one persistent pass.
 // The dK/dV schedule above (unit = 128 keys of one (batch, KV head), items =
 // (query head, 128-row query tile)) plus, per item, the dQ contribution of the
@@ -1127,14 +634,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // accumulator of config-5-sized problems fits there).  A final kernel scales
 // and rounds the accumulator to bf16.  dQ then depends on the order of the
 // fp32 additions (not bit-reproducible run to run); dK and dV do not.
-constexpr int kStagesF = 2;
+constexpr int kStagesF = 3;
 constexpr int kFusedThreads = 512;  // warps 0..3 control, 4..11 compute, 12..15 dQ drain
 
 struct __align__(8) BarsF {
   uint64_t fixed_full[2], fixed_empty[2];          // K/V per buffer
   uint64_t op_full[kStagesF], op_empty[kStagesF];  // Q/dO ring
   uint64_t s_full, s_free, p_full, stage_free, o_full, acc_free;
-  uint64_t dq_full, dq_free, stg_full, stg_free;   // dQ_part TMEM -> drain -> staging -> bulk reduce
+  uint64_t dq_full, dq_free;                       // dQ_part in TMEM -> drain warps
   UnitQueue uq;
   uint32_t tmem_base;
   int abort;
@@ -1157,8 +664,8 @@ __device__ __forceinline__ void sts128(uint32_t saddr, uint32_t a, uint32_t b, u
 
 // TMEM: S^T [0,128)  dP^T [128,256)  staging P^T [256,320)  dQ_part [320,384)
 // dV [384,448)  dK [448,512).  Shared memory: K/V x 2 buffers, Q/dO x
-// kStagesF, nlse2/dsum rows, dS^T (two 16 KB halves of 64 queries), dQ staging
-// (two 16 KB boxes of 32 fp32 columns).
+// kStagesF, dS^T (two 16 KB halves of 64 queries), dQ staging (four 4 KB
+// boxes, one per drain warp), nlse2/dsum rows.
 __global__ void __launch_bounds__(kFusedThreads, 1)
     bwd_fused64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -1172,8 +679,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   uint8_t* sQ = smem + 4 * kT;               // kStagesF
   uint8_t* sDO = sQ + kStagesF * kT;         // kStagesF
   uint8_t* sDS = sDO + kStagesF * kT;        // dS^T, 2 x 16 KB
-  uint8_t* sDQ = sDS + 2 * kT;               // dQ staging, 2 x 16 KB
-  float* sVec = reinterpret_cast<float*>(sDQ + 2 * kT);  // kStagesF x (nlse2[128], dsum[128])
+  uint8_t* sDQ = sDS + 2 * kT;               // dQ staging, one 16 KB box
+  float* sVec = reinterpret_cast<float*>(sDQ + kT);  // kStagesF x (nlse2[128], dsum[128])
   BarsF* bar = reinterpret_cast<BarsF*>(reinterpret_cast<uint8_t*>(sVec) + kStagesF * 2 * 128 * 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int group = p.H / p.HKV;
@@ -1212,8 +719,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     mbar_init(&bar->acc_free, 8);
     mbar_init(&bar->dq_full, 1);
     mbar_init(&bar->dq_free, 4);   // drain warps: dQ_part in registers
-    mbar_init(&bar->stg_full, 4);  // drain warps: staging written
-    mbar_init(&bar->stg_free, 1);  // the reduction has read the staging
     bar->abort = 0;
     fence_barrier_init();
   }
@@ -1429,12 +934,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ dQ drain
+    // Each drain warp owns 32 query rows of dQ_part and a 4 KB staging box
+    // (32 rows x 32 fp32, 128-byte swizzled); per item it stages and reduces
+    // the two 32-column halves in turn, waiting only for its own previous
+    // reduction to have read the box.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");
     const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;  // query row of the item
     const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
-    const uint32_t stg = smem_u32(sDQ) + row * 128;
-    const bool issuer = warp == 12 && lane == 0;
+    const uint32_t box = smem_u32(sDQ) + q4 * 4096;
+    const uint32_t stg = box + lane * 128;
     uint32_t gi = 0, nu = 0;
     bool ok = true;
     for (;; ++nu) {
@@ -1446,40 +954,32 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       for (int it = 0; it < n_items; ++it) {
         const uint32_t g = gi + it;
         const int h = hk * group + it / per_head;
-        const int t0 = (qt0 + it % per_head) * 128;
+        const int t0 = (qt0 + it % per_head) * 128 + q4 * 32;
         if (!(ok = mbar_wait(&bar->dq_full, g & 1, abort, p.err))) break;
         tc_fence_after();
-        // the previous reduction must have read the staging buffer
-        if (!(ok = mbar_wait(&bar->stg_free, (g & 1) ^ 1, abort, p.err))) break;
-#pragma unroll
-        for (int bx = 0; bx < 2; ++bx) {  // 32 columns (one staging box) at a time
+#pragma unroll 1
+        for (int bx = 0; bx < 2; ++bx) {
           uint32_t r[32];
           tmem_ld32(tl + 320 + 32 * bx, r);
           tmem_wait_ld();
           if (bx == 1) warp_arrive_after_tc(&bar->dq_free);  // dQ_part is out of TMEM
+          if (lane == 0) bulk_wait_read_all();  // the previous reduction has read the box
+          __syncwarp();
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch)
-            sts128(stg + bx * kT + ((ch ^ (row & 7)) << 4), r[4 * ch], r[4 * ch + 1], r[4 * ch + 2], r[4 * ch + 3]);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar->stg_full);
-        if (warp == 12) {  // lane 0 issues the item's two bulk reductions
-          bool good = true;
-          if (issuer && (good = mbar_wait(&bar->stg_full, g & 1, abort, p.err))) {
-            tma_reduce_add_4d(&tm_dqacc, smem_u32(sDQ), 0, t0, h, b);
-            tma_reduce_add_4d(&tm_dqacc, smem_u32(sDQ) + kT, 32, t0, h, b);
+            sts128(stg + ((ch ^ (lane & 7)) << 4), r[4 * ch], r[4 * ch + 1], r[4 * ch + 2], r[4 * ch + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_4d(&tm_dqacc, box, 32 * bx, t0, h, b);
             bulk_commit();
-            bulk_wait_read_all();
-            mbar_arrive(&bar->stg_free);
           }
-          if (!(ok = __shfl_sync(0xffffffffu, good ? 1 : 0, 0) != 0)) break;
         }
       }
       if (!ok) break;
       gi += n_items;
     }
-    if (issuer) bulk_wait_all();  // the reductions are complete before the CTA retires
+    if (lane == 0) bulk_wait_all();  // the reductions are complete before the CTA retires
   }
   tc_fence_before();
   __syncthreads();
@@ -1639,15 +1139,11 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     if (int st = cuda_status(cudaGetLastError(), "bwd prep launch")) return st;
   }
   // dK/dV kernel: 64-row query tiles, 128-key blocks; dQ kernel: 128-row query blocks, 64-key tiles
-  CUtensorMap tq64, tdo64, tk128, tv128, tq128, tdo128, tk64, tv64;
-  if (int st = map_bf16(&tq64, d.q, D, d.seqlen_q, d.heads_q, d.batch, d.q_stride, QT)) return st;
-  if (int st = map_bf16(&tdo64, d.dout, D, d.seqlen_q, d.heads_q, d.batch, d.do_stride, QT)) return st;
+  CUtensorMap tk128, tv128, tq128, tdo128;
   if (int st = map_bf16(&tk128, d.k, D, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, 128)) return st;
   if (int st = map_bf16(&tv128, d.v, D, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, 128)) return st;
   if (int st = map_bf16(&tq128, d.q, D, d.seqlen_q, d.heads_q, d.batch, d.q_stride, 128)) return st;
   if (int st = map_bf16(&tdo128, d.dout, D, d.seqlen_q, d.heads_q, d.batch, d.do_stride, 128)) return st;
-  if (int st = map_bf16(&tk64, d.k, D, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, KT)) return st;
-  if (int st = map_bf16(&tv64, d.v, D, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, KT)) return st;
   BwdParams p{};
   p.nlse2 = lse2;
   p.dsum = dsum;
@@ -1670,13 +1166,13 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
   const int need_q = 2 * (128 * D * 2) + kStages * 2 * (KT * D * 2) + 256 + 1024;
   const int smem_kv = need_kv > 120 * 1024 ? need_kv : 120 * 1024;
   const int smem_q = need_q > 120 * 1024 ? need_q : 120 * 1024;
-  if (D == 64) {  // one fused pass for dK, dV and dQ, then dQ scaled and rounded
+  if constexpr (D == 64) {  // one fused pass for dK, dV and dQ, then dQ scaled and rounded
     float* dqacc = reinterpret_cast<float*>(ws + w.dqacc);
     CUtensorMap tdq;
     {
       const uint64_t dims[4] = {64, (uint64_t)tpad, (uint64_t)d.heads_q, (uint64_t)d.batch};
       const uint64_t str[3] = {64 * 4, (uint64_t)tpad * 64 * 4, (uint64_t)(tpad * d.heads_q) * 64 * 4};
-      const uint32_t box[4] = {32, 128, 1, 1};
+      const uint32_t box[4] = {32, 32, 1, 1};
       if (int st = encode_tma_4d(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dqacc, dims, str, box,
                                  CU_TENSOR_MAP_SWIZZLE_128B))
         return st;
@@ -1690,7 +1186,7 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     p.n_blocks = (int)((d.seqlen_k + 127) / 128);
     p.ctr = ctr;
     const int64_t grid = (int64_t)p.n_blocks * d.heads_kv * d.batch;
-    const int smem = 12 * 16384 + kStagesF * 1024 + (int)sizeof(BarsF) + 1024;
+    const int smem = (7 + 2 * kStagesF) * 16384 + kStagesF * 1024 + (int)sizeof(BarsF) + 1024;
     cudaError_t e = cudaFuncSetAttribute(bwd_fused64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_status(e, "bwd fused64 smem attribute");
     const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
@@ -1703,59 +1199,49 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
                           (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (float)d.scale, n);
     if (e != cudaSuccess) return cuda_status(e, "bwd dq convert launch");
     return PDB_OK;
-  }
-  {  // dK, dV
-    p.out0 = d.dk;
-    p.out1 = d.dv;
-    for (int i = 0; i < 3; ++i) {
-      p.s0[i] = d.dk_stride[i];
-      p.s1[i] = d.dv_stride[i];
+  } else {
+    CUtensorMap tq64, tdo64, tk64, tv64;  // 64-row boxes: dK/dV query items, dQ key items
+    if (int st = map_bf16(&tq64, d.q, D, d.seqlen_q, d.heads_q, d.batch, d.q_stride, QT)) return st;
+    if (int st = map_bf16(&tdo64, d.dout, D, d.seqlen_q, d.heads_q, d.batch, d.do_stride, QT)) return st;
+    if (int st = map_bf16(&tk64, d.k, D, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, KT)) return st;
+    if (int st = map_bf16(&tv64, d.v, D, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, KT)) return st;
+    {  // dK, dV
+      p.out0 = d.dk;
+      p.out1 = d.dv;
+      for (int i = 0; i < 3; ++i) {
+        p.s0[i] = d.dk_stride[i];
+        p.s1[i] = d.dv_stride[i];
+      }
+      p.n_blocks = (int)((d.seqlen_k + 127) / 128);
+      const int64_t grid = (int64_t)p.n_blocks * d.heads_kv * d.batch;
+      {
+        cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
+        if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
+        p.ctr = ctr;
+        const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
+        e = launch_overlapped(bwd_dkdv_kernel<D>, pgrid, kThreads, smem_kv, stream, tq64, tk128, tv128, tdo64, p);
+        if (e != cudaSuccess) return cuda_status(e, "bwd dkdv launch");
+      }
+      if (int st = cuda_status(cudaGetLastError(), "bwd dkdv launch")) return st;
     }
-    p.n_blocks = (int)((d.seqlen_k + 127) / 128);
-    const int64_t grid = (int64_t)p.n_blocks * d.heads_kv * d.batch;
-    if (D == 64) {  // persistent: one CTA per SM takes key blocks from ctr[0]
-      const int smem = 4 * 16384 + kStages * 2 * 16384 + kStages * 1024 + (int)sizeof(Bars64P) + 1024;
-      cudaError_t e = cudaFuncSetAttribute(bwd_dkdv64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return cuda_status(e, "bwd dkdv64 smem attribute");
-      p.ctr = ctr;
-      const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      e = launch_overlapped(bwd_dkdv64_kernel, pgrid, kThreads, smem, stream, tq128, tk128, tv128, tdo128, p);
-      if (e != cudaSuccess) return cuda_status(e, "bwd dkdv64 launch");
-    } else {
-      cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
-      if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
-      p.ctr = ctr;
-      const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      e = launch_overlapped(bwd_dkdv_kernel<D>, pgrid, kThreads, smem_kv, stream, tq64, tk128, tv128, tdo64, p);
-      if (e != cudaSuccess) return cuda_status(e, "bwd dkdv launch");
+    {  // dQ
+      p.out0 = d.dq;
+      p.out1 = nullptr;
+      for (int i = 0; i < 3; ++i) p.s0[i] = d.dq_stride[i];
+      p.n_blocks = (int)(tpad / 128);
+      const int64_t grid = (int64_t)p.n_blocks * d.heads_q * d.batch;
+      {
+        cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
+        if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
+        p.ctr = ctr;
+        const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
+        e = launch_overlapped(bwd_dq_kernel<D>, pgrid, kThreads, smem_q, stream, tq128, tk64, tv64, tdo128, p);
+        if (e != cudaSuccess) return cuda_status(e, "bwd dq launch");
+      }
+      if (int st = cuda_status(cudaGetLastError(), "bwd dq launch")) return st;
     }
-    if (int st = cuda_status(cudaGetLastError(), "bwd dkdv launch")) return st;
+    return PDB_OK;
   }
-  {  // dQ
-    p.out0 = d.dq;
-    p.out1 = nullptr;
-    for (int i = 0; i < 3; ++i) p.s0[i] = d.dq_stride[i];
-    p.n_blocks = (int)(tpad / 128);
-    const int64_t grid = (int64_t)p.n_blocks * d.heads_q * d.batch;
-    if (D == 64) {  // persistent: one CTA per SM takes query blocks from ctr[1]
-      const int smem = 4 * 16384 + kStages * 2 * 16384 + (int)sizeof(Bars64P) + 1024;
-      cudaError_t e = cudaFuncSetAttribute(bwd_dq64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return cuda_status(e, "bwd dq64 smem attribute");
-      p.ctr = ctr;
-      const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      e = launch_overlapped(bwd_dq64_kernel, pgrid, kThreads, smem, stream, tq128, tk128, tv128, tdo128, p);
-      if (e != cudaSuccess) return cuda_status(e, "bwd dq64 launch");
-    } else {
-      cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
-      if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
-      p.ctr = ctr;
-      const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-      e = launch_overlapped(bwd_dq_kernel<D>, pgrid, kThreads, smem_q, stream, tq128, tk64, tv64, tdo128, p);
-      if (e != cudaSuccess) return cuda_status(e, "bwd dq launch");
-    }
-    if (int st = cuda_status(cudaGetLastError(), "bwd dq launch")) return st;
-  }
-  return PDB_OK;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -1764,6 +1250,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 }  // namespace pdb
 
 using namespace pdb;
+
 
 extern "C" size_t pdb_flash_bwd_workspace_size(const pdb_flash_bwd_desc* d) {
   if (!d || d->batch <= 0 || d->heads_q <= 0 || d->seqlen_q <= 0) return 0;
