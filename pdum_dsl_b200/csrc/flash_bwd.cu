@@ -779,39 +779,64 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       }
     } else if (warp == 1 && lane == 0) {
       // -------------------------------------------------------- MMA issuer
+      // The scores of the next unit's first item are issued at the last item of
+      // the current one (its K/V are already resident), so the compute warps
+      // move from unit to unit without waiting for the tensor core to drain.
       uint32_t gi = 0, nu = 0, nkv = 0;
       bool ok = true;
       const uint32_t sDSa = smem_u32(sDS);
-      for (;; ++nu) {
-        const int u = take_unit(&bar->uq, nu, abort, p.err, false);
-        if (u < 0) break;
-        int b, hk, s0, qt0, per_head;
-        unit_info(u, b, hk, s0, qt0, per_head);
-        const int n_items = per_head * group;
-        if (n_items == 0) continue;
+      int b, hk, s0, qt0, per_head, n_items = 0;
+      // the next unit that has items (units without any are taken and skipped)
+      auto next_unit = [&](int& ub, int& uhk, int& us0, int& uqt0, int& uper, int& un) -> int {
+        for (;;) {
+          const int u = take_unit(&bar->uq, nu++, abort, p.err, false);
+          if (u < 0) return u;  // -1: no more units, -2: gave up waiting
+          unit_info(u, ub, uhk, us0, uqt0, uper);
+          un = uper * group;
+          if (un > 0) return u;
+        }
+      };
+      auto issue_s = [&](uint32_t g, uint32_t sK, uint32_t sV) -> bool {
+        const int st = g % kStagesF;
+        if (!mbar_wait(&bar->op_full[st], (g / kStagesF) & 1, abort, p.err)) return false;
+        tc_fence_after();
+        mma_kmajor<D>(tmem + 0, sK, kBox, smem_u32(sQ + st * kT), kBox, idS);     // S^T = K Q^T
+        mma_kmajor<D>(tmem + 128, sV, kBox, smem_u32(sDO + st * kT), kBox, idS);  // dP^T = V dO^T
+        tc_commit(&bar->s_full);
+        return true;
+      };
+      int cur = next_unit(b, hk, s0, qt0, per_head, n_items);
+      if (cur >= 0) {
+        if ((ok = mbar_wait(&bar->fixed_full[0], 0, abort, p.err))) ok = issue_s(0, smem_u32(sKV), smem_u32(sKV) + kT);
+      }
+      while (ok && cur >= 0) {
         const int kb = nkv & 1;
-        const uint32_t sK = smem_u32(sKV + kb * 2 * kT), sV = sK + kT;
-        if (!(ok = mbar_wait(&bar->fixed_full[kb], (nkv >> 1) & 1, abort, p.err))) break;
-        auto issue_s = [&](uint32_t g) -> bool {
-          const int st = g % kStagesF;
-          if (!mbar_wait(&bar->op_full[st], (g / kStagesF) & 1, abort, p.err)) return false;
-          tc_fence_after();
-          mma_kmajor<D>(tmem + 0, sK, kBox, smem_u32(sQ + st * kT), kBox, idS);     // S^T = K Q^T
-          mma_kmajor<D>(tmem + 128, sV, kBox, smem_u32(sDO + st * kT), kBox, idS);  // dP^T = V dO^T
-          tc_commit(&bar->s_full);
-          return true;
-        };
-        if (gi > 0 && !(ok = mbar_wait(&bar->s_free, (gi - 1) & 1, abort, p.err))) break;
-        if (!(ok = issue_s(gi))) break;
+        const uint32_t sK = smem_u32(sKV + kb * 2 * kT);
+        int nb = 0, nhk = 0, ns0 = 0, nqt0 = 0, nper = 0, nn = 0, nxt = -1;
         for (int it = 0; ok && it < n_items; ++it) {
           const uint32_t g = gi + it;
           const int st = g % kStagesF;
-          if (it + 1 < n_items) {
+          if (it + 1 < n_items) {  // the next item's scores once this item's S / dP sit in registers
             if (!(ok = mbar_wait(&bar->s_free, g & 1, abort, p.err))) break;
             tc_fence_after();
-            if (!(ok = issue_s(g + 1))) break;
+            if (!(ok = issue_s(g + 1, sK, sK + kT))) break;
+          } else {  // last item: the next unit's first scores, on its (prefetched) K / V
+            nxt = next_unit(nb, nhk, ns0, nqt0, nper, nn);
+            if (nxt == -2) {
+              ok = false;
+              break;
+            }
+            if (nxt >= 0) {
+              const int nkb = (nkv + 1) & 1;
+              if (!(ok = mbar_wait(&bar->fixed_full[nkb], ((nkv + 1) >> 1) & 1, abort, p.err))) break;
+              if (!(ok = mbar_wait(&bar->s_free, g & 1, abort, p.err))) break;
+              tc_fence_after();
+              const uint32_t nK = smem_u32(sKV + nkb * 2 * kT);
+              if (!(ok = issue_s(g + 1, nK, nK + kT))) break;
+            }
           }
           if (!(ok = mbar_wait(&bar->p_full, g & 1, abort, p.err))) break;
+          // dV / dK of the previous unit must be read out before this unit's first accumulation
           if (it == 0 && nkv > 0 && !(ok = mbar_wait(&bar->acc_free, (nkv - 1) & 1, abort, p.err))) break;
           tc_fence_after();
           const uint32_t sQst = smem_u32(sQ + st * kT), sDOst = smem_u32(sDO + st * kT);
@@ -832,11 +857,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           tc_commit(&bar->dq_full);
         }
         if (!ok) break;
-        tc_commit(&bar->fixed_empty[kb]);
+        tc_commit(&bar->fixed_empty[kb]);  // every MMA reading this K/V buffer has been issued
         tc_commit(&bar->o_full);
         gi += n_items;
         ++nkv;
+        cur = nxt;
+        b = nb, hk = nhk, s0 = ns0, qt0 = nqt0, per_head = nper, n_items = nn;
       }
+      // the last item's s_free arrivals are never waited on: nothing reads S^T after them
     }
   } else if (warp < 12) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 176;" ::: "memory");
@@ -850,6 +878,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const uint32_t ds_row = smem_u32(sDS) + w * kT + row * 128;
     uint32_t gi = 0, nu = 0, nkv = 0;
     bool ok = true;
+    // dK / dV of a finished unit are read out of TMEM after the next unit's first
+    // item (whose scores the MMA thread issued ahead), not between the units
+    __nv_bfloat16* pend = nullptr;  // this thread's dV (w = 0) or dK (w = 1) row of the unit awaiting read-out
+    bool pend_store = false;
+    auto read_out = [&]() -> bool {
+      if (!mbar_wait(&bar->o_full, (nkv - 1) & 1, abort, p.err)) return false;
+      tc_fence_after();
+      store_cols_bf16<D>(tl + 384 + w * 64, w == 0 ? 1.0f : p.scale, pend, pend_store);
+      warp_arrive_after_tc(&bar->acc_free);
+      pend = nullptr;
+      return true;
+    };
     for (;; ++nu) {
       const int u = take_unit(&bar->uq, nu, abort, p.err, true);
       if (u < 0) break;
@@ -857,6 +897,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       unit_info(u, b, hk, s0, qt0, per_head);
       const int n_items = per_head * group;
       const int s = s0 + row;
+      const bool store = s < p.S;
+      __nv_bfloat16* dst = w == 0
+          ? static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] + (int64_t)s * p.s1[2]
+          : static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] + (int64_t)s * p.s0[2];
+      if (n_items == 0) {  // no query sees these keys: dK = dV = 0
+        if (store)
+          for (int i = 0; i < D; i += 8) *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
+        continue;
+      }
       for (int it = 0; it < n_items; ++it) {
         const uint32_t g = gi + it;
         const int st = g % kStagesF;
@@ -914,24 +963,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         fence_proxy_async_smem();
         tmem_wait_st();
         warp_arrive_after_tc(&bar->p_full);
+        if (it == 0 && pend != nullptr && !(ok = read_out())) break;  // the previous unit's dK / dV
       }
       if (!ok) break;
-      const bool store = s < p.S;
-      __nv_bfloat16* dst = w == 0
-          ? static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] + (int64_t)s * p.s1[2]
-          : static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] + (int64_t)s * p.s0[2];
-      if (n_items == 0) {
-        if (store)
-          for (int i = 0; i < D; i += 8) *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
-        continue;
-      }
-      if (!(ok = mbar_wait(&bar->o_full, nkv & 1, abort, p.err))) break;
-      tc_fence_after();
-      store_cols_bf16<D>(tl + 384 + w * 64, w == 0 ? 1.0f : p.scale, dst, store);
-      warp_arrive_after_tc(&bar->acc_free);
+      pend = dst;
+      pend_store = store;
       gi += n_items;
       ++nkv;
     }
+    if (ok && pend != nullptr) read_out();
   } else {
     // ------------------------------------------------------------ dQ drain
     // Each drain warp owns 32 query rows of dQ_part and a 4 KB staging box
