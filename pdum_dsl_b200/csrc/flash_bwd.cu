@@ -655,6 +655,12 @@ __device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, uint32
       "r"(smem_src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t smem_src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -669,7 +675,8 @@ __device__ __forceinline__ void sts128(uint32_t saddr, uint32_t a, uint32_t b, u
 __global__ void __launch_bounds__(kFusedThreads, 1)
     bwd_fused64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                       const __grid_constant__ CUtensorMap tm_dqacc, const BwdParams p) {
+                       const __grid_constant__ CUtensorMap tm_dqacc, const __grid_constant__ CUtensorMap tm_dk,
+                       const __grid_constant__ CUtensorMap tm_dv, const BwdParams p) {
   constexpr int D = 64;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -716,7 +723,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     mbar_init(&bar->p_full, 8);
     mbar_init(&bar->stage_free, 1);
     mbar_init(&bar->o_full, 1);
-    mbar_init(&bar->acc_free, 8);
+    mbar_init(&bar->acc_free, 4);  // drain warps: dV / dK read out of TMEM
     mbar_init(&bar->dq_full, 1);
     mbar_init(&bar->dq_free, 4);   // drain warps: dQ_part in registers
     bar->abort = 0;
@@ -876,20 +883,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const float c = p.scale_log2;
     const uint64_t c2 = f2_pack(c, c);
     const uint32_t ds_row = smem_u32(sDS) + w * kT + row * 128;
-    uint32_t gi = 0, nu = 0, nkv = 0;
+    uint32_t gi = 0, nu = 0;
     bool ok = true;
-    // dK / dV of a finished unit are read out of TMEM after the next unit's first
-    // item (whose scores the MMA thread issued ahead), not between the units
-    __nv_bfloat16* pend = nullptr;  // this thread's dV (w = 0) or dK (w = 1) row of the unit awaiting read-out
-    bool pend_store = false;
-    auto read_out = [&]() -> bool {
-      if (!mbar_wait(&bar->o_full, (nkv - 1) & 1, abort, p.err)) return false;
-      tc_fence_after();
-      store_cols_bf16<D>(tl + 384 + w * 64, w == 0 ? 1.0f : p.scale, pend, pend_store);
-      warp_arrive_after_tc(&bar->acc_free);
-      pend = nullptr;
-      return true;
-    };
     for (;; ++nu) {
       const int u = take_unit(&bar->uq, nu, abort, p.err, true);
       if (u < 0) break;
@@ -963,27 +958,24 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         fence_proxy_async_smem();
         tmem_wait_st();
         warp_arrive_after_tc(&bar->p_full);
-        if (it == 0 && pend != nullptr && !(ok = read_out())) break;  // the previous unit's dK / dV
       }
       if (!ok) break;
-      pend = dst;
-      pend_store = store;
       gi += n_items;
-      ++nkv;
     }
-    if (ok && pend != nullptr) read_out();
   } else {
-    // ------------------------------------------------------------ dQ drain
-    // Each drain warp owns 32 query rows of dQ_part and a 4 KB staging box
-    // (32 rows x 32 fp32, 128-byte swizzled); per item it stages and reduces
-    // the two 32-column halves in turn, waiting only for its own previous
-    // reduction to have read the box.
+    // ------------------------------------------------------- drain warps
+    // Each drain warp owns 32 TMEM lanes and a 4 KB staging box (32 rows x 128
+    // bytes, 128-byte swizzled).  Per item it stages the two 32-column halves of
+    // its 32 query rows of dQ_part in turn and adds each into the accumulator with
+    // a bulk reduction; per unit it stores its 32 key rows of dV and dK (bf16)
+    // with TMA stores.  It waits only for its own previous bulk operation to have
+    // read the box before refilling it.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");
     const int q4 = warp & 3;
     const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
     const uint32_t box = smem_u32(sDQ) + q4 * 4096;
     const uint32_t stg = box + lane * 128;
-    uint32_t gi = 0, nu = 0;
+    uint32_t gi = 0, nu = 0, nkv = 0;
     bool ok = true;
     for (;; ++nu) {
       const int u = take_unit(&bar->uq, nu, abort, p.err, true);
@@ -1017,9 +1009,44 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
       }
       if (!ok) break;
+      if (n_items > 0) {
+        // the unit's dV, then dK (scaled): this warp's 32 key rows, out of TMEM as
+        // bf16 into the staging box (one 128-byte row of 64 features per key) and
+        // to global memory by a TMA store, which also drops rows past the sequence
+        if (!(ok = mbar_wait(&bar->o_full, nkv & 1, abort, p.err))) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int t = 0; t < 2; ++t) {
+          const float mul = t == 0 ? 1.0f : p.scale;
+#pragma unroll 1
+          for (int hc = 0; hc < 2; ++hc) {
+            uint32_t r[32];
+            tmem_ld32(tl + 384 + 64 * t + 32 * hc, r);
+            tmem_wait_ld();
+            if (t == 1 && hc == 1) warp_arrive_after_tc(&bar->acc_free);  // dV / dK are out of TMEM
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * mul, __uint_as_float(r[2 * i + 1]) * mul);
+            if (hc == 0 && lane == 0) bulk_wait_read_all();  // the box's previous bulk operation has read it
+            __syncwarp();
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch)
+              sts128(stg + (((4 * hc + ch) ^ (lane & 7)) << 4), pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2],
+                     pk[4 * ch + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_4d(t == 0 ? &tm_dv : &tm_dk, box, 0, s0 + q4 * 32, hk, b);
+            bulk_commit();
+          }
+        }
+        ++nkv;
+      }
       gi += n_items;
     }
-    if (lane == 0) bulk_wait_all();  // the reductions are complete before the CTA retires
+    if (lane == 0) bulk_wait_all();  // the reductions and stores are complete before the CTA retires
   }
   tc_fence_before();
   __syncthreads();
@@ -1230,8 +1257,11 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     cudaError_t e = cudaFuncSetAttribute(bwd_fused64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_status(e, "bwd fused64 smem attribute");
     const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
+    CUtensorMap tdk32, tdv32;  // dK / dV stores: 32-row boxes, one per drain warp
+    if (int st = map_bf16(&tdk32, d.dk, D, d.seqlen_k, d.heads_kv, d.batch, d.dk_stride, 32)) return st;
+    if (int st = map_bf16(&tdv32, d.dv, D, d.seqlen_k, d.heads_kv, d.batch, d.dv_stride, 32)) return st;
     e = launch_overlapped(bwd_fused64_kernel, pgrid, kFusedThreads, smem, stream, tq128, tk128, tv128, tdo128, tdq,
-                          p);
+                          tdk32, tdv32, p);
     if (e != cudaSuccess) return cuda_status(e, "bwd fused64 launch");
     const int64_t n = d.batch * d.heads_q * d.seqlen_q * 8;
     e = launch_overlapped(bwd_dq_convert_kernel, (n + 255) / 256, 256, 0, stream, (const float*)dqacc,
