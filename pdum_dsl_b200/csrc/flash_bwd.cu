@@ -807,8 +807,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         const int st = g % kStagesF;
         if (!mbar_wait(&bar->op_full[st], (g / kStagesF) & 1, abort, p.err)) return false;
         tc_fence_after();
-        mma_kmajor<D>(tmem + 0, sK, kBox, smem_u32(sQ + st * kT), kBox, idS);     // S^T = K Q^T
-        mma_kmajor<D>(tmem + 128, sV, kBox, smem_u32(sDO + st * kT), kBox, idS);  // dP^T = V dO^T
+        // shared-memory descriptors advance by (byte offset >> 4) in their address field
+        const uint64_t dk = sdesc_sw128(sK, 16, 1024), dv = sdesc_sw128(sV, 16, 1024);
+        const uint64_t dq = sdesc_sw128(smem_u32(sQ + st * kT), 16, 1024);
+        const uint64_t ddo = sdesc_sw128(smem_u32(sDO + st * kT), 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)  // S^T = K Q^T
+          mma_ss(tmem + 0, dk + 2 * kk, dq + 2 * kk, idS, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)  // dP^T = V dO^T
+          mma_ss(tmem + 128, dv + 2 * kk, ddo + 2 * kk, idS, kk > 0 ? 1u : 0u);
         tc_commit(&bar->s_full);
         return true;
       };
@@ -847,18 +855,22 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           if (it == 0 && nkv > 0 && !(ok = mbar_wait(&bar->acc_free, (nkv - 1) & 1, abort, p.err))) break;
           tc_fence_after();
           const uint32_t sQst = smem_u32(sQ + st * kT), sDOst = smem_u32(sDO + st * kT);
-          mma_tmem_a<128>(tmem + 384, tmem + 256, sDOst, kBox, idG, it > 0);  // dV += P^T dO
+          const uint64_t bdo = sdesc_sw128(sDOst, kBox, 1024), bq = sdesc_sw128(sQst, kBox, 1024);
+          const uint64_t ads = sdesc_sw128(sDSa, 16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO  (A: P^T in TMEM, B: dO MN-major, 16 rows = 2048 B per step)
+            mma_ts(tmem + 384, tmem + 256 + kk * 8, bdo + 128 * kk, idG, (it > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q  (A: dS^T K-major, two 64-query halves)
-            mma_ss(tmem + 448, sdesc_sw128(sDSa + (kk >> 2) * kT + (kk & 3) * 32, 16, 1024),
-                   sdesc_sw128(sQst + kk * 2048, kBox, 1024), idG, (it > 0 || kk > 0) ? 1u : 0u);
+            mma_ss(tmem + 448, ads + (kk >> 2) * (kT >> 4) + (kk & 3) * 2, bq + 128 * kk, idG,
+                   (it > 0 || kk > 0) ? 1u : 0u);
           // dQ_part = dS K once the drain holds the previous item's part in registers
           if (g > 0 && !(ok = mbar_wait(&bar->dq_free, (g - 1) & 1, abort, p.err))) break;
           tc_fence_after();
+          const uint64_t adq = sdesc_sw128(sDSa, kT, 1024), bk = sdesc_sw128(sK, kBox, 1024);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)  // A: dS MN-major (query halves 16 KB apart), B: K MN-major
-            mma_ss(tmem + 320, sdesc_sw128(sDSa + kk * 2048, kT, 1024), sdesc_sw128(sK + kk * 2048, kBox, 1024), idQ,
-                   kk > 0 ? 1u : 0u);
+            mma_ss(tmem + 320, adq + 128 * kk, bk + 128 * kk, idQ, kk > 0 ? 1u : 0u);
           tc_commit(&bar->op_empty[st]);
           tc_commit(&bar->stage_free);
           tc_commit(&bar->dq_full);
