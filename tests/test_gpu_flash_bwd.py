@@ -108,7 +108,8 @@ def test_bwd_query_offset(cuda):
 
 
 @pytest.mark.parametrize("B,H,HKV,T,S,D", [(4, 16, 16, 1100, 1100, 128), (4, 32, 8, 1100, 1100, 128),
-                                           (4, 16, 4, 1100, 1100, 64), (2, 8, 8, 300, 1100, 128)])
+                                           (4, 16, 4, 1100, 1100, 64), (2, 8, 8, 300, 1100, 128),
+                                           (2, 8, 4, 300, 1100, 64)])
 def test_bwd_persistent_units_vs_oracle(cuda, B, H, HKV, T, S, D):
     """More work units than SMs (each persistent CTA takes several, light and heavy,
     across heads and KV groups), ragged tails, and key blocks no query row can see
@@ -138,3 +139,41 @@ def test_bwd_persistent_units_vs_oracle(cuda, B, H, HKV, T, S, D):
         assert_bf16(_np(gv[b:b + 1, hk:hk + 1]), rv, what=f"dv ({b},{hk})")
     if S > T:
         assert gk[:, :, T:].abs().max().item() == 0 and gv[:, :, T:].abs().max().item() == 0
+
+
+def test_bwd_strided_outputs_through_the_abi(cuda):
+    """dQ / dK / dV written into strided views (row stride 128 of a wider buffer)
+    through the C ABI equal the contiguous result; the bytes between rows stay
+    untouched (the D = 64 pass stores dK / dV with TMA and dQ with its own kernel)."""
+    import ctypes as C
+
+    import torch
+
+    from pdum_dsl_b200 import _lib, kernels
+
+    lib = _lib.load()
+    g = torch.Generator(device=cuda).manual_seed(77)
+    B, H, HKV, T, D = 2, 4, 2, 333, 64
+    q = torch.randn(B, H, T, D, device=cuda, generator=g).to(torch.bfloat16)
+    k, v = (torch.randn(B, HKV, T, D, device=cuda, generator=g).to(torch.bfloat16) for _ in range(2))
+    do = torch.randn(B, H, T, D, device=cuda, generator=g).to(torch.bfloat16)
+    o, lse = kernels.flash_attention(q, k, v, causal=True, return_lse=True)
+    ref = kernels.flash_attention_backward(q, k, v, o, do, lse, causal=True)
+    wide = [torch.full((*x.shape[:3], 2 * D), 7.0, device=cuda, dtype=torch.bfloat16) for x in (q, k, v)]
+    outs = [w[..., :D] for w in wide]
+    s3 = lambda t: _lib.I64x3(t.stride(0), t.stride(1), t.stride(2))
+    d = _lib.FlashBwdDesc()
+    d.q, d.k, d.v, d.o, d.dout, d.lse = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr()
+    d.dq, d.dk, d.dv = (x.data_ptr() for x in outs)
+    d.batch, d.heads_q, d.heads_kv, d.seqlen_q, d.seqlen_k, d.head_dim, d.head_dim_v = B, H, HKV, T, T, D, D
+    d.q_stride, d.k_stride, d.v_stride, d.o_stride, d.do_stride = s3(q), s3(k), s3(v), s3(o), s3(do)
+    d.dq_stride, d.dk_stride, d.dv_stride = (s3(x) for x in outs)
+    d.scale, d.causal, d.dtype = 1 / math.sqrt(D), 1, _lib.PDB_BF16
+    n = lib.pdb_flash_bwd_workspace_size(C.byref(d))
+    ws = torch.empty(n, dtype=torch.uint8, device=cuda)
+    d.workspace, d.workspace_bytes = ws.data_ptr(), n
+    _lib.check(lib.pdb_flash_bwd(C.byref(d), C.c_void_p(torch.cuda.current_stream().cuda_stream)), "pdb_flash_bwd")
+    kernels.check_device_errors()
+    for name, got, want, w in zip(("dq", "dk", "dv"), outs, ref, wide):
+        assert (got.float() - want.float()).abs().max().item() <= 2e-2, name
+        assert (w[..., D:] == 7.0).all(), f"{name}: bytes beyond the view were written"
