@@ -47,6 +47,7 @@ struct __align__(8) Barriers {
   uint64_t p_full[2];  // softmax -> MMA
   uint64_t o_full[2];  // last PV done -> epilogue
   uint64_t o_empty[2];  // epilogue read O -> next tile may accumulate
+  uint64_t stg_free[4];  // an O staging region has been read by its TMA stores (A, B take turns)
   uint32_t tmem_base;
   int abort;
 };
@@ -72,7 +73,10 @@ struct Smem {
   static constexpr int kQ1 = kTileBytes;
   static constexpr int kK = 2 * kTileBytes;  // 2 stages
   static constexpr int kV = 4 * kTileBytes;  // 2 stages
-  static constexpr int kBar = 6 * kTileBytes;
+  // O staging for the TMA-store epilogue: per TMEM lane quarter, D / 64 boxes of
+  // 32 rows x 64 bf16 (4 KB, 128-byte swizzled), shared by tiles A and B in turn
+  static constexpr int kStg = 6 * kTileBytes;
+  static constexpr int kBar = 7 * kTileBytes;
   static constexpr int kTotal = kBar + 1024 /*barriers*/ + 1024 /*alignment slack*/;
 };
 
@@ -143,7 +147,8 @@ __device__ __forceinline__ TileInfo tile_info(int tile, const FwdParams& p) {
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                           const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                           const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using L = Smem<D>;
@@ -165,6 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->o_empty[i], BM / 32);
     }
     bar->abort = 0;
+    for (int i = 0; i < 4; ++i) mbar_init(&bar->stg_free[i], 1);
     fence_barrier_init();
   }
   if (warp == 2) {
@@ -371,24 +377,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = 1.0f / l;
       const bool store = t < p.T;
       const int64_t bhq = (int64_t)ti.b * p.H + ti.h;
-      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.o) + (int64_t)ti.b * p.o_stride[0] +
-                            (int64_t)ti.h * p.o_stride[1] + (int64_t)t * p.o_stride[2];
+      // O / l as bf16 through this lane quarter's staging region (tiles A and B
+      // take turns: use n waits for use n - 1's stores to have read it) and TMA
+      // stores, which drop rows past T
+      const uint32_t stg = smem_u32(smem + L::kStg) + q4 * (D / 64) * 4096;
+      const uint32_t use = 2 * tt + x;
+      if (use > 0 && !(ok = mbar_wait(&bar->stg_free[q4], (use - 1) & 1, abort, p.err))) break;
 #pragma unroll
       for (int ch = 0; ch < D / 32; ++ch) {
         uint32_t r[32];
         tmem_ld32(tO + ch * 32, r);
         tmem_wait_ld();
+        if (ch == D / 32 - 1) warp_arrive_after_tc(&bar->o_empty[x]);  // O_x may now be overwritten by the next tile
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i)
           pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
-        if (store) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
+        const uint32_t rowb = stg + (ch >> 1) * 4096 + lane * 128;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-        }
+        for (int i = 0; i < 4; ++i)
+          sts128(rowb + ((((ch & 1) * 4 + i) ^ (lane & 7)) << 4), pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
-      warp_arrive_after_tc(&bar->o_empty[x]);  // O_x may now be overwritten by the next tile
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_store_4d(&tm_o, stg + bx * 4096, bx * 64, ti.t0 + x * BM + q4 * 32, ti.h, ti.b);
+        bulk_commit();
+        bulk_wait_read_all();
+        mbar_arrive(&bar->stg_free[q4]);
+      }
       if (store) {
         const int64_t idx = bhq * p.T + t;
         constexpr float kLn2 = 0.6931471805599453f;
@@ -397,6 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.den) p.den[idx] = l * ex2(m_used - m_true);
       }
     }
+    if (lane == 0) bulk_wait_all();  // the O stores are complete before the CTA retires
   }
   tc_fence_before();
   __syncthreads();
@@ -740,9 +760,17 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
     flash_fwd_d64_kernel<<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, p);
     return cuda_status(cudaGetLastError(), "bf16 flash launch");
   }
+  CUtensorMap to;  // O stores: 32-row boxes, one per softmax warp
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)d.seqlen_q, (uint64_t)d.heads_q, (uint64_t)d.batch};
+    const uint64_t so[3] = {(uint64_t)d.o_stride[2] * 2, (uint64_t)d.o_stride[1] * 2, (uint64_t)d.o_stride[0] * 2};
+    const uint32_t obox[4] = {64, 32, 1, 1};
+    if (int st = encode_tma_4d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.o, dims, so, obox, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+  }
   cudaError_t e = cudaFuncSetAttribute(flash_fwd_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_status(e, "bf16 flash: set smem attribute");
-  flash_fwd_sm100_kernel<D><<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, p);
+  flash_fwd_sm100_kernel<D><<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, to, p);
   return cuda_status(cudaGetLastError(), "bf16 flash launch");
 }
 
