@@ -1113,6 +1113,60 @@ __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_
   }
 }
 
+// The prologue for 64-wide rows (the fused D = 64 pass): each warp takes 8 rows
+// per step (8 lanes per row, one 16-byte chunk of O and of dO each, two rows
+// per lane in flight) over a grid-stride loop sized to the resident warps, and
+// zeroes the rows' fp32 dQ accumulator.
+__global__ void __launch_bounds__(256) bwd_prep64_kernel(
+    const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout, const float* __restrict__ lse,
+    float* __restrict__ lse2, float* __restrict__ dsum, int64_t so0, int64_t so1, int64_t so2, int64_t sd0,
+    int64_t sd1, int64_t sd2, int H, int T, int Tpad, int64_t rows, int* ctr, float* __restrict__ dqacc) {
+  if (blockIdx.x == 0 && threadIdx.x < 2) ctr[threadIdx.x] = 0;
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 8; base < rows;
+       base += nwarps * 8) {
+    int64_t r[2];
+    int t[2];
+    uint4 a[2], g[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      r[u] = base + 4 * u + (lane >> 3);
+      t[u] = (int)(r[u] % Tpad);
+      a[u] = g[u] = make_uint4(0, 0, 0, 0);
+      if (r[u] < rows && t[u] < T) {
+        const int64_t bh = r[u] / Tpad;
+        const int b = (int)(bh / H), h = (int)(bh % H);
+        a[u] = *reinterpret_cast<const uint4*>(o + b * so0 + h * so1 + t[u] * so2 + sub * 8);
+        g[u] = *reinterpret_cast<const uint4*>(dout + b * sd0 + h * sd1 + t[u] * sd2 + sub * 8);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (r[u] < rows) {
+        float4* z = reinterpret_cast<float4*>(dqacc + r[u] * 64 + sub * 8);
+        z[0] = z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a[u]);
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g[u]);
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 fa = __bfloat1622float2(a2[i]), fg = __bfloat1622float2(g2[i]);
+        acc = fmaf(fa.x, fg.x, fmaf(fa.y, fg.y, acc));
+      }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      if (sub == 0 && r[u] < rows) {
+        const bool live = t[u] < T;
+        dsum[r[u]] = live ? acc : 0.f;
+        lse2[r[u]] = live ? -lse[(r[u] / Tpad) * T + t[u]] * kLog2e : -INFINITY;
+      }
+    }
+  }
+}
+
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct WsLayout {
@@ -1173,6 +1227,8 @@ cudaError_t launch_overlapped(void (*kernel)(KArgs...), int64_t grid, int thread
 
 template <int D>
 int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
   uint8_t* ws = static_cast<uint8_t*>(d.workspace);
   const int64_t tpad = (d.seqlen_q + BT - 1) / BT * BT;
   float* lse2 = reinterpret_cast<float*>(ws + w.lse2);
@@ -1189,6 +1245,15 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       while (tpr < 32 && tpr * 8 < d.head_dim_v) tpr *= 2;
     }
     const int64_t threads = rows * tpr;
+    if (D == 64 && vec) {
+      int64_t blocks = (rows + 63) / 64;
+      const int64_t resident = 8LL * sm_count(dev);
+      if (blocks > resident) blocks = resident;
+      bwd_prep64_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(d.o), static_cast<const __nv_bfloat16*>(d.dout), lse, lse2, dsum,
+          d.o_stride[0], d.o_stride[1], d.o_stride[2], d.do_stride[0], d.do_stride[1], d.do_stride[2],
+          (int)d.heads_q, (int)d.seqlen_q, (int)tpad, rows, ctr, reinterpret_cast<float*>(ws + w.dqacc));
+    } else
     bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(d.o), static_cast<const __nv_bfloat16*>(d.dout), lse, lse2, dsum,
         d.o_stride[0], d.o_stride[1], d.o_stride[2], d.do_stride[0], d.do_stride[1], d.do_stride[2],
@@ -1216,8 +1281,6 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
   p.scale_log2 = (float)(d.scale * 1.4426950408889634);
   p.B = (int)d.batch;
   p.err = device_error_flag();
-  int dev = 0;
-  cudaGetDevice(&dev);
   // the kernels are persistent (one CTA per SM); >= 120 KB of shared memory also keeps a
   // second CTA of another launch off the SM while the 512-column TMEM allocation is held
   const int need_kv = 2 * (128 * D * 2) + kStages * 2 * (QT * D * 2) + kStages * 2 * QT * 4 + 256 + 1024;
