@@ -113,10 +113,12 @@ int pdb_flash_fwd(const pdb_flash_desc* d, void* stream);
  *   P = exp(scale*q.k - lse),  D = rowsum(dO * o)        ("held-back D")
  *   dV = P^T dO,  dS = P * (dO.V^T - D),  dQ = scale * dS K,  dK = scale * dS^T Q.
  * dq/dk/dv share the layouts of q/k/v (GQA: dk/dv are summed over the group).
- * Workspace (float32) holds D and the dQ accumulator; its size in bytes comes
- * from pdb_flash_bwd_workspace_size.  If lse is NULL the kernel recomputes it
- * (the "recompute" variant of the template); otherwise it is the forward's
- * stored lse ("stored" variant). */
+ * Workspace (float32) holds D and, for head_dim 64, the dQ accumulator; its
+ * size in bytes comes from pdb_flash_bwd_workspace_size.  If lse is NULL the
+ * kernel recomputes it (the "recompute" variant of the template); otherwise it
+ * is the forward's stored lse ("stored" variant).  head_dim 64 runs one fused
+ * pass whose dQ sums per-key-block parts with fp32 reductions in L2, so dq's
+ * last bits may differ run to run (dk, dv and head_dim 128 are reproducible). */
 typedef struct {
   const void* q;
   const void* k;
