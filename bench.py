@@ -316,7 +316,7 @@ def run_ours(args):
                          if peaks.get("bf16_tflops_sustained") else None,
                          # ncu dram read+write of one launch at B=2 (profiles/flash_fwd_sm100_config3.md),
                          # scaled by the 4x units of a config-3 launch; algorithmic bytes are 1073.7 MB
-                         "traffic": 4 * (202.08e6 + 43.79e6) * units / (B * H) if (B, H, S, D) == (8, 32, 4096, 128)
+                         "traffic": 4 * (202.89e6 + 45.39e6) * units / (B * H) if (B, H, S, D) == (8, 32, 4096, 128)
                          else None, "traffic_unit": "bytes per launch",
                          "kernel": "flash_fwd_sm100_kernel<128>",
                          "launch_ms": launch_ms},
