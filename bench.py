@@ -314,7 +314,7 @@ def run_ours(args):
                          "frac": achieved / peaks["bf16_tflops"], "peak_source": peaks["source"] + " (burst)",
                          "frac_sustained": achieved / peaks["bf16_tflops_sustained"]
                          if peaks.get("bf16_tflops_sustained") else None,
-                         # ncu dram read+write of one launch at B=2 (profiles/flash_fwd_sm100_config3.md),
+                         # ncu dram read+write of one launch at B=2 (the full ncu capture of this kernel),
                          # scaled by the 4x units of a config-3 launch; algorithmic bytes are 1073.7 MB
                          "traffic": 4 * (202.89e6 + 45.39e6) * units / (B * H) if (B, H, S, D) == (8, 32, 4096, 128)
                          else None, "traffic_unit": "bytes per launch",
