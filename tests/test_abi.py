@@ -81,3 +81,36 @@ def test_selftest_rejects_unbounded_limits():
     lib = _lib.load()
     assert lib.pdb_selftest_wait_timeout(0, None) == _lib.PDB_ERR_ARG
     assert lib.pdb_selftest_wait_timeout(3_000_000_000, None) == _lib.PDB_ERR_ARG
+
+
+def _bwd_desc(B, H, HKV, T, D, lse):
+    d = _lib.FlashBwdDesc()
+    d.q = d.k = d.v = d.o = d.dout = d.dq = d.dk = d.dv = 256
+    d.lse = 256 if lse else None
+    d.batch, d.heads_q, d.heads_kv, d.seqlen_q, d.seqlen_k, d.head_dim, d.head_dim_v = B, H, HKV, T, T, D, D
+    d.scale, d.causal, d.dtype = 0.125, 1, _lib.PDB_BF16
+    return d
+
+
+def test_backward_workspace_sizes():
+    """D and nlse2 rows (padded to 128) and two counters; at head_dim 64 also the fused
+    pass's fp32 dQ accumulator (64 floats per padded row); without lse the forward's
+    recomputed lse and output."""
+    lib = _lib.load()
+    al = lambda x: (x + 255) // 256 * 256
+    B, H, T = 2, 4, 300
+    rows = B * H * 384
+    base = al(rows * 4) * 2 + al(8)
+    assert lib.pdb_flash_bwd_workspace_size(C.byref(_bwd_desc(B, H, 2, T, 128, True))) == base
+    assert lib.pdb_flash_bwd_workspace_size(C.byref(_bwd_desc(B, H, 2, T, 64, True))) == base + al(rows * 64 * 4)
+    recompute = al(B * H * T * 4) + al(B * H * T * 64 * 2)
+    assert lib.pdb_flash_bwd_workspace_size(C.byref(_bwd_desc(B, H, 2, T, 64, False))) == (
+        base + al(rows * 64 * 4) + recompute)
+
+
+def test_backward_refuses_a_small_workspace_before_launching():
+    lib = _lib.load()
+    d = _bwd_desc(1, 2, 2, 200, 64, True)
+    d.workspace, d.workspace_bytes = 256, lib.pdb_flash_bwd_workspace_size(C.byref(d)) - 16
+    assert lib.pdb_flash_bwd(C.byref(d), None) == _lib.PDB_ERR_ARG
+    assert b"workspace too small" in lib.pdb_last_error_string()
