@@ -1,4 +1,4 @@
-"""Measurements as ledger facts (SURVEY next row: the analysis ledger as the
+"""Measurements as ledger facts (the analysis ledger as the
 measurement store; reference pdum/tl/analysis.py:121-175 and
 conformance/test_fusion_triton.py:87-117).  The device timing is replaced by a
 counter here; the GPU test measures for real."""

@@ -1,4 +1,4 @@
-"""The partition read off a placed region (SURVEY next row: mesh placement integration).
+"""The partition read off a placed region (mesh placement integration).
 
 A rider dim bound to a machine level in the reference's global-view spelling
 (``pdum/tl/zoo/megatron.py``) gives the shards; the reference's own traffic pass
