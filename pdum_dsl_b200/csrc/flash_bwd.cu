@@ -59,12 +59,6 @@ struct BwdParams {
   int* err;
 };
 
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
 
 // ---- MMA helpers.  Operand tiles are TMA boxes of 64 features x `rows` rows
 // (128-byte swizzle), so a feature-chunk of 64 sits `rows * 128` bytes after
