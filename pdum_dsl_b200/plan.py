@@ -49,6 +49,25 @@ def _twin_certificate(region, spec):
     return g.certificate
 
 
+# Per-CTA on-chip capacities of an sm_100a program (B200): dynamic shared
+# memory up to 227 KB (232448 bytes) per CTA, moved in 128-byte swizzle rows;
+# tensor memory 512 columns x 128 lanes x 4 bytes = 256 KB, allocated in
+# 32-column steps (16 KB).
+B200_SMEM_PER_CTA = 232448
+B200_TMEM_PER_SM = 512 * 128 * 4
+
+
+def b200_machine():
+    """One sm_100a CTA as the reference's per-program machine table (``TileMachine`` of
+    ``TileLevel`` rows, ``pdum/tl/launch.py:37-52``), for ``plan_region(region,
+    machine=b200_machine())``: the reference's ``propose`` / ``feasible``
+    (``launch.py:75-124``) then ladder launches against the B200's shared memory
+    (the tightest level) instead of a smaller part's."""
+    from pdum.tl.launch import TileLevel, TileMachine
+
+    return TileMachine((TileLevel("shared", 128, B200_SMEM_PER_CTA), TileLevel("tmem", 128 * 4 * 32, B200_TMEM_PER_SM)))
+
+
 def plan_region(region, machine=None, floor: int = 1024):
     """The reference's plan_region, with the widened flash rows (see the module docstring)."""
     from pdum.tl import fusion
