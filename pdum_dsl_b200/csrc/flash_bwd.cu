@@ -616,18 +616,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------------------
 // Fused D = 64 backward: dK, dV and dQ in one persistent pass.
-// The dK/dV schedule above (unit = 128 keys of one (batch, KV head), items =
-// (query head, 128-row query tile)) plus, per item, the dQ contribution of the
-// unit's keys, dQ_part = dS K, so the scores and exponentials are formed once
-// instead of once per kernel.  dS^T goes to shared memory (bf16, 128-byte
-// swizzled rows of 64 queries per key), where it serves as the K-major A
-// operand of dK += dS^T Q and, read the other way, as the MN-major A operand
-// of dQ_part = dS K.  dQ_part lands in its own TMEM columns; a drain warpgroup
-// reads it out, stages it in shared memory and adds it into an fp32 dQ
-// accumulator in the workspace with TMA bulk reductions (performed in L2; the
-// accumulator of config-5-sized problems fits there).  A final kernel scales
-// and rounds the accumulator to bf16.  dQ then depends on the order of the
-// fp32 additions (not bit-reproducible run to run); dK and dV do not.
+// Unit = 128 keys of one (batch, KV head), taken by one CTA per SM from a
+// global counter, heaviest first; items = (query head of the group, 128-row
+// query tile).  Per item the tensor core forms S^T = K Q^T and dP^T = V dO^T
+// (N = 128) in TMEM; the compute warpgroups (one thread per key row, each
+// warpgroup 64 of the 128 query columns) form P^T and dS^T = P^T (dP^T - D);
+// P^T goes to a TMEM staging area (A operand of dV += P^T dO) and dS^T to
+// shared memory (bf16, 128-byte swizzled rows of 64 queries per key), where it
+// serves as the K-major A operand of dK += dS^T Q and, read the other way, as
+// the MN-major A operand of dQ_part = dS K.  The scores and exponentials are
+// thus formed once for all three gradients.  dQ_part lands in its own TMEM
+// columns; four drain warps read it out, stage it in shared memory and add it
+// into an fp32 dQ accumulator in the workspace with TMA bulk reductions
+// (performed in L2; the accumulator of config-5-sized problems fits there),
+// and at the end of each unit store dV and dK (bf16) with TMA stores.  The
+// next item's scores are issued as soon as S / dP sit in registers, and the
+// next unit's first scores at the current unit's last item.  A final kernel
+// scales and rounds the accumulator to bf16.  dQ then depends on the order of
+// the fp32 additions (not bit-reproducible run to run); dK and dV do not.
 constexpr int kStagesF = 3;
 constexpr int kFusedThreads = 512;  // warps 0..3 control, 4..11 compute, 12..15 dQ drain
 
