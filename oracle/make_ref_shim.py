@@ -20,6 +20,8 @@ package's lowering.  Usage: ``python oracle/make_ref_shim.py [REFERENCE_ROOT]``.
 from __future__ import annotations
 
 import re
+import json
+import os
 import shutil
 import sys
 from pathlib import Path
@@ -37,7 +39,22 @@ def shim_text(text: str) -> str:
     )
 
 
-def make(ref_root: Path = Path("/root/reference")) -> Path:
+def reference_root() -> Path | None:
+    """Where the reference checkout is mounted: $PDUM_DSL_REFERENCE, else the
+    ``reference_path`` that BASELINE.json records; None when neither names an
+    existing directory (e.g. on a GPU box, which only uses the prebuilt copy)."""
+    env = os.environ.get("PDUM_DSL_REFERENCE")
+    cand = env
+    if cand is None:
+        bj = Path(__file__).resolve().parents[1] / "BASELINE.json"
+        if bj.exists():
+            cand = json.loads(bj.read_text()).get("reference_path")
+    if cand and Path(cand).is_dir():
+        return Path(cand)
+    return None
+
+
+def make(ref_root: Path) -> Path:
     for pkg in ("dsl", "tensorlib"):
         src = ref_root / "packages" / pkg / "src"
         dst = DEST / "packages" / pkg / "src"
@@ -68,5 +85,7 @@ def ensure_importable() -> bool:
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    root = Path(sys.argv[1]) if len(sys.argv) > 1 else reference_root()
+    if root is None:
+        sys.exit("usage: make_ref_shim.py <reference checkout> (or set PDUM_DSL_REFERENCE)")
     print(make(root))

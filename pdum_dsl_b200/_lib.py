@@ -36,6 +36,7 @@ EXPORTS = (
     "pdb_flash_bwd_noalloc_max_scratch",
     "pdb_contract",
     "pdb_pointwise_f32",
+    "pdb_score_program_f32",
     "pdb_check_error",
     "pdb_selftest_wait_timeout",
     "pdb_last_error_string",
@@ -196,6 +197,62 @@ class PointwiseDesc(C.Structure):
     ]
 
 
+# score-space programs (pdb_score_program_f32)
+SP_OPS = {"score": 1, "row": 2, "col": 3, "tile": 4, "iota_row": 5, "iota_col": 6, "const": 7, "where": 8,
+          "add": 9, "sub": 10, "mul": 11, "div": 12, "maximum": 13, "minimum": 14, "le": 15, "lt": 16, "ge": 17,
+          "gt": 18, "eq": 19, "ne": 20, "and": 21, "or": 22,
+          "exp": 23, "log": 24, "neg": 25, "recip": 26, "sqrt": 27, "tanh": 28, "not": 29, "abs": 30}
+SP_UNARY = ("exp", "log", "neg", "recip", "sqrt", "tanh", "not", "abs")
+SP_OUT = {"tile": 0, "row_sum": 1, "row_max": 2, "row_min": 3, "row_contract": 4}
+SP_MAX_OPS, SP_MAX_REGS, SP_MAX_SCORES, SP_MAX_VECS, SP_MAX_TILES = 64, 12, 2, 6, 4
+I64x2 = C.c_int64 * 2
+
+
+class SpOp(C.Structure):
+    _fields_ = [
+        ("op", C.c_int32),
+        ("dst", C.c_int32),
+        ("a", C.c_int32),
+        ("b", C.c_int32),
+        ("c", C.c_int32),
+        ("reserved", C.c_int32),
+        ("value", C.c_double),
+    ]
+
+
+class ScoreProgramDesc(C.Structure):
+    _fields_ = [
+        ("batch", C.c_int64),
+        ("rows", C.c_int64),
+        ("cols", C.c_int64),
+        ("row_start", C.c_int64),
+        ("col_start", C.c_int64),
+        ("n_scores", C.c_int32),
+        ("n_ops", C.c_int32),
+        ("n_regs", C.c_int32),
+        ("result", C.c_int32),
+        ("score_a", C.c_void_p * SP_MAX_SCORES),
+        ("score_b", C.c_void_p * SP_MAX_SCORES),
+        ("score_feat", C.c_int64 * SP_MAX_SCORES),
+        ("score_a_stride", I64x3 * SP_MAX_SCORES),
+        ("score_b_stride", I64x3 * SP_MAX_SCORES),
+        ("rowvec", C.c_void_p * SP_MAX_VECS),
+        ("rowvec_stride", I64x2 * SP_MAX_VECS),
+        ("colvec", C.c_void_p * SP_MAX_VECS),
+        ("colvec_stride", I64x2 * SP_MAX_VECS),
+        ("tile", C.c_void_p * SP_MAX_TILES),
+        ("tile_stride", I64x3 * SP_MAX_TILES),
+        ("ops", SpOp * SP_MAX_OPS),
+        ("out_mode", C.c_int32),
+        ("reserved", C.c_int32),
+        ("out", C.c_void_p),
+        ("out_stride", I64x3),
+        ("w", C.c_void_p),
+        ("w_stride", I64x3),
+        ("xdim", C.c_int64),
+    ]
+
+
 _LIB = None
 
 
@@ -226,6 +283,7 @@ def load(path: Path | None = None) -> C.CDLL:
     lib.pdb_flash_bwd_noalloc_max_scratch.restype = C.c_size_t
     lib.pdb_contract.argtypes = [C.POINTER(ContractDesc), vp]
     lib.pdb_pointwise_f32.argtypes = [C.POINTER(PointwiseDesc), vp]
+    lib.pdb_score_program_f32.argtypes = [C.POINTER(ScoreProgramDesc), vp]
     lib.pdb_check_error.argtypes = [vp]
     lib.pdb_selftest_wait_timeout.argtypes = [C.c_int64, vp]
     lib.pdb_last_error_string.restype = C.c_char_p

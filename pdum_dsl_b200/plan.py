@@ -95,50 +95,65 @@ def _bare(node):
     return node
 
 
-def _kernel_of(carve):
-    return carve.group.kernel if carve.group.kernel is not None else carve.kernel
+def _lowered(carve):
+    """The compile_tile runner of a carve: its plan group's tile kernel when a
+    template row lowers it, else the carve's canonical kernel (the naive
+    region the group was planned from -- same denotation), which the
+    score-space program family lowers.  Raises Untranslatable if neither does."""
+    from .tile import compile_tile
+
+    tried = []
+    for k in (carve.group.kernel, carve.kernel):
+        if k is None:
+            continue
+        try:
+            return compile_tile(k), k
+        except Untranslatable as e:
+            tried.append(str(e))
+    raise Untranslatable(f"carve {carve.root_op} ({carve.group.template}): " + " | ".join(tried))
 
 
 def device_assignment(plan) -> list[str]:
     """Per carve of a ``plan_model`` ModelPlan (``pdum/tl/partition.py:586``):
-    ``"device"`` when ``compile_tile`` lowers its kernel to the sm_100a library,
-    ``"reference"`` when the group is red or the kernel has no template here (the
-    reference doctrine: red groups are served by ``run_region``)."""
-    from .tile import compile_tile
-
+    ``"device"`` when a kernel of the sm_100a library executes it (every
+    carve of the attention joint, the red max-adjoint scan included), else
+    the reason it is refused."""
     out = []
     for c in plan.carves:
-        where = "reference"
-        if c.root is not None and c.group.confidence != "red":
-            try:
-                compile_tile(_kernel_of(c))
-                where = "device"
-            except Untranslatable:
-                pass
-        out.append(where)
+        if c.root is None:
+            out.append("none")
+            continue
+        try:
+            _lowered(c)
+            out.append("device")
+        except Untranslatable as e:
+            out.append(f"refused: {e}")
     return out
 
 
-def execute_model_plan(plan, region, values, *, device: bool = True):
+def execute_model_plan(plan, region, values):
     """Execute a carved plan carve by carve, the way the reference executes one
     (``tests/test_partition.py:124-193``): a carve runs once every boundary value
-    it reads is known; its kernel runs on the sm_100a library when
-    ``device_assignment`` says so (f32 IEEE column, numpy in / out), else through
-    ``run_region``.  ``values`` are ``Tensor``s per region param; returns the
-    yielded values (``Tensor``s) and the per-carve assignment."""
-    import numpy as np
-    from pdum.tl.dialect import run_region
-    from pdum.tl.tensor import Tensor
-
-    from .tile import compile_tile
-
-    assign = device_assignment(plan) if device else ["reference"] * len(plan.carves)
+    it reads is known, on the sm_100a library (f32 IEEE column; boundary values
+    stay on the device between carves).  ``values`` are CUDA tensors per region
+    param in type-dim order; returns the yielded values as CUDA tensors in the
+    yield's dim order, and the per-carve assignment.  A carve no kernel lowers
+    raises ``Untranslatable`` before anything runs -- there is no evaluator
+    fallback."""
+    runners = [(_lowered(c) if c.root is not None else None) for c in plan.carves]
     vals = {id(p): v for p, v in zip(region.params, values)}
+    dims = {id(p): tuple(d.name for d in p.type.dims) for p in region.params}
 
     def known(b):
         while id(b) not in vals and b.op in _CHART_OPS:
             b = b.args[0]
         return b
+
+    def arranged(b, param):
+        """A boundary value in the dim order the carve's param expects."""
+        v, have = vals[id(b)], dims[id(b)]
+        want = tuple(d.name for d in param.type.dims)
+        return v if have == want else v.permute(*[have.index(n) for n in want])
 
     pending = [(i, c) for i, c in enumerate(plan.carves) if c.root is not None]
     progressed = True
@@ -148,26 +163,21 @@ def execute_model_plan(plan, region, values, *, device: bool = True):
             bounds = [known(b) for b in c.bounds]
             if not all(id(b) in vals for b in bounds):
                 continue
-            kernel = _kernel_of(c)
-            ins = [vals[id(b)] for b in bounds]
-            if assign[i] == "device":
-                arrs = [t.to_numpy(order=tuple(d.name for d in p.type.dims)) for t, p in zip(ins, kernel.params)]
-                got = compile_tile(kernel)(arrs)
-                got = got if isinstance(got, tuple) else (got,)
-                y = kernel.body[-1].args[0]
-                ynodes = y.args if y.op == "core.tuple" else (y,)
-                outs = tuple(Tensor.from_numpy(np.asarray(a, dtype=np.float64), tuple(d.name for d in n.type.dims))
-                             for a, n in zip(got, ynodes))
-            else:
-                got = run_region(kernel, ins)
-                outs = tuple(got) if isinstance(got, (tuple, list)) else (got,)
-            for node, val in zip((c.root, *c.artifacts), outs):
-                vals[id(node)] = val
-                vals[id(_bare(node))] = val  # chart roots alias their bare value
+            run, kernel = runners[i]
+            ins = [arranged(b, p) for b, p in zip(bounds, kernel.params)]
+            got = run.run_t(*ins)
+            got = got if isinstance(got, tuple) else (got,)
+            y = kernel.body[-1].args[0]
+            ynodes = y.args if y.op == "core.tuple" else (y,)
+            for node, val, yn in zip((c.root, *c.artifacts), got, ynodes):
+                names = tuple(d.name for d in yn.type.dims)
+                for key in (id(node), id(_bare(node))):  # chart roots alias their bare value
+                    vals[key] = val.float()
+                    dims[key] = names
             pending.remove((i, c))
             progressed = True
     if pending:
         raise RuntimeError("plan stalled: a carve reads a boundary value no carve produces")
     y = region.body[-1].args[0]
     targets = y.args if y.op == "core.tuple" else (y,)
-    return tuple(vals[id(known(t))] for t in targets), assign
+    return tuple(vals[id(known(t))] for t in targets), ["device"] * sum(c.root is not None for c in plan.carves)

@@ -31,6 +31,7 @@ import math
 import numpy as np
 
 from .recognize import AttentionSpec, ContractSpec, MapSpec, RowSpec, Untranslatable, recognize
+from .score_program import ScoreProgramSpec, match_score_program, run_score_program
 
 # the executor fingerprint (the reference's Pair seat is keyed the same way, triton_tile.py:54)
 B200_FP = ("tile_sm100a", "pdb")
@@ -116,6 +117,8 @@ def _check_launch(spec, launch, prune, region):
         carried = {spec.s, spec.e}
     elif isinstance(spec, MapSpec):
         carried = set()
+    elif isinstance(spec, ScoreProgramSpec):
+        carried = {ps.cols for ps in spec.passes if ps.mode != "tile"}
     elif isinstance(spec, ContractSpec):
         carried = set(spec.k)
     else:
@@ -174,6 +177,9 @@ class _Runner:
             self.source = (f"pdb_contract dtype={dtype} batch={spec.batch} m={spec.m} n={spec.n} k={spec.k} "
                            f"prologue=({spec.a_pro}, {spec.b_pro}) epilogue={[e[0] for e in spec.epilogue]} "
                            f"kernel={kern}")
+        elif isinstance(spec, ScoreProgramSpec):
+            self.grid = sum(-(-(spec.extents[ps.rows][1] - spec.extents[ps.rows][0]) // 64) for ps in spec.passes)
+            self.source = spec.source
         else:
             R = 1
             for d in region.params[spec.x].type.dims:
@@ -192,6 +198,8 @@ class _Runner:
             return _run_contract(spec, tensors, self.dtype)
         if isinstance(spec, MapSpec):
             return _run_map(spec, tensors)
+        if isinstance(spec, ScoreProgramSpec):
+            return run_score_program(spec, tensors)
         if isinstance(spec, RowSpec):
             x = tensors[spec.x]
             perm = [spec.x_dims.index(n) for n in spec.x_dims if n != spec.dim] + [spec.x_dims.index(spec.dim)]
@@ -279,7 +287,15 @@ def compile_tile(region, launch: tuple = (), prune: tuple = (), *, dtype: str = 
     """Region -> runner over the prebuilt sm_100a kernels (see the module docstring)."""
     if dtype not in ("f32", "bf16"):
         raise ValueError("dtype must be 'f32' or 'bf16'")
-    spec = recognize(region)
+    try:
+        spec = recognize(region)
+    except Untranslatable as first:
+        try:
+            spec = match_score_program(region)
+        except Untranslatable as e:
+            raise Untranslatable(f"{first}; score-space program: {e}") from None
+    if isinstance(spec, ScoreProgramSpec) and dtype != "f32":
+        raise Untranslatable("score-space programs are f32")
     if isinstance(spec, MapSpec) and dtype != "f32":
         raise Untranslatable("the map-chain kernel is f32")
     if isinstance(spec, RowSpec) and dtype != "f32":

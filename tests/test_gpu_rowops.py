@@ -67,21 +67,28 @@ def test_strided_rows_and_large_magnitudes(cuda):
 
 
 def test_full_config_properties(cuda):
-    """Config-2 size (8192 x 4096): size-independent properties + sampled rows vs the oracle."""
+    """Config 2 (X 8192 x 4096 ~ N(0,1), gamma ~ N(1, 0.1), beta ~ N(0, 0.1), eps 1e-5, seeds
+    20..22): size-independent properties over every row, plus sampled rows vs the oracle."""
     import torch
 
     from pdum_dsl_b200 import kernels
 
-    g = torch.Generator(device=cuda).manual_seed(0)
-    x = torch.randn(8192, 4096, device=cuda, generator=g)
+    rng = [np.random.default_rng(20 + i) for i in range(3)]
+    xh = rng[0].standard_normal((8192, 4096), dtype=np.float32)
+    gam = (1 + 0.1 * rng[1].standard_normal(4096)).astype(np.float32)
+    bet = (0.1 * rng[2].standard_normal(4096)).astype(np.float32)
+    x = torch.from_numpy(xh).to(cuda)
     y = kernels.row_softmax(x)
     sums = y.double().sum(dim=1)
     assert torch.allclose(sums, torch.ones_like(sums), atol=1e-5)
     assert (y >= 0).all()
-    idx = [0, 1, 4095, 8191]
-    assert_f32(y[idx].cpu().numpy(), OR.softmax(x[idx].cpu().numpy().astype(np.float64)))
-    ln = kernels.layernorm(x)
-    assert torch.allclose(ln.double().mean(1), torch.zeros(8192, dtype=torch.float64, device=cuda), atol=1e-5)
-    assert torch.allclose(ln.double().var(1, unbiased=False), torch.ones(8192, dtype=torch.float64, device=cuda),
-                          atol=1e-3)
-    assert_f32(ln[idx].cpu().numpy(), OR.layernorm(x[idx].cpu().numpy().astype(np.float64)))
+    idx = [0, 1, 777, 4095, 5000, 8191]
+    assert_f32(y[idx].cpu().numpy(), OR.softmax(xh[idx].astype(np.float64)))
+    g, b = torch.from_numpy(gam).to(cuda), torch.from_numpy(bet).to(cuda)
+    ln = kernels.layernorm(x, g, b, eps=1e-5)
+    # undo the affine epilogue: the normalised rows have mean 0 and variance 1
+    z = (ln.double() - b.double()) / g.double()
+    assert torch.allclose(z.mean(1), torch.zeros(8192, dtype=torch.float64, device=cuda), atol=1e-4)
+    assert torch.allclose(z.var(1, unbiased=False), torch.ones(8192, dtype=torch.float64, device=cuda), atol=1e-3)
+    assert_f32(ln[idx].cpu().numpy(), OR.layernorm(xh[idx].astype(np.float64), gam.astype(np.float64),
+                                                  bet.astype(np.float64), eps=1e-5))
