@@ -85,10 +85,20 @@ int pdb_layernorm_f32(const pdb_layernorm_desc* d, void* stream);
  * (float32, [batch, heads_q, seqlen_q] contiguous):
  *   lse = log(sum_s exp(score)),   m = max_s score,   den = sum_s exp(score - m)
  * -- m / den are the template's artifact finals (fusion.py:611-613).
+ * General closed masks (the reference plans any closed iota mask forest as
+ * flash, fusion.py:468-477,521, and prunes it per program, :659-690): with
+ * key_lo / key_hi set (device int32 arrays of seqlen_q entries, `causal`
+ * must be 0), query row t sees exactly the keys s with key_lo[t] <= s <
+ * key_hi[t] (absolute key indices; the host evaluates the mask and checks
+ * each row's visible keys form one non-empty run).  When key_lo and key_hi
+ * are both nondecreasing in t, set mask_monotone: the kernels then visit, per
+ * block of query rows, only the key tiles between the block's first row's
+ * key_lo and its last row's key_hi; otherwise every key tile is visited and
+ * the per-row bounds alone mask.
  * dtype PDB_BF16: bf16 q/k/v/o, fp32 accumulate, tcgen05/TMEM tensor cores
  * (head_dim, head_dim_v in {64, 128}).  dtype PDB_F32: f32 everything, ieee
- * FMA path (any head_dim <= 128), the precision of the reference's f32
- * column (triton_tile.py:684-690 refuses tf32). */
+ * FMA path (any head_dim, head_dim_v <= 256), the precision of the reference's
+ * f32 column (triton_tile.py:684-690 refuses tf32). */
 typedef struct {
   const void* q;
   const void* k;
@@ -103,6 +113,10 @@ typedef struct {
   double scale;
   int32_t causal;
   int32_t dtype; /* enum pdb_dtype */
+  const int32_t* key_lo; /* nullable: per query row, first visible key */
+  const int32_t* key_hi; /* per query row, one past the last visible key */
+  int32_t mask_monotone;
+  int32_t reserved;
 } pdb_flash_desc;
 int pdb_flash_fwd(const pdb_flash_desc* d, void* stream);
 

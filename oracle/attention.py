@@ -101,3 +101,15 @@ def attention_bwd(q, k, v, dout, *, scale=None, causal=False, q_start=0, row_blo
                 dq[b, h, t0:t0 + row_block] = sc_mul * (dS @ kh)
                 dk[b, hk] += sc_mul * (dS.T @ qh)
     return dq.reshape(shapes[0]), dk.reshape(shapes[1]), dv.reshape(shapes[2])
+
+
+def masked_attention(q, k, v, visible, *, scale=None):
+    """One head under an arbitrary boolean mask ``visible`` (t, s): the reference's
+    denotation ``softmax(where(mask, scale * q k^T, -1e9)) @ v`` (zoo/attention.py:
+    98-101 spells the sliding window this way)."""
+    sc = np.asarray(q, dtype=np.float64) @ np.asarray(k, dtype=np.float64).T
+    if scale is not None:
+        sc = sc * scale
+    sc = np.where(visible, sc, FILL)
+    p = np.exp(sc - sc.max(axis=1, keepdims=True))
+    return (p / p.sum(axis=1, keepdims=True)) @ np.asarray(v, dtype=np.float64)

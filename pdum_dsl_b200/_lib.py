@@ -108,6 +108,10 @@ class FlashDesc(C.Structure):
         ("scale", C.c_double),
         ("causal", C.c_int32),
         ("dtype", C.c_int32),
+        ("key_lo", C.c_void_p),
+        ("key_hi", C.c_void_p),
+        ("mask_monotone", C.c_int32),
+        ("reserved", C.c_int32),
     ]
 
 

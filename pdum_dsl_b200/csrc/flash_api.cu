@@ -29,6 +29,9 @@ extern "C" int pdb_flash_fwd(const pdb_flash_desc* d, void* stream) {
                                d->head_dim_v, d->q_start, d->q, d->k, d->v))
     return st;
   if (!d->o) return set_error(PDB_ERR_ARG, "null o");
+  if ((d->key_lo == nullptr) != (d->key_hi == nullptr))
+    return set_error(PDB_ERR_ARG, "key_lo and key_hi are given together");
+  if (d->key_lo && d->causal) return set_error(PDB_ERR_ARG, "a key-interval mask replaces the causal flag");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (d->dtype) {
     case PDB_F32: return flash_fwd_f32(*d, s);

@@ -22,7 +22,7 @@ namespace {
 
 constexpr int BM = 64, BN = 64, NT = 256;
 
-template <int D>  // padded head-dim bound (64 or 128)
+template <int D>  // padded head-dim bound (64, 128 or 256)
 __global__ void __launch_bounds__(NT) flash_f32_kernel(pdb_flash_desc p) {
   extern __shared__ float sm[];
   const int E = (int)p.head_dim, O = (int)p.head_dim_v;
@@ -31,6 +31,8 @@ __global__ void __launch_bounds__(NT) flash_f32_kernel(pdb_flash_desc p) {
   float* Vs = Ks + BN * (D + 1);     // [BN][D]
   float* Ss = Vs + BN * D;           // [BM][BN+1]
   float* alpha_s = Ss + BM * (BN + 1);  // [BM]
+  int* row_lo = reinterpret_cast<int*>(alpha_s + BM);  // [BM] key-interval mask bounds
+  int* row_hi = row_lo + BM;                            // [BM]
 
   const int tid = threadIdx.x;
   const int64_t mblk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -55,13 +57,26 @@ __global__ void __launch_bounds__(NT) flash_f32_kernel(pdb_flash_desc p) {
 #pragma unroll
   for (int j = 0; j < D / 4; ++j) acc[j] = 0.f;
 
-  int64_t s_end = S;
+  const int64_t last = r0 + BM - 1 < T - 1 ? r0 + BM - 1 : T - 1;
+  int64_t s_begin = 0, s_end = S;
   if (p.causal) {
-    const int64_t last_row = (r0 + BM - 1 < T - 1 ? r0 + BM - 1 : T - 1) + p.q_start;
+    const int64_t last_row = last + p.q_start;
     s_end = last_row + 1 < S ? last_row + 1 : S;
   }
+  if (p.key_lo) {
+    for (int i = tid; i < BM; i += NT) {
+      const int64_t t = r0 + i < T ? r0 + i : T - 1;
+      row_lo[i] = p.key_lo[t];
+      row_hi[i] = p.key_hi[t];
+    }
+    if (p.mask_monotone) {  // this block's visible keys: [key_lo[first row], key_hi[last row])
+      s_begin = (p.key_lo[r0] / BN) * BN;
+      const int64_t h_ = p.key_hi[last];
+      s_end = h_ < S ? h_ : S;
+    }
+  }
   const int ty = tid >> 4, tx = tid & 15;
-  for (int64_t s0 = 0; s0 < s_end; s0 += BN) {
+  for (int64_t s0 = s_begin; s0 < s_end; s0 += BN) {
     __syncthreads();
     for (int i = tid; i < BN * E; i += NT) {
       const int r = i / E, c = i % E;
@@ -94,7 +109,9 @@ __global__ void __launch_bounds__(NT) flash_f32_kernel(pdb_flash_desc p) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int64_t t = r0 + ty * 4 + a, s = s0 + tx + 16 * j;
-        const bool ok = s < S && (!p.causal || s <= t + p.q_start);
+        const int rr = ty * 4 + a;
+        const bool ok = s < S && (!p.causal || s <= t + p.q_start) &&
+                        (!p.key_lo || (s >= row_lo[rr] && s < row_hi[rr]));
         Ss[(ty * 4 + a) * (BN + 1) + tx + 16 * j] = ok ? sc[a][j] * scale : -FLT_MAX;
       }
     __syncthreads();
@@ -154,26 +171,27 @@ __global__ void __launch_bounds__(NT) flash_f32_kernel(pdb_flash_desc p) {
   }
 }
 
+template <int D>
+cudaError_t launch_f32(const pdb_flash_desc& p, dim3 grid, cudaStream_t stream) {
+  const size_t smem = sizeof(float) * (BM * (D + 1) + BN * (D + 1) + BN * D + BM * (BN + 1) + 3 * BM);
+  cudaError_t e = cudaFuncSetAttribute(flash_f32_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) flash_f32_kernel<D><<<grid, NT, smem, stream>>>(p);
+  return e;
+}
+
 }  // namespace
 
 int flash_fwd_f32(const pdb_flash_desc& p, cudaStream_t stream) {
-  if (p.head_dim > 128 || p.head_dim_v > 128)
-    return set_error(PDB_ERR_UNSUPPORTED, "f32 flash: head_dim and head_dim_v must be <= 128");
+  if (p.head_dim > 256 || p.head_dim_v > 256)
+    return set_error(PDB_ERR_UNSUPPORTED, "f32 flash: head_dim and head_dim_v must be <= 256");
   const int64_t mblocks = (p.seqlen_q + BM - 1) / BM;
   if (mblocks > 0x7fffffff || p.heads_q > 65535 || p.batch > 65535)
     return set_error(PDB_ERR_SHAPE, "f32 flash: grid too large");
   dim3 grid((unsigned)mblocks, (unsigned)p.heads_q, (unsigned)p.batch);
-  const bool big = p.head_dim > 64 || p.head_dim_v > 64;
-  const int D = big ? 128 : 64;
-  const size_t smem = sizeof(float) * (BM * (D + 1) + BN * (D + 1) + BN * D + BM * (BN + 1) + BM);
-  cudaError_t e;
-  if (big) {
-    e = cudaFuncSetAttribute(flash_f32_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess) flash_f32_kernel<128><<<grid, NT, smem, stream>>>(p);
-  } else {
-    e = cudaFuncSetAttribute(flash_f32_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess) flash_f32_kernel<64><<<grid, NT, smem, stream>>>(p);
-  }
+  const int64_t dmax = p.head_dim > p.head_dim_v ? p.head_dim : p.head_dim_v;
+  const cudaError_t e = dmax <= 64 ? launch_f32<64>(p, grid, stream)
+                        : dmax <= 128 ? launch_f32<128>(p, grid, stream)
+                                      : launch_f32<256>(p, grid, stream);
   if (e != cudaSuccess) return cuda_status(e, "f32 flash: set smem attribute");
   return cuda_status(cudaGetLastError(), "f32 flash launch");
 }

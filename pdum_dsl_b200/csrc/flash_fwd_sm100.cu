@@ -61,6 +61,9 @@ struct FwdParams {
   int T, S, H, HKV, B;
   int q_start;
   int causal;
+  const int32_t* key_lo;  // per-row key intervals (general closed masks) or null
+  const int32_t* key_hi;
+  int mask_monotone;
   int num_mblocks;  // 256-row blocks per head
   float scale_log2;  // scale * log2(e)
   int* err;
@@ -99,8 +102,9 @@ __device__ __forceinline__ void mma_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_
   }
 }
 
+// Key tiles j0 .. j0 + nA - 1 (tile A) and j0 .. j0 + nB - 1 (tile B, nB >= nA).
 struct TileInfo {
-  int b, h, hk, t0, nA, nB;
+  int b, h, hk, t0, j0, nA, nB;
 };
 
 // Tile ordinals run head-major (concurrent CTAs share the K/V of a few heads
@@ -123,16 +127,21 @@ __device__ __forceinline__ TileInfo tile_info(int tile, const FwdParams& p) {
   ti.t0 = mblk * 2 * BM;
   const int n_kv = (p.S + BN - 1) / BN;
   int n[2];
+  ti.j0 = 0;
+  if (p.key_lo && p.mask_monotone) {
+    // visible keys of the 256 rows: [key_lo[first row], key_hi[last row])
+    const int first = ti.t0 < p.T ? ti.t0 : p.T - 1;
+    ti.j0 = __ldg(p.key_lo + first) / BN;
+  }
 #pragma unroll
   for (int x = 0; x < 2; ++x) {
-    if (p.causal) {
-      int last_row = ti.t0 + x * BM + BM - 1;
-      if (last_row > p.T - 1) last_row = p.T - 1;
-      const int c = (last_row + p.q_start) / BN + 1;
-      n[x] = c < n_kv ? c : n_kv;
-    } else {
-      n[x] = n_kv;
-    }
+    int last_row = ti.t0 + x * BM + BM - 1;
+    if (last_row > p.T - 1) last_row = p.T - 1;
+    int c = n_kv;
+    if (p.causal) c = (last_row + p.q_start) / BN + 1;
+    else if (p.key_lo && p.mask_monotone) c = (__ldg(p.key_hi + last_row) + BN - 1) / BN;
+    c = c < n_kv ? c : n_kv;
+    n[x] = c - ti.j0 > 1 ? c - ti.j0 : 1;
   }
   ti.nA = n[0];
   ti.nB = n[1] < n[0] ? n[0] : n[1];
@@ -144,7 +153,7 @@ __device__ __forceinline__ TileInfo tile_info(int tile, const FwdParams& p) {
 // Barrier phases run on counters that continue across tiles, so the loads and
 // score MMAs of tile n+1 overlap the epilogue of tile n; O_x is only
 // overwritten after the epilogue of its previous tile released it (o_empty).
-template <int D>
+template <int D, bool kKeyMask>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -213,13 +222,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = mbar_wait(&bar->k_empty[st], ph ^ 1, abort, p.err))) break;
           mbar_expect_tx(&bar->k_full[st], L::kTileBytes);
           for (int i = 0; i < kNB; ++i)
-            tma_load_4d(smem + L::kK + st * L::kTileBytes + i * kBoxBytes, &tm_k, &bar->k_full[st], i * 64, j * BN,
-                        ti.hk, ti.b);
+            tma_load_4d(smem + L::kK + st * L::kTileBytes + i * kBoxBytes, &tm_k, &bar->k_full[st], i * 64,
+                        (ti.j0 + j) * BN, ti.hk, ti.b);
           if (!(ok = mbar_wait(&bar->v_empty[st], ph ^ 1, abort, p.err))) break;
           mbar_expect_tx(&bar->v_full[st], L::kTileBytes);
           for (int i = 0; i < kNB; ++i)
-            tma_load_4d(smem + L::kV + st * L::kTileBytes + i * kBoxBytes, &tm_v, &bar->v_full[st], i * 64, j * BN,
-                        ti.hk, ti.b);
+            tma_load_4d(smem + L::kV + st * L::kTileBytes + i * kBoxBytes, &tm_v, &bar->v_full[st], i * 64,
+                        (ti.j0 + j) * BN, ti.hk, ti.b);
         }
         if (!ok) break;
       }
@@ -295,17 +304,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TileInfo ti = tile_info(tile, p);
       const int t = ti.t0 + x * BM + row;  // query row
       const int n = x ? ti.nB : ti.nA;
+      // this row's visible keys [row_lo, row_hi) under a key-interval mask
+      int row_lo = 0, row_hi = p.S;
+      if constexpr (kKeyMask) {
+        const int tc = t < p.T ? t : p.T - 1;
+        row_lo = __ldg(p.key_lo + tc);
+        row_hi = __ldg(p.key_hi + tc);
+      }
       float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
       for (int j = 0; j < n; ++j, ++cs) {
         if (!(ok = mbar_wait(&bar->s_full[x], cs & 1, abort, p.err))) break;
         tc_fence_after();
         // keys at or past `lim` (tile-relative) are masked for this row
-        int lim = p.S - j * BN;
+        const int kb = (ti.j0 + j) * BN;  // first key of this tile
+        int lim = p.S - kb;
         if (p.causal) {
-          const int lc = t + p.q_start + 1 - j * BN;
+          const int lc = t + p.q_start + 1 - kb;
           lim = lc < lim ? lc : lim;
         }
-        const bool need_mask = __any_sync(0xffffffffu, lim < BN);
+        int lo_rel = 0;
+        if constexpr (kKeyMask) {
+          lo_rel = row_lo - kb;
+          lim = row_hi - kb < lim ? row_hi - kb : lim;
+        }
+        const bool need_mask = __any_sync(0xffffffffu, lim < BN || lo_rel > 0);
         // all 128 scores of the row in registers: one TMEM round trip
         uint32_t sr[BN];
 #pragma unroll
@@ -314,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (need_mask) {
 #pragma unroll
           for (int i = 0; i < BN; ++i)
-            if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
+            if (i >= lim || i < lo_rel) sr[i] = __float_as_uint(-INFINITY);
         }
         float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;  // 4 independent chains
 #pragma unroll
@@ -450,6 +472,7 @@ struct __align__(8) BarriersD64 {
   int abort;
 };
 
+template <bool kKeyMask>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_d64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
@@ -509,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int st = gk & 1;
           if (!(ok = mbar_wait(&bar->k_empty[st], ((gk >> 1) & 1) ^ 1, abort, p.err))) break;
           mbar_expect_tx(&bar->k_full[st], L::kTileBytes);
-          tma_load_4d(smem + L::kK + st * L::kTileBytes, &tm_k, &bar->k_full[st], 0, j * BN, ti.hk, ti.b);
+          tma_load_4d(smem + L::kK + st * L::kTileBytes, &tm_k, &bar->k_full[st], 0, (ti.j0 + j) * BN, ti.hk, ti.b);
         }
       }
     } else if (warp == 2 && lane == 0) {
@@ -523,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int st = gv & 1;
           if (!(ok = mbar_wait(&bar->v_empty[st], ((gv >> 1) & 1) ^ 1, abort, p.err))) break;
           mbar_expect_tx(&bar->v_full[st], L::kTileBytes);
-          tma_load_4d(smem + L::kV + st * L::kTileBytes, &tm_v, &bar->v_full[st], 0, j * BN, ti.hk, ti.b);
+          tma_load_4d(smem + L::kV + st * L::kTileBytes, &tm_v, &bar->v_full[st], 0, (ti.j0 + j) * BN, ti.hk, ti.b);
         }
       }
     } else if (warp == 1 && lane == 0) {
@@ -596,16 +619,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TileInfo ti = tile_info(tile, p);
       const int t = ti.t0 + x * BM + row;
       const int n = x ? ti.nB : ti.nA;
+      // this row's visible keys [row_lo, row_hi) under a key-interval mask
+      int row_lo = 0, row_hi = p.S;
+      if constexpr (kKeyMask) {
+        const int tc = t < p.T ? t : p.T - 1;
+        row_lo = __ldg(p.key_lo + tc);
+        row_hi = __ldg(p.key_hi + tc);
+      }
       float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
       for (int j = 0; j < n; ++j, ++cs) {
         if (!(ok = mbar_wait(&bar->s_full[x], cs & 1, abort, p.err))) break;
         tc_fence_after();
-        int lim = p.S - j * BN;
+        const int kb = (ti.j0 + j) * BN;  // first key of this tile
+        int lim = p.S - kb;
         if (p.causal) {
-          const int lc = t + p.q_start + 1 - j * BN;
+          const int lc = t + p.q_start + 1 - kb;
           lim = lc < lim ? lc : lim;
         }
-        const bool need_mask = __any_sync(0xffffffffu, lim < BN);
+        int lo_rel = 0;
+        if constexpr (kKeyMask) {
+          lo_rel = row_lo - kb;
+          lim = row_hi - kb < lim ? row_hi - kb : lim;
+        }
+        const bool need_mask = __any_sync(0xffffffffu, lim < BN || lo_rel > 0);
         uint32_t sr[BN];
 #pragma unroll
         for (int ch = 0; ch < BN / 32; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
@@ -614,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (need_mask) {
 #pragma unroll
           for (int i = 0; i < BN; ++i)
-            if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
+            if (i >= lim || i < lo_rel) sr[i] = __float_as_uint(-INFINITY);
         }
         float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
 #pragma unroll
@@ -744,6 +780,9 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   p.B = (int)d.batch;
   p.q_start = (int)d.q_start;
   p.causal = d.causal ? 1 : 0;
+  p.key_lo = d.key_lo;
+  p.key_hi = d.key_hi;
+  p.mask_monotone = d.mask_monotone ? 1 : 0;
   p.num_mblocks = (int)((d.seqlen_q + 2 * BM - 1) / (2 * BM));
   p.scale_log2 = (float)(d.scale * 1.4426950408889634);
   p.err = device_error_flag();
@@ -755,9 +794,10 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   const int64_t grid = units < sm_count(dev) ? units : sm_count(dev);  // persistent: one CTA per SM
   const int smem = Smem<D>::kTotal;
   if (D == 64) {  // P in its own TMEM columns (656 vs 610 TFLOP/s at B8 H32 S4096 causal)
-    cudaError_t e = cudaFuncSetAttribute(flash_fwd_d64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    auto kern = p.key_lo ? flash_fwd_d64_kernel<true> : flash_fwd_d64_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_status(e, "bf16 flash: set smem attribute");
-    flash_fwd_d64_kernel<<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, p);
+    kern<<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, p);
     return cuda_status(cudaGetLastError(), "bf16 flash launch");
   }
   CUtensorMap to;  // O stores: 32-row boxes, one per softmax warp
@@ -768,9 +808,10 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
     if (int st = encode_tma_4d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.o, dims, so, obox, CU_TENSOR_MAP_SWIZZLE_128B))
       return st;
   }
-  cudaError_t e = cudaFuncSetAttribute(flash_fwd_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  auto kern = p.key_lo ? flash_fwd_sm100_kernel<D, true> : flash_fwd_sm100_kernel<D, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_status(e, "bf16 flash: set smem attribute");
-  flash_fwd_sm100_kernel<D><<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, to, p);
+  kern<<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, to, p);
   return cuda_status(cudaGetLastError(), "bf16 flash launch");
 }
 

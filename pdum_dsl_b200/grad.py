@@ -38,6 +38,9 @@ class _GradRunner:
         self.spec: AttentionSpec = match_naive_attention(region, _unwrap(yld.args[0]))
         if self.spec.artifacts:
             raise Untranslatable("artifact-yielding forward inside a joint is not lowered")
+        if self.spec.mask is not None:
+            raise Untranslatable("the fused backward takes causal or unmasked attention; a general mask's "
+                                 "joint runs carve by carve (plan_model + execute_model_plan)")
         self.n_params = len(region.params)
         self.do_index = self.n_params - 1  # the seed is passed last (RegionGrad docstring)
         pnames = {rg.names[id(p)]: i for i, p in enumerate(region.params) if id(p) in rg.names}

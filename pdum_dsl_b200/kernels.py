@@ -11,6 +11,7 @@ from __future__ import annotations
 import ctypes as C
 import math
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -90,13 +91,15 @@ def _s3(t: torch.Tensor):
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float | None = None,
                     causal: bool = False, q_start: int = 0, out: torch.Tensor | None = None,
-                    return_lse: bool = False, return_artifacts: bool = False):
+                    return_lse: bool = False, return_artifacts: bool = False, key_intervals=None):
     """softmax(scale * q k^T [causal: s <= t + q_start]) v.
 
     q (B, Hq, T, D), k/v (B, Hkv, S, D|Dv) with Hq a multiple of Hkv (GQA);
     2-D and 3-D inputs drop the leading dims.  bf16 runs the tcgen05 kernel
     (D = Dv in {64, 128}); f32 runs the IEEE CUDA-core kernel.  Returns o, or
-    (o, lse) / (o, m, den) with the per-row float32 statistics."""
+    (o, lse) / (o, m, den) with the per-row float32 statistics.
+    ``key_intervals`` (a ``recognize.KeyIntervals`` of T rows) is a general
+    closed mask: row t sees keys lo[t] <= s < hi[t] (``causal`` must be False)."""
     _need_cuda(q, k, v)
     if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
         raise TypeError(f"flash_attention: q/k/v must share dtype float32 or bfloat16, got {q.dtype}/{k.dtype}/{v.dtype}")
@@ -123,7 +126,17 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale:
     d.batch, d.heads_q, d.heads_kv, d.seqlen_q, d.seqlen_k, d.head_dim, d.head_dim_v = B, H, HKV, T, S, D, DV
     d.q_stride, d.k_stride, d.v_stride, d.o_stride = _s3(q4), _s3(k4), _s3(v4), _s3(o)
     d.q_start, d.scale, d.causal, d.dtype = int(q_start), float(scale), int(bool(causal)), _DTYPES[q.dtype]
+    keep = None
+    if key_intervals is not None:
+        if causal:
+            raise ValueError("flash_attention: key_intervals replace the causal flag")
+        if len(key_intervals.lo) != T:
+            raise ValueError(f"flash_attention: key_intervals has {len(key_intervals.lo)} rows, q has {T}")
+        keep = torch.from_numpy(np.stack([key_intervals.lo, key_intervals.hi])).to(q.device)
+        d.key_lo, d.key_hi = keep[0].data_ptr(), keep[1].data_ptr()
+        d.mask_monotone = int(key_intervals.monotone)
     check(load().pdb_flash_fwd(C.byref(d), _stream(q)), "pdb_flash_fwd")
+    del keep  # the launch is stream-ordered before any reuse of this memory by the caching allocator
     o_ret = o.view(*shape_in[:-1], DV) if out is None else out
     lead = shape_in[:-1]
     if return_artifacts:

@@ -10,14 +10,13 @@ same ``Plan`` / ``Group`` objects with a ``flash`` group instead:
 
 * ``kernel`` is the region itself, so ``run_region(group.kernel, ...)``
   remains the oracle and ``compile_tile(group.kernel)`` lowers it;
-* ``certificate`` is the reference's own flash certificate
-  (``certify`` with the ``flash.online-softmax`` license over the
-  adversarial families, ``fusion.py:696-715``) of the strict single-head
-  twin at the shrunk extents (<= 128, the reference's ``_CERT_CAP``): the
-  riders are independent instances of that program and the scale is a
-  pointwise factor on the scores, so the twin's online-softmax law is the
-  one the widened row relies on;
-* ``params`` records what was widened (riders, group, scale, causal).
+* ``certificate`` is the reference's own certificate (``certify`` with the
+  ``flash.online-softmax`` license over its adversarial families,
+  ``fusion.py:618-656,696-715``) of the widened region itself: the
+  online-softmax fold spelled for its riders / group / scale / mask
+  (``widen.generate_widened_flash``) against the region, on a twin clamped
+  to 2 per rider and 128 per other dim (the reference's cap);
+* ``params`` records what was widened (riders, group, scale, mask).
 
 Requires the reference DSL (pdum.dsl / pdum.tl) to be importable.
 """
@@ -25,28 +24,23 @@ Requires the reference DSL (pdum.dsl / pdum.tl) to be importable.
 from __future__ import annotations
 
 from .recognize import Untranslatable, match_naive_attention
-from .regions import attention_region
 from .tile import B200_FP
 
-_CERT_CAP = 128
+_CERTS: dict = {}
 
 
-def _twin_certificate(region, spec):
-    from pdum.tl import fusion
+def _certificate(region, spec):
+    """certify_widened, memoised by the region's content key (the reference keeps
+    certificates as analysis facts, fusion.py:696-715)."""
+    from .widen import certify_widened
 
-    def ext(i, n):
-        d = next(d for d in region.params[i].type.dims if d.name == n)
-        return d.stop - d.start
-
-    T = min(ext(spec.q, spec.t), _CERT_CAP)
-    S = T if spec.causal else min(ext(spec.k, spec.s), _CERT_CAP)
-    E = min(ext(spec.q, spec.e), _CERT_CAP)
-    O = min(ext(spec.v, spec.o), _CERT_CAP)
-    twin = attention_region(T=T, S=S, D=E, DV=O, causal=spec.causal, all_true_mask=not spec.causal)
-    (g,) = fusion.plan_region(twin).groups
-    if g.template != "flash":
-        raise Untranslatable(f"the strict twin did not plan as flash: {g.reason}")
-    return g.certificate
+    key = getattr(region.body[-1], "key", None)
+    if key is None or key not in _CERTS:
+        cert = certify_widened(region, spec)
+        if key is None:
+            return cert
+        _CERTS[key] = cert
+    return _CERTS[key]
 
 
 # Per-CTA on-chip capacities of an sm_100a program (B200): dynamic shared
@@ -77,10 +71,11 @@ def plan_region(region, machine=None, floor: int = 1024):
         return plan
     try:
         spec = match_naive_attention(region)
-        cert = _twin_certificate(region, spec)
     except Untranslatable:
         return plan
-    params = (("riders", spec.riders), ("group", spec.group), ("scale", spec.scale), ("causal", spec.causal),
+    cert = _certificate(region, spec)
+    mask = "causal" if spec.causal else ("intervals" if spec.mask is not None else "none")
+    params = (("riders", spec.riders), ("group", spec.group), ("scale", spec.scale), ("mask", mask),
               ("backend", B200_FP))
     arts = ("m", "den") if spec.artifacts else ()
     return fusion.Plan((fusion.Group("flash", region, cert, "yellow", params=params, artifacts=arts),))

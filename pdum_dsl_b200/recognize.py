@@ -117,7 +117,8 @@ def softmax_core(pr):
 # --------------------------------------------------------------- mask forests
 _CMP = {"le": np.less_equal, "lt": np.less, "ge": np.greater_equal, "gt": np.greater, "eq": np.equal,
         "ne": np.not_equal, "add": np.add, "sub": np.subtract, "mul": np.multiply, "maximum": np.maximum,
-        "minimum": np.minimum, "and": np.logical_and, "or": np.logical_or}
+        "minimum": np.minimum, "and": np.logical_and, "or": np.logical_or, "div": np.true_divide}
+_UNARY_MASK = {"floor": np.floor, "abs": np.abs, "neg": np.negative}
 
 
 def _eval_mask(n, grid: dict):
@@ -138,33 +139,77 @@ def _eval_mask(n, grid: dict):
             return _CMP[f](vals[0], vals[1])
         if f == "not" and len(vals) == 1:
             return np.logical_not(vals[0])
+        if f in _UNARY_MASK and len(vals) == 1:
+            return _UNARY_MASK[f](vals[0])
         if f == "where" and len(vals) == 3:
             return np.where(vals[0], vals[1], vals[2])
         raise Untranslatable(f"mask op {f!r}")
     raise Untranslatable(f"mask node {n.op!r} reads data")
 
 
-def classify_mask(mask, t: str, s: str, t_range: tuple[int, int], s_range: tuple[int, int]) -> bool:
-    """True when the mask is causal (s <= t in absolute coordinates); False when
-    it is all-true.  Other masks are refused."""
+class KeyIntervals:
+    """A closed mask read as one run of visible keys per query row: row t (relative
+    to the query dim's start) sees keys lo[t] <= s < hi[t].  ``monotone`` when lo
+    and hi are both nondecreasing (causal, sliding-window and block-local masks),
+    which lets the kernels bound each block of rows' key tiles by its edge rows."""
+
+    __slots__ = ("lo", "hi", "monotone")
+
+    def __init__(self, lo, hi):
+        self.lo = np.ascontiguousarray(lo, dtype=np.int32)
+        self.hi = np.ascontiguousarray(hi, dtype=np.int32)
+        self.monotone = bool(np.all(np.diff(self.lo) >= 0) and np.all(np.diff(self.hi) >= 0))
+
+    def __repr__(self):
+        return f"KeyIntervals(rows={len(self.lo)}, monotone={self.monotone})"
+
+
+_ROW_CHUNK_ELEMS = 1 << 22
+
+
+def classify_mask(mask, t: str, s: str, t_range: tuple[int, int], s_range: tuple[int, int]):
+    """Evaluate a closed mask forest exactly over the whole (t, s) grid.
+
+    Returns True when it is causal (s <= t in absolute coordinates), False when
+    it is all-true, else the ``KeyIntervals`` of a mask whose every row's visible
+    keys form one run.  Refuses (Untranslatable) a row with no visible key --
+    the reference gives such a row uniform-softmax semantics and refuses to
+    prune it (fusion.py:659-687) -- and rows whose visible keys are not one run."""
     if f_of(mask) == "le" and all(a.op == "tl.iota" for a in mask.args):
-        if (attrs(mask.args[0])["name"], attrs(mask.args[1])["name"]) == (s, t):
-            return True
+        if (attrs(mask.args[0])["name"], attrs(mask.args[1])["name"]) == (s, t) and s_range[0] == 0:
+            if s_range[1] >= t_range[1]:  # every row sees keys 0..t
+                return True
     if f_of(mask) == "ge" and all(a.op == "tl.iota" for a in mask.args):
-        if (attrs(mask.args[0])["name"], attrs(mask.args[1])["name"]) == (t, s):
-            return True
+        if (attrs(mask.args[0])["name"], attrs(mask.args[1])["name"]) == (t, s) and s_range[0] == 0:
+            if s_range[1] >= t_range[1]:
+                return True
     (t0, t1), (s0, s1) = t_range, s_range
-    ts = np.arange(t0, t1)
-    ss = np.arange(s0, s1)
-    if len(ts) * len(ss) > (1 << 22):  # sample rows: first, last, and a spread
-        ts = np.unique(np.concatenate([ts[:64], ts[-64:], ts[:: max(1, len(ts) // 256)]]))
-    grid = {t: ts[:, None].astype(np.int64), s: ss[None, :].astype(np.int64)}
-    m = np.broadcast_to(np.asarray(_eval_mask(mask, grid), dtype=bool), (len(ts), len(ss)))
-    if m.all():
+    ss = np.arange(s0, s1, dtype=np.int64)
+    S = len(ss)
+    chunk = max(1, _ROW_CHUNK_ELEMS // max(S, 1))
+    los, his = [], []
+    for a in range(t0, t1, chunk):
+        ts = np.arange(a, min(a + chunk, t1), dtype=np.int64)
+        grid = {t: ts[:, None], s: ss[None, :]}
+        m = np.broadcast_to(np.asarray(_eval_mask(mask, grid), dtype=bool), (len(ts), S))
+        any_ = m.any(axis=1)
+        if not any_.all():
+            bad = int(ts[np.argmin(any_)])
+            raise Untranslatable(f"mask row {t}={bad} sees no key (uniform-softmax semantics; not lowered)")
+        lo = m.argmax(axis=1)
+        hi = S - m[:, ::-1].argmax(axis=1)
+        if not np.array_equal(m.sum(axis=1), hi - lo):
+            raise Untranslatable("mask rows are not single runs of visible keys")
+        los.append(lo + s0)
+        his.append(hi + s0)
+    lo = np.concatenate(los)
+    hi = np.concatenate(his)
+    if (lo == s0).all() and (hi == s1).all():
         return False
-    if np.array_equal(m, ss[None, :] <= ts[:, None]):
+    tabs = np.arange(t0, t1)
+    if s0 == 0 and (lo == 0).all() and np.array_equal(hi, np.minimum(tabs + 1, s1)) and s1 >= t1:
         return True
-    raise Untranslatable("mask forest is neither causal (s <= t) nor all-true")
+    return KeyIntervals(lo, hi)
 
 
 # ------------------------------------------------------------------ attention
@@ -189,6 +234,7 @@ class AttentionSpec:
     stat_dims: tuple  # dims of the m / den artifacts
     t_start: int
     source: str  # "naive" | "tile"
+    mask: KeyIntervals | None = None  # a general closed mask (causal is then False)
 
 
 def _param_index(region, n):
@@ -279,13 +325,15 @@ def match_naive_attention(region, yld=None) -> AttentionSpec:
     out_dims = names_of(yld)
     t_hint = _pick_t(out_dims, qdims_only, names_of(v))
     qi, ki, vi, qd, kd, vd, t, o, riders, group, t_start = _attention_dims(region, q, k, v, e, s, t_hint)
-    causal = False
+    causal, kmask = False, None
     if mask is not None:
         tdim = next(d for d in dims_of(q) if d.name == t)
         sdim = next(d for d in dims_of(k) if d.name == s)
         causal = classify_mask(mask, t, s, (tdim.start, tdim.stop), (sdim.start, sdim.stop))
+        if isinstance(causal, KeyIntervals):
+            causal, kmask = False, causal
     return AttentionSpec(qi, ki, vi, qd, kd, vd, t, s, e, o, riders, group, scale, causal, artifacts, out_dims,
-                         names_of(m_out) if artifacts else (), t_start, "naive")
+                         names_of(m_out) if artifacts else (), t_start, "naive", kmask)
 
 
 def _pick_t(out_dims, q_only, v_dims):
@@ -343,8 +391,11 @@ def match_flash_tile(region) -> AttentionSpec:
     tdim = next(d for d in dims_of(q) if d.name == t)
     sdim = next(d for d in dims_of(k) if d.name == s)
     causal = classify_mask(mask, t, s, (tdim.start, tdim.stop), (sdim.start, sdim.stop))
+    kmask = None
+    if isinstance(causal, KeyIntervals):
+        causal, kmask = False, causal
     return AttentionSpec(qi, ki, vi, qd, kd, vd, t, s, e, o, riders, group, None, causal, artifacts, out_dims,
-                         names_of(f_m) if artifacts else (), t_start, "tile")
+                         names_of(f_m) if artifacts else (), t_start, "tile", kmask)
 
 
 def _check_flash_step(step):

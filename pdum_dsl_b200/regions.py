@@ -71,14 +71,18 @@ def attention_shapes(B, H, T, S, D, DV, group=None):
 
 
 def attention_region(B=None, H=None, T=6, S=None, D=3, DV=None, *, causal=True, scale=None,
-                     group=None, artifacts=False, all_true_mask=False):
+                     group=None, artifacts=False, all_true_mask=False, window=None, block=None):
     """The naive (materialised-softmax) attention region; returns the Region.
 
     ``artifacts=True`` yields the tuple ``(out, m, den)`` -- the flash
     template's artifact variant (``pdum/tl/fusion.py:480-497``).
     ``all_true_mask=True`` (non-causal only) spells "no mask" as a closed
     always-true mask ``where(iota(s) <= iota(s), sc, -1e9)``, the form the
-    reference's strict flash matcher requires (``fusion.py:468-477``)."""
+    reference's strict flash matcher requires (``fusion.py:468-477``).
+    ``window=W`` (with causal) is the zoo's sliding mask ``(s <= t) * (t - s < W)``
+    (``zoo/attention.py:84-103``); ``block=Bk`` is the block-diagonal (chunked)
+    mask ``floor(t / Bk) == floor(s / Bk)``, causal within the block when
+    ``causal`` -- both closed iota forests."""
     Builder, Region, OPS, f64, _, _ = _dsl()
     S = T if S is None else S
     DV = D if DV is None else DV
@@ -90,9 +94,21 @@ def attention_region(B=None, H=None, T=6, S=None, D=3, DV=None, *, causal=True, 
     sc = _contract(b, pq, pk, "e")
     if scale is not None:
         sc = b.emit("tl.pointwise", sc, b.emit("core.const", type=f64, value=float(scale)), f="mul")
+    mask = None
     if causal or all_true_mask:
         other = "t" if causal else "s"
         mask = b.emit("tl.pointwise", b.emit("tl.iota", sc, name="s"), b.emit("tl.iota", sc, name=other), f="le")
+    if window is not None:
+        lag = b.emit("tl.pointwise", b.emit("tl.iota", sc, name="t"), b.emit("tl.iota", sc, name="s"), f="sub")
+        inwin = b.emit("tl.pointwise", lag, b.emit("core.const", type=f64, value=float(window)), f="lt")
+        mask = inwin if mask is None else b.emit("tl.pointwise", mask, inwin, f="mul")
+    if block is not None:
+        bk = b.emit("core.const", type=f64, value=float(block))
+        bt = b.emit("tl.pointwise", b.emit("tl.pointwise", b.emit("tl.iota", sc, name="t"), bk, f="div"), f="floor")
+        bs = b.emit("tl.pointwise", b.emit("tl.pointwise", b.emit("tl.iota", sc, name="s"), bk, f="div"), f="floor")
+        same = b.emit("tl.pointwise", bt, bs, f="eq")
+        mask = same if mask is None else b.emit("tl.pointwise", mask, same, f="mul")
+    if mask is not None:
         sc = b.emit("tl.pointwise", mask, sc, b.emit("core.const", type=f64, value=-1e9), f="where")
     pr, mx, den = _softmax(b, sc, "s")
     out = _contract(b, pr, pv, "s")

@@ -131,8 +131,8 @@ def _check_launch(spec, launch, prune, region):
         if int(tile) <= 0:
             raise Untranslatable(f"launch tile for {name!r} must be positive")
     for entry in prune:
-        if not isinstance(spec, AttentionSpec) or not spec.causal:
-            raise Untranslatable("prune bounds only apply to the causal flash template")
+        if not isinstance(spec, AttentionSpec) or not (spec.causal or spec.mask is not None):
+            raise Untranslatable("prune bounds only apply to a masked flash template")
         if entry[0] != "so":
             raise Untranslatable(f"prune dim {entry[0]!r} is not the flash scan dim")
 
@@ -156,7 +156,7 @@ class _Runner:
                 heads *= _extent(region, spec.q, spec.group)
             rows = 256 if dtype == "bf16" else 64
             self.grid = heads * -(-T // rows)
-            self.source = (f"pdb_flash_fwd dtype={dtype} causal={spec.causal} scale={spec.scale} "
+            self.source = (f"pdb_flash_fwd dtype={dtype} causal={spec.causal} mask={spec.mask} scale={spec.scale} "
                            f"riders={spec.riders} group={spec.group} artifacts={spec.artifacts} "
                            f"kernel={'flash_fwd_sm100_kernel (tcgen05/TMEM, TMA)' if dtype == 'bf16' else 'flash_f32_kernel (IEEE FMA)'}")
         elif isinstance(spec, MapSpec):
@@ -243,7 +243,7 @@ class _Runner:
         q4, k4, v4 = (x if x.dtype == dt else x.to(dt) for x in (q4, k4, v4))
         scale = 1.0 if spec.scale is None else spec.scale
         res = kernels.flash_attention(q4, k4, v4, scale=scale, causal=spec.causal, q_start=spec.t_start,
-                                      return_artifacts=spec.artifacts)
+                                      return_artifacts=spec.artifacts, key_intervals=spec.mask)
         o = res[0] if spec.artifacts else res
         # back to the yield's dim order: (riders..., [group], t, o)
         onames = tuple(rid + qg + [spec.t, spec.o])
@@ -309,9 +309,9 @@ def compile_tile(region, launch: tuple = (), prune: tuple = (), *, dtype: str = 
         DV = _extent(region, spec.v, spec.o)
         if D != DV or D not in (64, 128):
             raise Untranslatable(f"bf16 flash needs head dims e == o in (64, 128), got {D}, {DV}")
-    if isinstance(spec, AttentionSpec) and (_extent(region, spec.q, spec.e) > 128 or
-                                            _extent(region, spec.v, spec.o) > 128):
-        raise Untranslatable("flash head dims above 128 are not built")
+    if isinstance(spec, AttentionSpec) and (_extent(region, spec.q, spec.e) > 256 or
+                                            _extent(region, spec.v, spec.o) > 256):
+        raise Untranslatable("flash head dims above 256 are not built")
     _check_launch(spec, launch, prune, region)
     runner = _Runner(region, spec, dtype, launch, prune)
 
@@ -339,4 +339,6 @@ def flops(region) -> float:
     if spec.group:
         heads *= _extent(region, spec.q, spec.group)
     f = 2.0 * heads * T * S * (D + DV)
+    if spec.mask is not None:  # the visible (row, key) pairs of a general closed mask
+        return 2.0 * heads * float(np.sum(spec.mask.hi.astype(np.int64) - spec.mask.lo)) * (D + DV)
     return f / 2 if spec.causal else f

@@ -73,6 +73,42 @@ def attention_case(case, *, dtype, seeds, **kw):
          meta={"run_region_s": round(time.time() - t0, 3)})
 
 
+def masked_case(case, *, dtype, seeds, zoo_sliding=None, **kw):
+    """General closed masks: the reference zoo's sliding_attention (zoo/attention.py:84-103)
+    or a region spelled with a window / block mask."""
+    from pdum_dsl_b200.regions import attention_region
+
+    if zoo_sliding is not None:
+        from pdum.tl.zoo.attention import sliding_attention
+
+        region = sliding_attention(**zoo_sliding).region
+        rkw = {"zoo": "sliding_attention", **zoo_sliding}
+    else:
+        region = attention_region(**kw)
+        rkw = kw
+    shapes, names = _param_shapes(region), _param_names(region)
+    arrays = [draw(seed, shp, dtype) for seed, shp in zip(seeds, shapes)]
+    t0 = time.time()
+    outs, onames = _run(region, arrays, names)
+    spec = [{"seed": s, "shape": list(shp), "names": list(n), "dtype": dtype, "scale": 1.0,
+             "checksum": input_checksum(a)} for s, shp, n, a in zip(seeds, shapes, names, arrays)]
+    save(case, region_kw=rkw, inputs_spec=spec, outputs=outs, out_names=[list(n) for n in onames],
+         meta={"run_region_s": round(time.time() - t0, 3)})
+
+
+def mask_cases():
+    masked_case("sliding_zoo_f32", dtype="f32", seeds=(601, 602, 603),
+                zoo_sliding=dict(T=300, E=64, OD=64, W=70))
+    masked_case("sliding_zoo_bf16", dtype="bf16", seeds=(604, 605, 606),
+                zoo_sliding=dict(T=384, E=64, OD=64, W=130))
+    masked_case("sliding_bf16_riders", dtype="bf16", seeds=(611, 612, 613), B=1, H=2, T=300, D=128,
+                causal=True, window=100, scale=1 / np.sqrt(128))
+    masked_case("block_bf16_d128", dtype="bf16", seeds=(621, 622, 623), H=2, T=384, D=128, causal=False,
+                block=128, scale=1 / np.sqrt(128))
+    masked_case("block_causal_f32", dtype="f32", seeds=(631, 632, 633), T=200, D=32, causal=True, block=50,
+                scale=0.2)
+
+
 def row_case(case, kind, R, C, dtype, seeds, eps=1e-5):
     from pdum_dsl_b200.regions import layernorm_region, row_softmax_region
 
@@ -134,6 +170,9 @@ def joint_case(case, T, E, OD, seed):
 def main():
     if not ensure_importable():
         raise SystemExit("reference DSL not importable: run `python oracle/make_ref_shim.py` first")
+    if "--masks-only" in sys.argv:  # just the general-mask cases
+        mask_cases()
+        return
     flash_tile_case()
     attention_case("cfg1_flash_f32", dtype="f32", seeds=(101, 102, 103), B=1, H=4, T=256, D=64,
                    causal=False, scale=1 / 8)
@@ -153,6 +192,7 @@ def main():
     row_case("layernorm_37x1001", "layernorm", 37, 1001, "f32", (414, 415, 416))
     joint_case("flash_joint_bwd", T=64, E=16, OD=16, seed=501)
     joint_case("flash_joint_bwd_d64", T=200, E=64, OD=64, seed=511)
+    mask_cases()
 
 
 if __name__ == "__main__":

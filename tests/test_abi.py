@@ -8,7 +8,8 @@ import pytest
 
 from pdum_dsl_b200 import _lib
 
-HEADER = Path(__file__).resolve().parents[1] / "include" / "pdb.h"
+REPO = Path(__file__).resolve().parents[1]
+HEADER = REPO / "include" / "pdb.h"
 
 
 def declared_symbols():
@@ -27,12 +28,40 @@ def test_library_loads_and_exports_everything():
     assert _lib.version().startswith("pdb-sm100a")
 
 
-def test_descriptor_layouts_match_the_header():
-    # pointer-sized fields first, then int64 sizes; the offsets the C side expects
-    assert C.sizeof(_lib.RowSoftmaxDesc) == 6 * 8
-    assert C.sizeof(_lib.LayerNormDesc) == 9 * 8
-    assert C.sizeof(_lib.FlashDesc) == 7 * 8 + 7 * 8 + 12 * 8 + 8 + 8 + 4 + 4
-    assert C.sizeof(_lib.FlashBwdDesc) == 11 * 8 + 7 * 8 + 24 * 8 + 8 + 8 + 4 + 4
+_STRUCTS = {
+    "pdb_rowsoftmax_desc": "RowSoftmaxDesc", "pdb_layernorm_desc": "LayerNormDesc", "pdb_flash_desc": "FlashDesc",
+    "pdb_flash_bwd_desc": "FlashBwdDesc", "pdb_ew_op": "EwOp", "pdb_contract_desc": "ContractDesc",
+    "pdb_pointwise_desc": "PointwiseDesc", "pdb_sp_op": "SpOp", "pdb_score_program_desc": "ScoreProgramDesc",
+}
+
+
+def test_descriptor_layouts_match_the_header(tmp_path):
+    """Every descriptor's size and every field's offset, as a C compiler lays out
+    include/pdb.h, equal the ctypes mirror's."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "pdb.h"', "int main(void) {"]
+    for cname, pyname in _STRUCTS.items():
+        st = getattr(_lib, pyname)
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in st._fields_:
+            lines.append(f'printf("{cname}.{fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(l.rsplit(" ", 1) for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                          check=True).stdout.splitlines())
+    for cname, pyname in _STRUCTS.items():
+        st = getattr(_lib, pyname)
+        assert int(got[f"{cname} size"]) == C.sizeof(st), cname
+        for fname, _ in st._fields_:
+            assert int(got[f"{cname}.{fname}"]) == getattr(st, fname).offset, f"{cname}.{fname}"
 
 
 def test_null_descriptors_are_refused():

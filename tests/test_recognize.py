@@ -68,13 +68,6 @@ def test_refusals_name_the_reason(dsl):
         recognize(region)
 
 
-def test_sliding_window_mask_is_refused(dsl):
-    from pdum.tl.zoo.attention import sliding_attention
-
-    with pytest.raises(Untranslatable):
-        recognize(sliding_attention().region)
-
-
 def test_compile_tile_checks_launch_and_dtype(dsl):
     from pdum.tl.fusion import plan_region
     from pdum.tl.launch import TileLevel, TileMachine
@@ -99,18 +92,43 @@ def test_widened_plan_region(dsl):
     from pdum_dsl_b200.plan import plan_region
     from pdum_dsl_b200.regions import attention_region
 
-    for kw in (dict(B=1, H=2, T=200, D=64, causal=True, scale=0.125),
-               dict(B=1, H=2, T=64, D=16, causal=False, scale=0.25),
-               dict(B=1, H=2, T=64, D=16, causal=True, scale=0.25, group=2)):
+    for kw, mask in ((dict(B=1, H=2, T=200, D=64, causal=True, scale=0.125), "causal"),
+                     (dict(B=1, H=2, T=64, D=16, causal=False, scale=0.25), "none"),
+                     (dict(B=1, H=2, T=64, D=16, causal=True, scale=0.25, group=2), "causal"),
+                     (dict(H=2, T=96, D=16, causal=True, window=40, scale=0.25), "intervals"),
+                     (dict(B=2, T=96, D=16, causal=False, block=32, scale=0.25), "intervals")):
         (g,) = plan_region(attention_region(**kw)).groups
         assert g.template == "flash" and g.confidence == "yellow"
+        # certified on the widened region itself (its own online-softmax fold vs the region)
         assert g.certificate.verdict == "licensed-differential"
         assert "flash.online-softmax" in g.certificate.licenses
-        assert dict(g.params)["causal"] == kw["causal"]
+        assert g.certificate.families == ("gaussian", "wide-scores", "dominant-key")
+        assert dict(g.params)["mask"] == mask
     from pdum_dsl_b200.regions import row_softmax_region
 
     (g,) = plan_region(row_softmax_region(4, 8)).groups  # untouched rows stay the reference's
     assert g.template == "row-normalization"
+
+
+def test_widened_fold_is_the_region_on_every_family(dsl):
+    """The generated fold of a widened region (riders, GQA group, scale, sliding mask)
+    evaluates equal to the naive region under run_region (the certificate's differential,
+    rerun here directly at a tight tolerance)."""
+    import numpy as np
+    from pdum.tl.dialect import run_region
+    from pdum.tl.tensor import Tensor
+
+    from pdum_dsl_b200.recognize import match_naive_attention
+    from pdum_dsl_b200.regions import attention_region
+    from pdum_dsl_b200.widen import generate_widened_flash
+
+    r = attention_region(B=2, H=2, T=48, D=8, causal=True, window=20, scale=0.3, group=2)
+    tile = generate_widened_flash(r, match_naive_attention(r))
+    rng = np.random.default_rng(0)
+    vals = [Tensor.from_numpy(rng.standard_normal(tuple(d.stop for d in p.type.dims)),
+                              tuple(d.name for d in p.type.dims)) for p in r.params]
+    a, b = run_region(r, vals), run_region(tile, list(vals))
+    np.testing.assert_allclose(b.to_numpy(order=a.names), a.to_numpy(order=a.names), rtol=1e-12, atol=1e-12)
 
 
 def test_compile_grad_reads_the_autodiff_joint(dsl):
@@ -221,3 +239,49 @@ def _rows_only_unsupported():
     x = b.param(0, tensor_type_of_layout(Tensor.from_numpy(np.zeros((3, 4)), ("r", "c")).layout))
     y = b.emit("tl.reduce", x, dims=("r", "c"), f="sum")
     return Region(params=(x,), body=(b.emit("core.yield", y),))
+
+
+def test_general_closed_masks_read_as_key_intervals(dsl):
+    """Sliding-window, block-diagonal and the zoo's sliding_attention masks evaluate
+    exactly to one run of visible keys per row (the reference plans them as flash,
+    fusion.py:468-477,521); rows with no visible key and non-run rows are refused."""
+    import numpy as np
+    from pdum.tl.zoo.attention import sliding_attention
+
+    from pdum_dsl_b200.recognize import KeyIntervals
+    from pdum_dsl_b200.regions import attention_region
+
+    t = np.arange(300)
+    sp = recognize(sliding_attention(T=300, E=4, OD=4, W=70).region)
+    assert not sp.causal and isinstance(sp.mask, KeyIntervals) and sp.mask.monotone
+    assert np.array_equal(sp.mask.lo, np.maximum(t - 69, 0)) and np.array_equal(sp.mask.hi, t + 1)
+    bl = recognize(attention_region(T=300, D=4, causal=False, block=64)).mask
+    assert np.array_equal(bl.lo, (t // 64) * 64) and np.array_equal(bl.hi, np.minimum((t // 64 + 1) * 64, 300))
+    blc = recognize(attention_region(T=300, D=4, causal=True, block=64)).mask
+    assert np.array_equal(blc.hi, t + 1) and np.array_equal(blc.lo, (t // 64) * 64)
+    # the causal mask still reads as causal (the dedicated kernels' fast path)
+    assert recognize(attention_region(T=300, D=4, causal=True)).causal is True
+    with pytest.raises(Untranslatable, match="sees no key"):
+        recognize(attention_region(T=40, D=4, causal=True, window=0))
+    with pytest.raises(Untranslatable, match="single runs"):
+        recognize(_strided_mask_region())
+
+
+def _strided_mask_region():
+    """Attention whose mask keeps the even keys only (not one run per row)."""
+    from pdum.dsl.types import f64
+
+    from pdum_dsl_b200 import regions as R
+
+    Builder, Region, OPS, _, _, _ = R._dsl()
+    (qn, qs), (kn, ks), (vn, vs) = R.attention_shapes(None, None, 16, 16, 4, 4, None)
+    b = Builder(OPS)
+    pq, pk, pv = (b.param(i, R._ptype(sh, nm)) for i, (nm, sh) in enumerate(((qn, qs), (kn, ks), (vn, vs))))
+    sc = R._contract(b, pq, pk, "e")
+    two = b.emit("core.const", type=f64, value=2.0)
+    si = b.emit("tl.iota", sc, name="s")
+    half = b.emit("tl.pointwise", b.emit("tl.pointwise", si, two, f="div"), f="floor")
+    even = b.emit("tl.pointwise", b.emit("tl.pointwise", half, two, f="mul"), si, f="eq")
+    sc = b.emit("tl.pointwise", even, sc, b.emit("core.const", type=f64, value=-1e9), f="where")
+    pr, _, _ = R._softmax(b, sc, "s")
+    return Region(params=(pq, pk, pv), body=(b.emit("core.yield", R._contract(b, pr, pv, "s")),))
