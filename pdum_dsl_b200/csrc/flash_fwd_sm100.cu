@@ -352,7 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           m_used = mt;
         } else if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
           const float m_new = fmaxf(m_used, mt);
-          const float alpha = ex2(m_used - m_new);
+          // a row that has seen no visible key yet (m_used = -inf) has l = 0 and O = 0: alpha 0 keeps it so
+          const float alpha = m_used == -INFINITY ? 0.f : ex2(m_used - m_new);
           m_used = m_new;
           l *= alpha;
           // O is quiescent here: the commit that released S(j) also covers PV(j-1)
@@ -669,7 +670,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           m_used = mt;
         } else if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
           const float m_new = fmaxf(m_used, mt);
-          const float alpha = ex2(m_used - m_new);
+          // a row that has seen no visible key yet (m_used = -inf) has l = 0 and O = 0: alpha 0 keeps it so
+          const float alpha = m_used == -INFINITY ? 0.f : ex2(m_used - m_new);
           m_used = m_new;
           l *= alpha;
           uint32_t r[32];
