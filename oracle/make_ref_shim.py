@@ -11,10 +11,13 @@ git-ignored ``baseline/_ref/`` and rewrites those forms mechanically:
   (``pdum/tl/units.py:26``; only t-string unit literals use it, and nothing on
   the attention / row-reduction path does).
 
-Nothing else is changed.  The copy is used only to (a) regenerate the golden
-fixtures under ``tests/golden/`` with the reference's own ``run_region`` and
-(b) run the CPU tests that drive the reference's ``plan_region`` into this
-package's lowering.  Usage: ``python oracle/make_ref_shim.py [REFERENCE_ROOT]``.
+Nothing else is changed.  The reference's own GPU columns
+(``conformance/triton_zoo.py``: the hand-written Triton flash kernel) are
+copied unchanged to ``baseline/_ref/conformance/`` so the bench can time them
+as labelled bars.  The copy is used only to (a) regenerate the golden
+fixtures under ``tests/golden/`` with the reference's own ``run_region``,
+(b) run the tests that drive the reference's ``plan_region`` into this
+package's lowering and (c) time the reference's columns beside ours.  Usage: ``python oracle/make_ref_shim.py [REFERENCE_ROOT]``.
 """
 
 from __future__ import annotations
@@ -66,6 +69,10 @@ def make(ref_root: Path) -> Path:
             s = shim_text(t)
             if s != t:
                 f.write_text(s)
+    conf = DEST / "conformance"
+    conf.mkdir(parents=True, exist_ok=True)
+    for name in ("triton_zoo.py",):
+        shutil.copy2(ref_root / "conformance" / name, conf / name)
     return DEST
 
 

@@ -64,6 +64,7 @@ struct FwdParams {
   const int32_t* key_lo;  // per-row key intervals (general closed masks) or null
   const int32_t* key_hi;
   int mask_monotone;
+  int lpt;          // heaviest-first snake schedule (else head-major pairs)
   int num_mblocks;  // 256-row blocks per head
   float scale_log2;  // scale * log2(e)
   int* err;
@@ -107,20 +108,41 @@ struct TileInfo {
   int b, h, hk, t0, j0, nA, nB;
 };
 
-// Tile ordinals run head-major (concurrent CTAs share the K/V of a few heads
-// in L2); within a head they alternate heavy and light row blocks (last,
-// first, second-to-last, second, ...).  A CTA takes ordinals in pairs, so each
-// pair costs about the same under the causal mask and the static persistent
-// schedule stays balanced.
-__device__ __forceinline__ int kth_tile(int k) {
-  return (blockIdx.x + (k >> 1) * gridDim.x) * 2 + (k & 1);
+// Two static schedules of the persistent grid over the work tiles (256 query
+// rows of one head each).
+// * Pairs (large jobs): ordinals run head-major (concurrent CTAs share the K/V
+//   of a few heads in L2); within a head they alternate heavy and light row
+//   blocks (last, first, second-to-last, second, ...).  A CTA takes ordinals in
+//   pairs, so each pair costs about the same under the causal mask.
+// * Heaviest-first snake (small jobs, e.g. one rank's shard of a job split over
+//   several GPUs, where a few hundred equal pairs over 148 SMs leave the last
+//   wave half empty): ordinals run from the last row block of every head down
+//   to the first, and CTA c takes ordinals c, 2G-1-c, 2G+c, ... (G CTAs), the
+//   longest-processing-time-first rule dealt in a boustrophedon.  The K/V of
+//   all heads of such a job fit in L2, so the head-major order buys nothing.
+__device__ __forceinline__ int kth_tile(int k, int num_tiles, int lpt) {
+  int t;
+  if (lpt) {
+    const int G = gridDim.x;
+    t = k * G + ((k & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  } else {
+    t = (blockIdx.x + (k >> 1) * gridDim.x) * 2 + (k & 1);
+  }
+  return t < num_tiles ? t : -1;
 }
 
 __device__ __forceinline__ TileInfo tile_info(int tile, const FwdParams& p) {
   TileInfo ti;
-  const int bh = tile / p.num_mblocks;
-  const int r = tile % p.num_mblocks;
-  const int mblk = (r & 1) ? (r >> 1) : p.num_mblocks - 1 - (r >> 1);
+  int bh, mblk;
+  if (p.lpt) {
+    const int nbh = p.H * p.B;
+    bh = tile % nbh;
+    mblk = p.num_mblocks - 1 - tile / nbh;
+  } else {
+    bh = tile / p.num_mblocks;
+    const int r = tile % p.num_mblocks;
+    mblk = (r & 1) ? (r >> 1) : p.num_mblocks - 1 - (r >> 1);
+  }
   ti.b = bh / p.H;
   ti.h = bh % p.H;
   ti.hk = ti.h / (p.H / p.HKV);
@@ -207,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tm_k);
       prefetch_tensormap(&tm_v);
       uint32_t g = 0, tt = 0;  // K/V tiles loaded, tiles started
-      for (int k = 0, tile = kth_tile(0); tile < num_tiles; tile = kth_tile(++k), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info(tile, p);
         if (!mbar_wait(&bar->q_empty, (tt & 1) ^ 1, abort, p.err)) break;
         mbar_expect_tx(&bar->q_full, 2 * L::kTileBytes);
@@ -238,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
       uint32_t g = 0, tt = 0, cs[2] = {0, 0};  // K/V tiles consumed, tiles, P tiles consumed per x
       bool ok = true;
-      for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info(tile, p);
         if (!(ok = mbar_wait(&bar->q_full, tt & 1, abort, p.err))) break;
         if (!(ok = mbar_wait(&bar->k_full[g & 1], (g >> 1) & 1, abort, p.err))) break;
@@ -300,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c = p.scale_log2;
     uint32_t cs = 0, tt = 0;
     bool ok = true;
-    for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+    for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
       const TileInfo ti = tile_info(tile, p);
       const int t = ti.t0 + x * BM + row;  // query row
       const int n = x ? ti.nB : ti.nA;
@@ -523,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tm_k);
       uint32_t gk = 0, tt = 0;
       bool ok = true;
-      for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info(tile, p);
         if (!(ok = mbar_wait(&bar->q_empty, (tt & 1) ^ 1, abort, p.err))) break;
         mbar_expect_tx(&bar->q_full, 2 * L::kTileBytes);
@@ -541,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tm_v);
       uint32_t gv = 0;
       bool ok = true;
-      for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k)) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt)) {
         const TileInfo ti = tile_info(tile, p);
         for (int j = 0; j < ti.nB; ++j, ++gv) {
           const int st = gv & 1;
@@ -564,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++nqk[x];
         return true;
       };
-      for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info(tile, p);
         if (!(ok = mbar_wait(&bar->q_full, tt & 1, abort, p.err))) break;
         for (int j = 0; ok && j < ti.nB; ++j) {
@@ -582,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tP[2] = {tmem + 384, tmem + 448};
       uint32_t gv = 0, tt = 0, npf[2] = {0, 0};
       bool ok = true;
-      for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info(tile, p);
         for (int j = 0; ok && j < ti.nB; ++j) {
           const int st = gv & 1;
@@ -616,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c = p.scale_log2;
     uint32_t cs = 0, tt = 0, pw = 0;  // S tiles read, work tiles, P tiles written
     bool ok = true;
-    for (int k = 0, tile = kth_tile(0); ok && tile < num_tiles; tile = kth_tile(++k), ++tt) {
+    for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
       const TileInfo ti = tile_info(tile, p);
       const int t = ti.t0 + x * BM + row;
       const int n = x ? ti.nB : ti.nA;
@@ -792,8 +814,12 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   if (nblk > 0x7fffffffLL) return set_error(PDB_ERR_SHAPE, "bf16 flash: grid too large");
   int dev = 0;
   cudaGetDevice(&dev);
-  const int64_t units = (nblk + 1) / 2;  // tile pairs
-  const int64_t grid = units < sm_count(dev) ? units : sm_count(dev);  // persistent: one CTA per SM
+  const int64_t pairs = (nblk + 1) / 2;
+  const int sms = sm_count(dev);
+  // a job of fewer than 4 waves of pairs schedules single tiles heaviest first
+  p.lpt = pairs < 4 * (int64_t)sms ? 1 : 0;
+  const int64_t units = p.lpt ? nblk : pairs;
+  const int64_t grid = units < sms ? units : sms;  // persistent: one CTA per SM
   const int smem = Smem<D>::kTotal;
   if (D == 64) {  // P in its own TMEM columns (656 vs 610 TFLOP/s at B8 H32 S4096 causal)
     auto kern = p.key_lo ? flash_fwd_d64_kernel<true> : flash_fwd_d64_kernel<false>;

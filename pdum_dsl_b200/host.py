@@ -8,7 +8,9 @@ chunks and runs three CUDA streams -- host-to-device copies, the sm_100a
 kernel, device-to-host copies -- so the PCIe traffic of one chunk overlaps the
 compute of the next and both copy directions run at once.  Device staging
 buffers are allocated per call (two chunks deep) through torch's caching
-allocator.
+allocator.  Host tensors may be float32 / float64 (the reference's numpy
+convention) while the kernel runs bf16: each chunk is copied in its host dtype
+and cast on the device, and the output is cast back before its copy out.
 """
 
 from __future__ import annotations
@@ -22,10 +24,12 @@ from . import kernels
 
 def flash_attention_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, *,
                          scale: float | None = None, causal: bool = False, chunks: int = 8,
-                         device: torch.device | None = None) -> torch.Tensor:
+                         device: torch.device | None = None, compute_dtype: torch.dtype | None = None,
+                         q_start: int = 0, key_intervals=None) -> torch.Tensor:
     """q (B, Hq, T, D), k / v (B, Hkv, S, D), out (B, Hq, T, Dv): contiguous host
-    tensors (pin them for full PCIe speed).  Returns ``out`` after the device
-    work has completed."""
+    tensors (pin them for full PCIe speed).  ``compute_dtype`` (default: q's
+    dtype) is what the kernel runs in.  Returns ``out`` after the device work has
+    completed."""
     for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
         if t.is_cuda or not t.is_contiguous() or t.dim() != 4:
             raise ValueError(f"{name}: expected a contiguous 4-D host tensor")
@@ -48,8 +52,14 @@ def flash_attention_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out:
         s.wait_stream(cur)
     depth = 2
     size = max(hi - lo for lo, hi in bounds)
+    cdt = compute_dtype or q.dtype
+    cast = any(t.dtype != cdt for t in (q, k, v, out))
     bufs = [{name: torch.empty((size,) + tuple(t.shape[1:]), dtype=t.dtype, device=dev)
              for name, t in (("q", qf), ("k", kf), ("v", vf), ("o", of))} for _ in range(depth)]
+    if cast:  # device-side casts between the host dtype and the compute dtype
+        for b in bufs:
+            for name in ("q", "k", "v", "o"):
+                b["c" + name] = torch.empty(b[name].shape, dtype=cdt, device=dev)
     loaded = [torch.cuda.Event() for _ in range(n)]
     computed = [torch.cuda.Event() for _ in range(n)]
     drained = [torch.cuda.Event() for _ in range(n)]
@@ -66,11 +76,19 @@ def flash_attention_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out:
             s_cmp.wait_event(loaded[i])
             if i >= depth:
                 s_cmp.wait_event(drained[i - depth])  # output of this slot copied out
-            qj = b["q"][:m].reshape(1, m * r, T, D)
-            kj = b["k"][:m].reshape(1, m, *kf.shape[2:])
-            vj = b["v"][:m].reshape(1, m, *vf.shape[2:])
-            kernels.flash_attention(qj, kj, vj, scale=scale, causal=causal,
-                                    out=b["o"][:m].reshape(1, m * r, T, of.shape[3]))
+            src = {}
+            for name in ("q", "k", "v"):
+                if cast:
+                    b["c" + name][:m].copy_(b[name][:m])
+                src[name] = b[("c" if cast else "") + name][:m]
+            ob = b["co" if cast else "o"][:m]
+            qj = src["q"].reshape(1, m * r, T, D)
+            kj = src["k"].reshape(1, m, *kf.shape[2:])
+            vj = src["v"].reshape(1, m, *vf.shape[2:])
+            kernels.flash_attention(qj, kj, vj, scale=scale, causal=causal, q_start=q_start,
+                                    key_intervals=key_intervals, out=ob.reshape(1, m * r, T, of.shape[3]))
+            if cast:
+                b["o"][:m].copy_(ob)
             computed[i].record(s_cmp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(computed[i])

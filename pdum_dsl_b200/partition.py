@@ -204,3 +204,47 @@ def sharded_attention(q, k, v, *, world: int, rank: int, attend, gather: bool = 
     full = torch.empty((world * per[0] * r, T, v.shape[3]), dtype=o.dtype, device=o.device)
     dist.all_gather_into_tensor(full, o.reshape(per[0] * r, T, v.shape[3]).contiguous(), group=group)
     return full.reshape(B, Hq, T, v.shape[3])
+
+
+def chunked_shards(n_units: int, world: int, rank: int, chunks: int) -> list[Shard]:
+    """The partition for a final gather that overlaps the computation.
+
+    The units are cut into ``chunks`` consecutive slabs and every slab is split
+    evenly over the ranks: rank r owns block r of each slab.  The all-gather of
+    one slab's outputs (``all_gather_into_tensor``, rank-major) then lands
+    exactly on that slab of the global output -- no reordering copy -- while
+    the next slab computes.  Requires chunks * world to divide the unit count."""
+    if n_units % (chunks * world):
+        raise ValueError(f"{n_units} units do not split into {chunks} slabs x {world} ranks")
+    per = n_units // (chunks * world)
+    return [Shard(rank, world, c * per * world + rank * per, c * per * world + (rank + 1) * per)
+            for c in range(chunks)]
+
+
+def gather_overlapped(attend, slabs_in, slabs_out, *, group=None, comm_stream=None):
+    """For each slab: ``attend(*slabs_in[c])`` -> this rank's block of outputs, then
+    ``all_gather_into_tensor(slabs_out[c], block)`` -- on ``comm_stream`` (CUDA)
+    once that block's kernel has completed, so the gather of slab c runs under
+    the computation of slab c + 1.  ``slabs_out[c]`` is the global output of the
+    slab (world x block, rank-major).  Returns the per-slab blocks."""
+    import torch
+    import torch.distributed as dist
+
+    blocks = []
+    cur = torch.cuda.current_stream() if comm_stream is not None else None
+    for ins, out in zip(slabs_in, slabs_out):
+        blk = attend(*ins)
+        blocks.append(blk)
+        flat = blk.reshape(out.shape[0] // dist.get_world_size(group), *out.shape[1:])
+        if comm_stream is None:
+            dist.all_gather_into_tensor(out, flat.contiguous(), group=group)
+            continue
+        done = torch.cuda.Event()
+        done.record(cur)
+        comm_stream.wait_event(done)
+        with torch.cuda.stream(comm_stream):
+            dist.all_gather_into_tensor(out, flat, group=group)
+            flat.record_stream(comm_stream)
+    if comm_stream is not None:
+        cur.wait_stream(comm_stream)
+    return blocks

@@ -259,11 +259,68 @@ class _Runner:
         return (o, *stats)
 
     # ------------------------------------------------------------------ host path
-    def __call__(self, values):
+    def _attention_host(self, values, out):
+        """Attention on host values through the pipelined host entry point: the
+        (batch, KV-head) units are chunked so host-to-device copies, the kernel and
+        device-to-host copies overlap (host.flash_attention_host)."""
+        import torch
+
+        from .host import flash_attention_host
+
+        spec = self.spec
+        rid = list(spec.riders)
+        qg = [spec.group] if spec.group else []
+        ts = [v if isinstance(v, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(v)) for v in values]
+        q = ts[spec.q].permute(*[spec.q_dims.index(n) for n in rid + qg + [spec.t, spec.e]])
+        k = ts[spec.k].permute(*[spec.k_dims.index(n) for n in rid + [spec.s, spec.e]])
+        v = ts[spec.v].permute(*[spec.v_dims.index(n) for n in rid + [spec.s, spec.o]])
+        lead = list(k.shape[:-2])
+        while len(lead) < 2:
+            lead.insert(0, 1)
+        Bn, HK = lead
+        G = q.shape[len(rid)] if spec.group else 1
+        T, D = q.shape[-2:]
+        S, DV = v.shape[-2:]
+        q4 = q.reshape(Bn, HK * G, T, D).contiguous()
+        k4 = k.reshape(Bn, HK, S, D).contiguous()
+        v4 = v.reshape(Bn, HK, S, DV).contiguous()
+        onames = tuple(rid + qg + [spec.t, spec.o])
+        perm = [onames.index(n) for n in spec.out_dims]
+        oshape = tuple(list(q.shape[:-2]) + [T, DV])
+        if out is None:
+            o4 = torch.empty((Bn, HK * G, T, DV), dtype=q4.dtype)
+        else:  # the caller's host buffer, in the yield's dim order
+            inv = [spec.out_dims.index(n) for n in onames]
+            o4 = out.permute(*inv).reshape(Bn, HK * G, T, DV)
+            if o4.data_ptr() != out.data_ptr() or not o4.is_contiguous():
+                raise ValueError("out must be a contiguous host tensor in the yield's dim order")
+        cdt = torch.bfloat16 if self.dtype == "bf16" else torch.float32
+        flash_attention_host(q4, k4, v4, o4, scale=1.0 if spec.scale is None else spec.scale, causal=spec.causal,
+                             compute_dtype=cdt, q_start=spec.t_start, key_intervals=spec.mask)
+        if out is not None:
+            return out
+        return o4.reshape(oshape).permute(*perm).float().numpy()
+
+    def __call__(self, values, out=None):
+        """values: host arrays (numpy, or CPU torch tensors -- pinned for full copy
+        speed), positional per region param in type-dim order.  ``out`` (optional,
+        attention only) is a host tensor in the yield's dim order that receives
+        the result instead of a freshly allocated array."""
         import torch
 
         if not torch.cuda.is_available():
             raise RuntimeError("compile_tile runners execute on a CUDA device (sm_100a); none is available")
+        if isinstance(self.spec, AttentionSpec) and not self.spec.artifacts:
+            res = self._attention_host(values, out)
+            if not self.checked:
+                from .kernels import check_device_errors
+
+                check_device_errors()
+                self.checked = True
+            return res
+        if out is not None:
+            raise ValueError("out= is taken by the attention runner only")
+        values = [v.numpy() if isinstance(v, torch.Tensor) else v for v in values]
         dt = torch.bfloat16 if self.dtype == "bf16" else torch.float32
         ins = []
         for i, v in enumerate(values):
@@ -315,8 +372,8 @@ def compile_tile(region, launch: tuple = (), prune: tuple = (), *, dtype: str = 
     _check_launch(spec, launch, prune, region)
     runner = _Runner(region, spec, dtype, launch, prune)
 
-    def run(values):
-        return runner(values)
+    def run(values, out=None):
+        return runner(values, out=out)
 
     run.run_t = runner.run_t
     run.source = runner.source

@@ -219,3 +219,28 @@ def test_ledger_measures_and_greens_planned_groups(cuda, dsl):
     with no_reanalysis():
         again = ledger.sm100_us(plan.groups[0].kernel, machine=machine, dtype="bf16", reps=5)
     assert again.key == facts[0].key
+
+
+@pytest.mark.parametrize("group", [None, 2])
+def test_runner_host_path_pinned_buffers_and_out(cuda, dsl, group):
+    """compile_tile's host call with pinned bf16 torch buffers and a caller-owned
+    output (the pipelined host path) equals the device path bit for bit."""
+    import torch
+
+    from pdum_dsl_b200.regions import attention_region
+    from pdum_dsl_b200.tile import compile_tile
+
+    H = 4
+    region = attention_region(B=2, H=H if group is None else H // group, T=300, D=128, causal=True,
+                              scale=0.088, group=group)
+    run = compile_tile(region, dtype="bf16")
+    g = torch.Generator().manual_seed(9)
+    vals = [torch.randn(tuple(d.stop - d.start for d in p.type.dims), generator=g).to(torch.bfloat16).pin_memory()
+            for p in region.params]
+    yld = region.body[-1].args[0]
+    out = torch.empty(tuple(d.stop - d.start for d in yld.type.dims), dtype=torch.bfloat16).pin_memory()
+    assert run(vals, out=out) is out
+    want = run.run_t(*[v.cuda() for v in vals]).cpu()
+    assert torch.equal(out, want)
+    got_np = run([v.float().numpy() for v in vals])  # the reference's numpy convention
+    np.testing.assert_array_equal(got_np, want.float().numpy())
