@@ -495,12 +495,34 @@ struct PointwiseArgs {
   int64_t xs[3], ys[3];
 };
 
-__global__ void pointwise_f32_kernel(const PointwiseArgs d, const EwProgram pg) {
-  const int64_t total = d.batch * d.m * d.n;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t j = e % d.n, i = (e / d.n) % d.m, b = e / (d.n * d.m);
-    const float v = d.x[b * d.xs[0] + i * d.xs[1] + j * d.xs[2]];
-    d.y[b * d.ys[0] + i * d.ys[1] + j * d.ys[2]] = ew_apply(pg, v, b, i, j);
+// Work items are 1024-column segments of one (batch, row): a block of 256
+// threads takes a segment, each thread four consecutive columns -- one 16-byte
+// load and store when both tensors are unit-stride along n and 16-byte aligned
+// (`vec`), else four scalar accesses.  The (batch, row) coordinates are derived
+// once per segment, not per element.
+constexpr int kPwThreads = 256, kPwSeg = 4 * kPwThreads;
+
+__global__ void __launch_bounds__(kPwThreads) pointwise_f32_kernel(const PointwiseArgs d, const EwProgram pg,
+                                                                   const int vec) {
+  const int64_t rows = d.batch * d.m;
+  const int64_t nseg = (d.n + kPwSeg - 1) / kPwSeg;
+  for (int64_t w = blockIdx.x; w < rows * nseg; w += gridDim.x) {
+    const int64_t r = w / nseg, sg = w - r * nseg;
+    const int64_t b = r / d.m, i = r - b * d.m;
+    const int64_t j0 = sg * kPwSeg + 4 * threadIdx.x;
+    if (j0 >= d.n) continue;
+    const float* xr = d.x + b * d.xs[0] + i * d.xs[1];
+    float* yr = d.y + b * d.ys[0] + i * d.ys[1];
+    if (vec && j0 + 4 <= d.n) {
+      float4 v = __ldcs(reinterpret_cast<const float4*>(xr + j0));
+      v.x = ew_apply(pg, v.x, b, i, j0);
+      v.y = ew_apply(pg, v.y, b, i, j0 + 1);
+      v.z = ew_apply(pg, v.z, b, i, j0 + 2);
+      v.w = ew_apply(pg, v.w, b, i, j0 + 3);
+      __stcs(reinterpret_cast<float4*>(yr + j0), v);
+    } else {
+      for (int64_t j = j0; j < j0 + 4 && j < d.n; ++j) yr[j * d.ys[2]] = ew_apply(pg, xr[j * d.xs[2]], b, i, j);
+    }
   }
 }
 
@@ -627,10 +649,14 @@ extern "C" int pdb_pointwise_f32(const pdb_pointwise_desc* d, void* stream) {
   const EwProgram pg = make_program(d->n_ops, d->ops);
   int dev = 0;
   cudaGetDevice(&dev);
-  const int64_t blocks = (total + 255) / 256;
-  const int64_t cap = (int64_t)sm_count(dev) * 16;
+  const int64_t blocks = d->batch * d->m * ((d->n + kPwSeg - 1) / kPwSeg);
+  const int64_t cap = (int64_t)sm_count(dev) * 8;
   PointwiseArgs a{d->x, d->y, d->batch, d->m, d->n, {d->x_stride[0], d->x_stride[1], d->x_stride[2]},
                   {d->y_stride[0], d->y_stride[1], d->y_stride[2]}};
-  pointwise_f32_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, static_cast<cudaStream_t>(stream)>>>(a, pg);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(d->x) | reinterpret_cast<uintptr_t>(d->y)) & 15u) == 0;
+  const int vec = aligned && d->x_stride[2] == 1 && d->y_stride[2] == 1 && ((d->x_stride[0] | d->x_stride[1] |
+                  d->y_stride[0] | d->y_stride[1]) & 3) == 0;
+  pointwise_f32_kernel<<<(unsigned)(blocks < cap ? blocks : cap), kPwThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      a, pg, vec);
   return cuda_status(cudaGetLastError(), "pointwise launch");
 }

@@ -13,8 +13,9 @@
 // space).  The host compiles such a carve into one program of SSA steps; this
 // kernel runs it.
 //
-// Layout: one CTA owns 64 rows of the program space and walks all columns in
-// 32-column tiles.  The per-element values live in a shared-memory register
+// Layout: one CTA owns 64 rows of the program space and walks its columns in
+// 32-column tiles (all of them, or -- for sum outputs of a job with few row
+// blocks -- a contiguous share, the shares' partial sums added atomically).  The per-element values live in a shared-memory register
 // file R[reg][64 * 32] (element e = row * 32 + col; thread tid owns elements
 // tid + 256 i, i < 8, so each warp owns whole 32-column rows and every global
 // tile access is a coalesced 128-byte row).  Score contractions C[t, s] =
@@ -37,6 +38,7 @@ constexpr int SP_XMAX = 128;  // contraction-output columns per launch
 
 struct SpParams {
   pdb_score_program_desc d;
+  int csplit;  // CTAs per row block along the columns (sum outputs then combine with atomicAdd)
 };
 
 __device__ __forceinline__ float sp_apply1(int op, float a) {
@@ -127,6 +129,10 @@ __global__ void __launch_bounds__(SP_THREADS) score_program_kernel(const __grid_
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t bidx = blockIdx.y;
   const int64_t t0 = (int64_t)blockIdx.x * SP_ROWS;
+  // this CTA's column tiles [c_lo, c_hi) of the row block
+  const int64_t ntiles = (d.cols + SP_COLS - 1) / SP_COLS;
+  const int64_t c_lo = ntiles * blockIdx.z / P.csplit, c_hi = ntiles * (blockIdx.z + 1) / P.csplit;
+  const bool atomic_out = P.csplit > 1;
   // shared memory: register file, contraction staging, W staging
   float* R = smem;                                                   // n_regs x 2048
   float(*As)[SP_ROWS + 1] = reinterpret_cast<float(*)[SP_ROWS + 1]>(R + d.n_regs * SP_ROWS * SP_COLS);
@@ -143,7 +149,7 @@ __global__ void __launch_bounds__(SP_THREADS) score_program_kernel(const __grid_
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[u][j] = 0.f;
 
-  for (int64_t s0 = 0; s0 < d.cols; s0 += SP_COLS) {
+  for (int64_t s0 = c_lo * SP_COLS; s0 < c_hi * SP_COLS; s0 += SP_COLS) {
     for (int k = 0; k < d.n_ops; ++k) {
       const pdb_sp_op& o = d.ops[k];
       float* Rd = R + o.dst * (SP_ROWS * SP_COLS);
@@ -239,15 +245,31 @@ __global__ void __launch_bounds__(SP_THREADS) score_program_kernel(const __grid_
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int x = tx + 16 * j;
-        if (x < d.xdim) d.out[bidx * d.out_stride[0] + t * d.out_stride[1] + x * d.out_stride[2]] = acc[u][j];
+        if (x >= d.xdim) continue;
+        float* o = d.out + bidx * d.out_stride[0] + t * d.out_stride[1] + x * d.out_stride[2];
+        if (atomic_out) atomicAdd(o, acc[u][j]);
+        else *o = acc[u][j];
       }
     }
   } else if (mode != PDB_SP_OUT_TILE && lane == 0) {
 #pragma unroll
     for (int i = 0; i < SP_EPT; ++i) {
       const int64_t t = t0 + warp + 8 * i;
-      if (t < d.rows) d.out[bidx * d.out_stride[0] + t * d.out_stride[1]] = red[i];
+      if (t >= d.rows) continue;
+      float* o = d.out + bidx * d.out_stride[0] + t * d.out_stride[1];
+      if (atomic_out) atomicAdd(o, red[i]);
+      else *o = red[i];
     }
+  }
+}
+
+// zeroes out[b, t (, x)] ahead of a column-split launch that accumulates into it
+__global__ void sp_zero_kernel(float* out, int64_t batch, int64_t rows, int64_t xdim, int64_t s0, int64_t s1,
+                               int64_t s2) {
+  const int64_t total = batch * rows * xdim;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t x = e % xdim, t = (e / xdim) % rows, b = e / (xdim * rows);
+    out[b * s0 + t * s1 + x * s2] = 0.f;
   }
 }
 
@@ -319,9 +341,23 @@ extern "C" int pdb_score_program_f32(const pdb_score_program_desc* d, void* stre
   const size_t smem = sp_smem_bytes(d->n_regs);
   cudaError_t e = cudaFuncSetAttribute(score_program_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return cuda_status(e, "score program smem attribute");
-  dim3 grid((unsigned)((d->rows + SP_ROWS - 1) / SP_ROWS), (unsigned)d->batch);
+  const int64_t row_blocks = (d->rows + SP_ROWS - 1) / SP_ROWS;
+  const int64_t col_tiles = (d->cols + SP_COLS - 1) / SP_COLS;
   SpParams P;
   P.d = *d;
+  // Few row blocks leave most SMs idle: sum-type outputs split the columns over
+  // more CTAs (about two waves, at least four column tiles each) and add their
+  // partial results atomically (the f32 summation order then varies run to run).
+  P.csplit = 1;
+  if (mode == PDB_SP_OUT_ROW_SUM || mode == PDB_SP_OUT_ROW_CONTRACT) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int64_t want = (2 * (int64_t)sm_count(dev) + row_blocks * d->batch - 1) / (row_blocks * d->batch);
+    const int64_t most = col_tiles / 4 > 1 ? col_tiles / 4 : 1;
+    P.csplit = (int)(want < most ? (want > 1 ? want : 1) : most);
+    if (P.csplit > 64) P.csplit = 64;
+  }
+  dim3 grid((unsigned)row_blocks, (unsigned)d->batch, (unsigned)P.csplit);
   // contraction outputs wider than SP_XMAX: one launch per 128-column slab of w / out
   const int64_t xdim = mode == PDB_SP_OUT_ROW_CONTRACT ? d->xdim : 1;
   for (int64_t x0 = 0; x0 < xdim; x0 += SP_XMAX) {
@@ -329,6 +365,11 @@ extern "C" int pdb_score_program_f32(const pdb_score_program_desc* d, void* stre
       P.d.w = d->w + x0 * d->w_stride[2];
       P.d.out = d->out + x0 * d->out_stride[2];
       P.d.xdim = xdim - x0 < SP_XMAX ? xdim - x0 : SP_XMAX;
+    }
+    if (P.csplit > 1) {
+      const int64_t xd = mode == PDB_SP_OUT_ROW_CONTRACT ? P.d.xdim : 1;
+      sp_zero_kernel<<<256, 256, 0, s>>>(P.d.out, d->batch, d->rows, xd, d->out_stride[0], d->out_stride[1],
+                                         mode == PDB_SP_OUT_ROW_CONTRACT ? d->out_stride[2] : 0);
     }
     score_program_kernel<<<grid, SP_THREADS, smem, s>>>(P);
     e = cudaGetLastError();
