@@ -26,8 +26,6 @@
 // it by more than 8 (a factor 256), so most tiles need no O correction; the
 // true max is tracked on the side for the m / den / lse outputs.
 #include <cfloat>
-#include <cstdlib>
-#include <mutex>
 
 #include "common.cuh"
 #include "tma.h"
@@ -774,467 +772,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// D = 128 on CTA pairs (a cluster of two CTAs on two SMs, cta_group::2 MMAs).
-// The single-CTA kernel reads, per 128-key step, Q_A, Q_B, K twice and V twice
-// from shared memory plus the TMA writes of K and V: ~256 KB against 128 B per
-// cycle, as long as the tensor core's 2048-cycle ideal for the step, so the
-// MMAs stretch (~1700 instead of ~1024 cycles per tile under load).  Paired,
-// one M256 MMA covers 128 query rows of each CTA and reads B (the key tile for
-// Q K^T, the value tile for P V) half from each CTA: each CTA stages only 64
-// keys of K (all 128 features) and 64 features of V (all 128 keys) per step,
-// so its shared-memory traffic per step drops to ~160 KB.
-// Work tile = 512 query rows of one head: tile A = rows [t0, t0+256) (rank r
-// holds [t0 + 128 r, +128)), tile B = rows [t0+256, t0+512).  Per CTA the
-// roles, TMEM layout (S_A, S_B, O_A, O_B; P aliases S) and the softmax are the
-// single-CTA kernel's; rank 0's thread of warp 1 issues every MMA of the pair.
-// Barriers: q_full, k_full, v_full, p_full, o_empty of rank 0 count the pair
-// (TMA bytes of both CTAs; arrivals of both CTAs' softmax warps); q_empty,
-// k_empty, v_empty, s_full, o_full of each CTA receive rank 0's pair commits.
-constexpr int kPairStages = 3;
-constexpr int kPairKBox = 64 * 64 * 2;  // K half: 64 keys x 64 features per box, two boxes
-struct PairSmem {
-  static constexpr int kTileBytes = BM * 128 * 2;  // Q tile: 128 rows x 128 features
-  static constexpr int kHalf = 64 * 128 * 2;       // K or V half tile per CTA
-  static constexpr int kQ0 = 0;
-  static constexpr int kQ1 = kTileBytes;
-  static constexpr int kK = 2 * kTileBytes;
-  static constexpr int kV = kK + kPairStages * kHalf;
-  static constexpr int kStg = kV + kPairStages * kHalf;  // O staging (32 KB)
-  static constexpr int kBar = kStg + kTileBytes;
-  static constexpr int kTotal = kBar + 1024 + 1024;
-};
-
-struct __align__(8) PairBarriers {
-  uint64_t q_full, q_empty;
-  uint64_t k_full[kPairStages], k_empty[kPairStages];
-  uint64_t v_full[kPairStages], v_empty[kPairStages];
-  uint64_t s_full[2], p_full[2], o_full[2], o_empty[2];
-  uint64_t stg_free[4];
-  uint32_t tmem_base;
-  int abort;
-};
-
-__device__ __forceinline__ void mma_qk_pair(uint32_t d_tmem, uint32_t q_saddr, uint32_t k_saddr) {
-  constexpr uint32_t idesc = idesc_bf16(2 * BM, BN, 0, 0);
-#pragma unroll
-  for (int kk = 0; kk < 128 / 16; ++kk)
-    mma_ss_pair(d_tmem, sdesc_sw128(q_saddr + (kk >> 2) * kBoxBytes + (kk & 3) * 32, 16, 1024),
-                sdesc_sw128(k_saddr + (kk >> 2) * kPairKBox + (kk & 3) * 32, 16, 1024), idesc, kk > 0);
-}
-
-__device__ __forceinline__ void mma_pv_pair(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_saddr, bool acc) {
-  constexpr uint32_t idesc = idesc_bf16(2 * BM, 128, 0, 1);
-#pragma unroll
-  for (int kk = 0; kk < BN / 16; ++kk)
-    mma_ts_pair(o_tmem, p_tmem + kk * 8, sdesc_sw128(v_saddr + kk * 2048, kBoxBytes, 1024), idesc,
-                (acc || kk > 0) ? 1u : 0u);
-}
-
-// the k-th work tile of pair `pr` of `npr` (see kth_tile; ordinals over 512-row tiles)
-__device__ __forceinline__ int kth_tile_pair(int k, int num_tiles, int lpt, int pr, int npr) {
-  int t;
-  if (lpt) t = k * npr + ((k & 1) ? npr - 1 - pr : pr);
-  else t = (pr + (k >> 1) * npr) * 2 + (k & 1);
-  return t < num_tiles ? t : -1;
-}
-
-__device__ __forceinline__ TileInfo tile_info_pair(int tile, const FwdParams& p) {
-  TileInfo ti;
-  int bh, mblk;
-  if (p.lpt) {
-    const int nbh = p.H * p.B;
-    bh = tile % nbh;
-    mblk = p.num_mblocks - 1 - tile / nbh;
-  } else {
-    bh = tile / p.num_mblocks;
-    const int r = tile % p.num_mblocks;
-    mblk = (r & 1) ? (r >> 1) : p.num_mblocks - 1 - (r >> 1);
-  }
-  ti.b = bh / p.H;
-  ti.h = bh % p.H;
-  ti.hk = ti.h / (p.H / p.HKV);
-  ti.t0 = mblk * 4 * BM;
-  const int n_kv = (p.S + BN - 1) / BN;
-  int n[2];
-  ti.j0 = 0;
-  if (p.key_lo && p.mask_monotone) {
-    const int first = ti.t0 < p.T ? ti.t0 : p.T - 1;
-    ti.j0 = __ldg(p.key_lo + first) / BN;
-  }
-#pragma unroll
-  for (int x = 0; x < 2; ++x) {
-    int last_row = ti.t0 + x * 2 * BM + 2 * BM - 1;
-    if (last_row > p.T - 1) last_row = p.T - 1;
-    int c = n_kv;
-    if (p.causal) c = (last_row + p.q_start) / BN + 1;
-    else if (p.key_lo && p.mask_monotone) c = (__ldg(p.key_hi + last_row) + BN - 1) / BN;
-    c = c < n_kv ? c : n_kv;
-    n[x] = c - ti.j0 > 1 ? c - ti.j0 : 1;
-  }
-  ti.nA = n[0];
-  ti.nB = n[1] < n[0] ? n[0] : n[1];
-  return ti;
-}
-
-template <bool kKeyMask>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    flash_fwd_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                          const FwdParams p) {
-  constexpr int D = 128;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  using L = PairSmem;
-  PairBarriers* bar = reinterpret_cast<PairBarriers*>(smem + L::kBar);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const int pr = blockIdx.x >> 1, npr = gridDim.x >> 1;
-  const int num_tiles = p.num_mblocks * p.H * p.B;
-
-  if (threadIdx.x == 0) {
-    mbar_init(&bar->q_full, 1);
-    mbar_init(&bar->q_empty, 1);
-    for (int i = 0; i < kPairStages; ++i) {
-      mbar_init(&bar->k_full[i], 1);
-      mbar_init(&bar->k_empty[i], 1);
-      mbar_init(&bar->v_full[i], 1);
-      mbar_init(&bar->v_empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar->s_full[i], 1);
-      mbar_init(&bar->p_full[i], 2 * BM / 32);  // one arrival per softmax warp of the pair
-      mbar_init(&bar->o_full[i], 1);
-      mbar_init(&bar->o_empty[i], 2 * BM / 32);
-    }
-    for (int i = 0; i < 4; ++i) mbar_init(&bar->stg_free[i], 1);
-    bar->abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == 2) {
-    tmem_alloc_pair(&bar->tmem_base, 512);
-    tmem_relinquish_pair();
-  }
-  tc_fence_before();
-  cluster_sync_all();
-  tc_fence_after();
-  const uint32_t tmem = bar->tmem_base;
-  volatile int* abort = &bar->abort;
-  const uint32_t sQ0 = smem_u32(smem + L::kQ0), sQ1 = smem_u32(smem + L::kQ1);
-  const uint32_t sK = smem_u32(smem + L::kK), sV = smem_u32(smem + L::kV);
-
-  if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
-    if (warp == 0 && lane == 0) {
-      // ---------------------------------------------------------- producer (both CTAs: own halves)
-      prefetch_tensormap(&tm_q);
-      prefetch_tensormap(&tm_k);
-      prefetch_tensormap(&tm_v);
-      const uint32_t q_full0 = mapa_shared(smem_u32(&bar->q_full), 0);
-      uint32_t g = 0, tt = 0;
-      bool ok = true;
-      for (int k = 0, tile = kth_tile_pair(0, num_tiles, p.lpt, pr, npr); ok && tile >= 0;
-           tile = kth_tile_pair(++k, num_tiles, p.lpt, pr, npr), ++tt) {
-        const TileInfo ti = tile_info_pair(tile, p);
-        if (!(ok = mbar_wait_cluster(&bar->q_empty, (tt & 1) ^ 1, abort, p.err))) break;
-        if (rank == 0) mbar_expect_tx(&bar->q_full, 4 * L::kTileBytes);
-        for (int i = 0; i < 2; ++i) {
-          tma_load_4d_pair(smem + L::kQ0 + i * kBoxBytes, &tm_q, q_full0, i * 64, ti.t0 + (int)rank * BM, ti.h, ti.b);
-          tma_load_4d_pair(smem + L::kQ1 + i * kBoxBytes, &tm_q, q_full0, i * 64, ti.t0 + 2 * BM + (int)rank * BM,
-                           ti.h, ti.b);
-        }
-        for (int j = 0; j < ti.nB; ++j, ++g) {
-          const int st = g % kPairStages;
-          const uint32_t ph = (g / kPairStages) & 1;
-          const int key0 = (ti.j0 + j) * BN;
-          if (!(ok = mbar_wait_cluster(&bar->k_empty[st], ph ^ 1, abort, p.err))) break;
-          if (rank == 0) mbar_expect_tx(&bar->k_full[st], 2 * L::kHalf);
-          const uint32_t kf0 = mapa_shared(smem_u32(&bar->k_full[st]), 0);
-          for (int i = 0; i < 2; ++i)  // keys [key0 + 64 r, +64), features [64 i, +64)
-            tma_load_4d_pair(smem + L::kK + st * L::kHalf + i * kPairKBox, &tm_k, kf0, i * 64,
-                             key0 + (int)rank * 64, ti.hk, ti.b);
-          if (!(ok = mbar_wait_cluster(&bar->v_empty[st], ph ^ 1, abort, p.err))) break;
-          if (rank == 0) mbar_expect_tx(&bar->v_full[st], 2 * L::kHalf);
-          // keys [key0, +128), features [64 r, +64)
-          tma_load_4d_pair(smem + L::kV + st * L::kHalf, &tm_v, mapa_shared(smem_u32(&bar->v_full[st]), 0),
-                           (int)rank * 64, key0, ti.hk, ti.b);
-        }
-      }
-    } else if (warp == 1 && lane == 0 && rank == 0) {
-      // -------------------------------------------------------- MMA issuer (rank 0)
-      const uint32_t tS[2] = {tmem + 0, tmem + 128};
-      const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
-      auto commit2 = [](uint64_t* b) {
-        const uint32_t a = smem_u32(b);
-        tc_commit_pair(a);
-        tc_commit_pair(mapa_shared(a, 1));
-      };
-      uint32_t g = 0, tt = 0, cs[2] = {0, 0};
-      bool ok = true;
-      for (int k = 0, tile = kth_tile_pair(0, num_tiles, p.lpt, pr, npr); ok && tile >= 0;
-           tile = kth_tile_pair(++k, num_tiles, p.lpt, pr, npr), ++tt) {
-        const TileInfo ti = tile_info_pair(tile, p);
-        if (!(ok = mbar_wait_cluster(&bar->q_full, tt & 1, abort, p.err))) break;
-        if (!(ok = mbar_wait_cluster(&bar->k_full[g % kPairStages], (g / kPairStages) & 1, abort, p.err))) break;
-        tc_fence_after();
-        mma_qk_pair(tS[0], sQ0, sK + (g % kPairStages) * L::kHalf);
-        commit2(&bar->s_full[0]);
-        mma_qk_pair(tS[1], sQ1, sK + (g % kPairStages) * L::kHalf);
-        commit2(&bar->s_full[1]);
-        commit2(&bar->k_empty[g % kPairStages]);
-        for (int j = 0; ok && j < ti.nB; ++j) {
-          const uint32_t gj = g + j, gn = gj + 1;
-          const int st = gj % kPairStages, stn = gn % kPairStages;
-          const uint32_t ph = (gj / kPairStages) & 1, phn = (gn / kPairStages) & 1;
-          if (!(ok = mbar_wait_cluster(&bar->v_full[st], ph, abort, p.err))) break;
-          if (j < ti.nA) {
-            if (!(ok = mbar_wait_cluster(&bar->p_full[0], cs[0] & 1, abort, p.err))) break;
-            ++cs[0];
-            if (j == 0 && !(ok = mbar_wait_cluster(&bar->o_empty[0], (tt & 1) ^ 1, abort, p.err))) break;
-            tc_fence_after();
-            mma_pv_pair(tO[0], tS[0], sV + st * L::kHalf, j > 0);
-            if (j + 1 < ti.nA) {
-              if (!(ok = mbar_wait_cluster(&bar->k_full[stn], phn, abort, p.err))) break;
-              tc_fence_after();
-              mma_qk_pair(tS[0], sQ0, sK + stn * L::kHalf);
-              commit2(&bar->s_full[0]);
-            } else {
-              commit2(&bar->o_full[0]);
-            }
-          }
-          if (!(ok = mbar_wait_cluster(&bar->p_full[1], cs[1] & 1, abort, p.err))) break;
-          ++cs[1];
-          if (j == 0 && !(ok = mbar_wait_cluster(&bar->o_empty[1], (tt & 1) ^ 1, abort, p.err))) break;
-          tc_fence_after();
-          mma_pv_pair(tO[1], tS[1], sV + st * L::kHalf, j > 0);
-          commit2(&bar->v_empty[st]);
-          if (j + 1 < ti.nB) {
-            if (!(ok = mbar_wait_cluster(&bar->k_full[stn], phn, abort, p.err))) break;
-            tc_fence_after();
-            mma_qk_pair(tS[1], sQ1, sK + stn * L::kHalf);
-            commit2(&bar->s_full[1]);
-            commit2(&bar->k_empty[stn]);
-          } else {
-            commit2(&bar->o_full[1]);
-            commit2(&bar->q_empty);  // every score MMA of this tile has been issued
-          }
-        }
-        g += ti.nB;
-      }
-    }
-  } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
-    // ------------------------------------------------------------- softmax (each CTA, own rows)
-    const int x = (warp >= 8) ? 1 : 0;
-    const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const uint32_t tS = tmem + lane_off + x * 128;
-    const uint32_t tO = tmem + lane_off + 256 + x * D;
-    const uint32_t p_full0 = mapa_shared(smem_u32(&bar->p_full[x]), 0);
-    const uint32_t o_empty0 = mapa_shared(smem_u32(&bar->o_empty[x]), 0);
-    const float c = p.scale_log2;
-    uint32_t cs = 0, tt = 0;
-    bool ok = true;
-    for (int k = 0, tile = kth_tile_pair(0, num_tiles, p.lpt, pr, npr); ok && tile >= 0;
-         tile = kth_tile_pair(++k, num_tiles, p.lpt, pr, npr), ++tt) {
-      const TileInfo ti = tile_info_pair(tile, p);
-      const int r0 = ti.t0 + x * 2 * BM + (int)rank * BM;  // this CTA's first row of tile x
-      const int t = r0 + row;
-      const int n = x ? ti.nB : ti.nA;
-      int row_lo = 0, row_hi = p.S;
-      if constexpr (kKeyMask) {
-        const int tc = t < p.T ? t : p.T - 1;
-        row_lo = __ldg(p.key_lo + tc);
-        row_hi = __ldg(p.key_hi + tc);
-      }
-      float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
-      for (int j = 0; j < n; ++j, ++cs) {
-        if (!(ok = mbar_wait_cluster(&bar->s_full[x], cs & 1, abort, p.err))) break;
-        tc_fence_after();
-        const int kb = (ti.j0 + j) * BN;
-        int lim = p.S - kb;
-        if (p.causal) {
-          const int lc = t + p.q_start + 1 - kb;
-          lim = lc < lim ? lc : lim;
-        }
-        int lo_rel = 0;
-        if constexpr (kKeyMask) {
-          lo_rel = row_lo - kb;
-          lim = row_hi - kb < lim ? row_hi - kb : lim;
-        }
-        const bool need_mask = __any_sync(0xffffffffu, lim < BN || lo_rel > 0);
-        uint32_t sr[BN];
-#pragma unroll
-        for (int ch = 0; ch < BN / 32; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
-        tmem_wait_ld();
-        if (need_mask) {
-#pragma unroll
-          for (int i = 0; i < BN; ++i)
-            if (i >= lim || i < lo_rel) sr[i] = __float_as_uint(-INFINITY);
-        }
-        float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < BN; i += 8) {
-          mxa = max3(mxa, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
-          mxb = max3(mxb, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
-          mxc = max3(mxc, __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
-          mxd = max3(mxd, __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
-        }
-        const float mt = fmaxf(max3(mxa, mxb, mxc), mxd) * c;
-        m_true = fmaxf(m_true, mt);
-        if (j == 0) {
-          m_used = mt;
-        } else if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
-          const float m_new = fmaxf(m_used, mt);
-          const float alpha = m_used == -INFINITY ? 0.f : ex2(m_used - m_new);
-          m_used = m_new;
-          l *= alpha;
-          uint32_t r[32];
-#pragma unroll
-          for (int ch = 0; ch < D / 32; ++ch) {
-            tmem_ld32(tO + ch * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(tO + ch * 32, r);
-          }
-        }
-        const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
-        const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(neg_m, neg_m);
-        uint64_t sum_a = 0, sum_b = 0;
-#pragma unroll
-        for (int ch = 0; ch < BN / 32; ++ch) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const uint64_t sv = (uint64_t)sr[ch * 32 + 2 * i] | ((uint64_t)sr[ch * 32 + 2 * i + 1] << 32);
-            float x0, x1;
-            f2_unpack(f2_fma(sv, c2, nm2), x0, x1);
-            const float p0 = ex2(x0), p1 = ex2(x1);
-            const uint64_t pv = f2_pack(p0, p1);
-            if (i & 1) sum_b = f2_add(sum_b, pv); else sum_a = f2_add(sum_a, pv);
-            pk[i] = pack_bf16(p0, p1);
-          }
-          tmem_st16(tS + ch * 16, pk);
-        }
-        float sa0, sa1, sb0, sb1;
-        f2_unpack(sum_a, sa0, sa1);
-        f2_unpack(sum_b, sb0, sb1);
-        l += (sa0 + sa1) + (sb0 + sb1);
-        tmem_wait_st();
-        warp_arrive_cluster_after_tc(p_full0);
-      }
-      if (!ok || !(ok = mbar_wait_cluster(&bar->o_full[x], tt & 1, abort, p.err))) break;
-      tc_fence_after();
-      const float inv_l = 1.0f / l;
-      const bool store = t < p.T;
-      const int64_t bhq = (int64_t)ti.b * p.H + ti.h;
-      const uint32_t stg = smem_u32(smem + L::kStg) + q4 * (D / 64) * 4096;
-      const uint32_t use = 2 * tt + x;
-      if (use > 0 && !(ok = mbar_wait(&bar->stg_free[q4], (use - 1) & 1, abort, p.err))) break;
-#pragma unroll
-      for (int ch = 0; ch < D / 32; ++ch) {
-        uint32_t r[32];
-        tmem_ld32(tO + ch * 32, r);
-        tmem_wait_ld();
-        if (ch == D / 32 - 1) warp_arrive_cluster_after_tc(o_empty0);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
-        const uint32_t rowb = stg + (ch >> 1) * 4096 + lane * 128;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          sts128(rowb + ((((ch & 1) * 4 + i) ^ (lane & 7)) << 4), pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-#pragma unroll
-        for (int bx = 0; bx < D / 64; ++bx) tma_store_4d(&tm_o, stg + bx * 4096, bx * 64, r0 + q4 * 32, ti.h, ti.b);
-        bulk_commit();
-        bulk_wait_read_all();
-        mbar_arrive(&bar->stg_free[q4]);
-      }
-      if (store) {
-        const int64_t idx = bhq * p.T + t;
-        constexpr float kLn2 = 0.6931471805599453f;
-        if (p.lse) p.lse[idx] = (m_used + __log2f(l)) * kLn2;
-        if (p.m) p.m[idx] = m_true * kLn2;
-        if (p.den) p.den[idx] = l * ex2(m_used - m_true);
-      }
-    }
-    if (lane == 0) bulk_wait_all();
-  }
-  tc_fence_before();
-  cluster_sync_all();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem, 512);
-  }
-}
-
-// PDB_FWD_PAIR=0 selects the single-CTA D = 128 kernel (for comparison runs).
-bool use_pair_kernel() {
-  const char* e = getenv("PDB_FWD_PAIR");
-  return !(e && e[0] == '0');
-}
-
-int launch_pair(const pdb_flash_desc& d, FwdParams p, const CUtensorMap& tq, const CUtensorMap& tv,
-                cudaStream_t stream) {
-  CUtensorMap tk, to;
-  {
-    const uint64_t dims[4] = {128, (uint64_t)d.seqlen_k, (uint64_t)d.heads_kv, (uint64_t)d.batch};
-    const uint64_t sk[3] = {(uint64_t)d.k_stride[2] * 2, (uint64_t)d.k_stride[1] * 2, (uint64_t)d.k_stride[0] * 2};
-    const uint32_t box[4] = {64, 64, 1, 1};  // 64 keys x 64 features: half a key tile per CTA
-    if (int st = encode_tma_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.k, dims, sk, box, CU_TENSOR_MAP_SWIZZLE_128B))
-      return st;
-  }
-  {
-    const uint64_t dims[4] = {128, (uint64_t)d.seqlen_q, (uint64_t)d.heads_q, (uint64_t)d.batch};
-    const uint64_t so[3] = {(uint64_t)d.o_stride[2] * 2, (uint64_t)d.o_stride[1] * 2, (uint64_t)d.o_stride[0] * 2};
-    const uint32_t obox[4] = {64, 32, 1, 1};
-    if (int st = encode_tma_4d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.o, dims, so, obox, CU_TENSOR_MAP_SWIZZLE_128B))
-      return st;
-  }
-  p.num_mblocks = (int)((d.seqlen_q + 4 * BM - 1) / (4 * BM));
-  const int64_t nblk = (int64_t)p.num_mblocks * d.heads_q * d.batch;  // 512-row work tiles
-  if (nblk > 0x7fffffffLL) return set_error(PDB_ERR_SHAPE, "bf16 flash: grid too large");
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int smem = PairSmem::kTotal;
-  auto kern = p.key_lo ? flash_fwd_pair_kernel<true> : flash_fwd_pair_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return cuda_status(e, "bf16 flash pair: set smem attribute");
-  // clusters of two that fit at once on this device (queried once per device, under a lock)
-  static std::mutex mu;
-  static int max_pairs[64] = {};
-  int cap = sm_count(dev) / 2;
-  if (dev >= 0 && dev < 64) {
-    std::lock_guard<std::mutex> lk(mu);
-    if (max_pairs[dev] == 0) {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(2 * cap);
-      cfg.blockDim = dim3(kThreads);
-      cfg.dynamicSmemBytes = smem;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-        cudaGetLastError();
-        n = cap;
-      }
-      max_pairs[dev] = n;
-    }
-    cap = max_pairs[dev];
-  }
-  const int64_t tile_pairs = (nblk + 1) / 2;
-  p.lpt = tile_pairs < 4 * (int64_t)cap ? 1 : 0;  // small jobs: single tiles heaviest first
-  const int64_t units = p.lpt ? nblk : tile_pairs;
-  const int64_t pairs = units < cap ? units : cap;
-  kern<<<(unsigned)(2 * pairs), kThreads, smem, stream>>>(tq, tk, tv, to, p);
-  return cuda_status(cudaGetLastError(), "bf16 flash pair launch");
-}
-
 template <int D>
 int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   CUtensorMap tq, tk, tv;
@@ -1291,7 +828,6 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
     kern<<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, p);
     return cuda_status(cudaGetLastError(), "bf16 flash launch");
   }
-  if (D == 128 && use_pair_kernel()) return launch_pair(d, p, tq, tv, stream);
   CUtensorMap to;  // O stores: 32-row boxes, one per softmax warp
   {
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)d.seqlen_q, (uint64_t)d.heads_q, (uint64_t)d.batch};
