@@ -90,6 +90,13 @@ __device__ __forceinline__ float ew_apply(const EwProgram& pg, float v, int64_t 
     (void)x; (void)y;                          \
     v[c] = (EXPR);                             \
   }
+#define PDB_EW_ROW4(EXPR)                      \
+  _Pragma("unroll") for (int c = 0; c < 4; ++c) { \
+    const float x = sw ? w[c] : v[c];          \
+    const float y = sw ? v[c] : w[c];          \
+    (void)x; (void)y;                          \
+    v[c] = (EXPR);                             \
+  }
 __device__ __forceinline__ void ew_apply_row32(const EwProgram& pg, float (&v)[32], int64_t b, int64_t i, int64_t j0,
                                                int nvalid) {
   for (int s = 0; s < pg.n; ++s) {
@@ -514,12 +521,37 @@ __global__ void __launch_bounds__(kPwThreads) pointwise_f32_kernel(const Pointwi
     const float* xr = d.x + b * d.xs[0] + i * d.xs[1];
     float* yr = d.y + b * d.ys[0] + i * d.ys[1];
     if (vec && j0 + 4 <= d.n) {
-      float4 v = __ldcs(reinterpret_cast<const float4*>(xr + j0));
-      v.x = ew_apply(pg, v.x, b, i, j0);
-      v.y = ew_apply(pg, v.y, b, i, j0 + 1);
-      v.z = ew_apply(pg, v.z, b, i, j0 + 2);
-      v.w = ew_apply(pg, v.w, b, i, j0 + 3);
-      __stcs(reinterpret_cast<float4*>(yr + j0), v);
+      const float4 x4 = __ldcs(reinterpret_cast<const float4*>(xr + j0));
+      float v[4] = {x4.x, x4.y, x4.z, x4.w};
+      // one dispatch per step for the four values
+      for (int st = 0; st < pg.n; ++st) {
+        const EwOp& o = pg.ops[st];
+        float w[4];
+        if (o.operand == 2) {
+          const float* base = o.ptr + b * o.stride[0] + i * o.stride[1] + j0 * o.stride[2];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) w[c] = __ldg(base + c * o.stride[2]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) w[c] = o.value;
+        }
+        const bool sw = o.swap != 0;
+        switch (o.op) {
+          case PDB_EW_ADD: PDB_EW_ROW4(x + y) break;
+          case PDB_EW_SUB: PDB_EW_ROW4(x - y) break;
+          case PDB_EW_MUL: PDB_EW_ROW4(x * y) break;
+          case PDB_EW_DIV: PDB_EW_ROW4(x / y) break;
+          case PDB_EW_MAX: PDB_EW_ROW4(fmaxf(x, y)) break;
+          case PDB_EW_MIN: PDB_EW_ROW4(fminf(x, y)) break;
+          case PDB_EW_EXP: PDB_EW_ROW4(expf(v[c])) break;
+          case PDB_EW_LOG: PDB_EW_ROW4(logf(v[c])) break;
+          case PDB_EW_SQRT: PDB_EW_ROW4(sqrtf(v[c])) break;
+          case PDB_EW_TANH: PDB_EW_ROW4(tanhf(v[c])) break;
+          case PDB_EW_NEG: PDB_EW_ROW4(-v[c]) break;
+          default: break;
+        }
+      }
+      __stcs(reinterpret_cast<float4*>(yr + j0), make_float4(v[0], v[1], v[2], v[3]));
     } else {
       for (int64_t j = j0; j < j0 + 4 && j < d.n; ++j) yr[j * d.ys[2]] = ew_apply(pg, xr[j * d.xs[2]], b, i, j);
     }

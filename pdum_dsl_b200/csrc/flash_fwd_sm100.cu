@@ -108,6 +108,23 @@ struct TileInfo {
   int b, h, hk, t0, j0, nA, nB;
 };
 
+// The exponential phase of one 32-score chunk: P = exp2(s c - m) as 16 bf16
+// pairs (packed f32x2 FMA for the argument, MUFU ex2 per score, cvt.rn.bf16x2
+// to pack) and the pairs' f32 row sums on two chains.
+__device__ __forceinline__ void exp_chunk(const uint32_t* sr, uint64_t c2, uint64_t nm2, uint64_t& sum_a,
+                                          uint64_t& sum_b, uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint64_t sv = (uint64_t)sr[2 * i] | ((uint64_t)sr[2 * i + 1] << 32);
+    float x0, x1;
+    f2_unpack(f2_fma(sv, c2, nm2), x0, x1);
+    const float p0 = ex2(x0), p1 = ex2(x1);
+    const uint64_t pv = f2_pack(p0, p1);
+    if (i & 1) sum_b = f2_add(sum_b, pv); else sum_a = f2_add(sum_a, pv);
+    pk[i] = pack_bf16(p0, p1);
+  }
+}
+
 // Two static schedules of the persistent grid over the work tiles (256 query
 // rows of one head each).
 // * Pairs (large jobs): ordinals run head-major (concurrent CTAs share the K/V
@@ -398,16 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int ch = 0; ch < BN / 32; ++ch) {
           uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const uint64_t sv = (uint64_t)sr[ch * 32 + 2 * i] | ((uint64_t)sr[ch * 32 + 2 * i + 1] << 32);
-            float x0, x1;
-            f2_unpack(f2_fma(sv, c2, nm2), x0, x1);
-            const float p0 = ex2(x0), p1 = ex2(x1);
-            const uint64_t pv = f2_pack(p0, p1);
-            if (i & 1) sum_b = f2_add(sum_b, pv); else sum_a = f2_add(sum_a, pv);
-            pk[i] = pack_bf16(p0, p1);
-          }
+          exp_chunk(sr + ch * 32, c2, nm2, sum_a, sum_b, pk);
           tmem_st16(tS + ch * 16, pk);
         }
         float sa0, sa1, sb0, sb1;
@@ -712,16 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int ch = 0; ch < BN / 32; ++ch) {
           uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const uint64_t sv = (uint64_t)sr[ch * 32 + 2 * i] | ((uint64_t)sr[ch * 32 + 2 * i + 1] << 32);
-            float x0, x1;
-            f2_unpack(f2_fma(sv, c2, nm2), x0, x1);
-            const float p0 = ex2(x0), p1 = ex2(x1);
-            const uint64_t pv = f2_pack(p0, p1);
-            if (i & 1) sum_b = f2_add(sum_b, pv); else sum_a = f2_add(sum_a, pv);
-            pk[i] = pack_bf16(p0, p1);
-          }
+          exp_chunk(sr + ch * 32, c2, nm2, sum_a, sum_b, pk);
           tmem_st16(tP + ch * 16, pk);
         }
         float sa0, sa1, sb0, sb1;
@@ -821,13 +820,13 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   const int64_t units = p.lpt ? nblk : pairs;
   const int64_t grid = units < sms ? units : sms;  // persistent: one CTA per SM
   const int smem = Smem<D>::kTotal;
-  if (D == 64) {  // P in its own TMEM columns (656 vs 610 TFLOP/s at B8 H32 S4096 causal)
+  if constexpr (D == 64) {  // P in its own TMEM columns (656 vs 610 TFLOP/s at B8 H32 S4096 causal)
     auto kern = p.key_lo ? flash_fwd_d64_kernel<true> : flash_fwd_d64_kernel<false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_status(e, "bf16 flash: set smem attribute");
     kern<<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, p);
     return cuda_status(cudaGetLastError(), "bf16 flash launch");
-  }
+  } else {
   CUtensorMap to;  // O stores: 32-row boxes, one per softmax warp
   {
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)d.seqlen_q, (uint64_t)d.heads_q, (uint64_t)d.batch};
@@ -841,6 +840,7 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   if (e != cudaSuccess) return cuda_status(e, "bf16 flash: set smem attribute");
   kern<<<(unsigned)grid, kThreads, smem, stream>>>(tq, tk, tv, to, p);
   return cuda_status(cudaGetLastError(), "bf16 flash launch");
+  }
 }
 
 }  // namespace
