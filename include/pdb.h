@@ -165,8 +165,11 @@ int pdb_flash_bwd(const pdb_flash_bwd_desc* d, void* stream);
  * Problems whose scratch (pdb_flash_bwd_workspace_size) exceeds
  * pdb_flash_bwd_noalloc_max_scratch() are refused with PDB_ERR_SHAPE.  The
  * first call on a device looks up the array's address (make it before any
- * stream capture); calls that may overlap on the GPU share the array and
- * race, so the caller must order them.  Nothing is allocated or freed. */
+ * stream capture) and keeps it for the life of the process, so a device reset
+ * (cudaDeviceReset, or destroying the primary context) invalidates it: do not
+ * call this entry point on a device after resetting it.  Calls that may
+ * overlap on the GPU share the array and race, so the caller must order them.
+ * Nothing is allocated or freed. */
 int pdb_flash_bwd_noalloc(const pdb_flash_bwd_desc* d, void* stream);
 size_t pdb_flash_bwd_noalloc_max_scratch(void);
 
@@ -304,7 +307,9 @@ int pdb_score_program_f32(const pdb_score_program_desc* d, void* stream);
 
 /* ---- status --------------------------------------------------------------------
  * pdb_check_error synchronises `stream`, reads and clears the device error flag
- * of the current device (set by bounded waits that expired) and returns
+ * of the current device (set by bounded waits that expired; its address is
+ * looked up once per device and, like the no-alloc scratch, is invalidated by
+ * a device reset) and returns
  * PDB_ERR_TIMEOUT if it was set, PDB_ERR_CUDA on a CUDA error, else PDB_OK.
  * pdb_last_error_string returns a thread-local description of the last non-OK
  * status returned on this thread.  pdb_version returns a constant string that

@@ -1174,9 +1174,19 @@ struct WsLayout {
 };
 
 WsLayout ws_layout(const pdb_flash_bwd_desc& d) {
-  const int64_t tpad = (d.seqlen_q + BT - 1) / BT * BT;
-  const size_t rows = (size_t)(d.batch * d.heads_q * tpad);
   WsLayout w{};
+  // Every size below is a product of descriptor fields; a descriptor whose
+  // products would wrap gets total = SIZE_MAX, which no workspace (and no fixed
+  // scratch) satisfies.
+  size_t rows = 0, tmp = 0;
+  const int64_t tpad = (d.seqlen_q + BT - 1) / BT * BT;
+  if (d.batch <= 0 || d.heads_q <= 0 || tpad <= 0 || d.head_dim_v <= 0 ||
+      __builtin_mul_overflow((size_t)d.batch, (size_t)d.heads_q, &tmp) ||
+      __builtin_mul_overflow(tmp, (size_t)tpad, &rows) || __builtin_mul_overflow(rows, (size_t)(64 * 4 * 4), &tmp) ||
+      __builtin_mul_overflow(rows, (size_t)d.head_dim_v * 2 + 64, &tmp)) {
+    w.total = SIZE_MAX;
+    return w;
+  }
   size_t off = 0;
   w.lse2 = off;
   off = align256(off + rows * 4);
@@ -1446,7 +1456,11 @@ extern "C" int pdb_flash_bwd(const pdb_flash_bwd_desc* d, void* stream) {
 // only.  The scratch (D and lse2 rows, plus the recomputed lse and a scratch
 // forward output when lse is NULL) lives in g_bwd_scratch below; its address
 // is looked up once per device, on the first call made with that device
-// current (so make that first call before any stream capture).  The prologue
+// current (so make that first call before any stream capture), and kept for
+// the life of the process: a device reset (cudaDeviceReset, or anything that
+// destroys the primary context) reloads the library's device code and
+// invalidates it, so a process that resets a device must not call this entry
+// point on that device afterwards.  The prologue
 // kernel rewrites every scratch word it later reads on each call, so nothing
 // has to be cleared between calls.  Every call on a device shares the one
 // array: calls that can overlap on the GPU (different streams without

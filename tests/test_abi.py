@@ -143,3 +143,16 @@ def test_backward_refuses_a_small_workspace_before_launching():
     d.workspace, d.workspace_bytes = 256, lib.pdb_flash_bwd_workspace_size(C.byref(d)) - 16
     assert lib.pdb_flash_bwd(C.byref(d), None) == _lib.PDB_ERR_ARG
     assert b"workspace too small" in lib.pdb_last_error_string()
+
+
+def test_workspace_size_of_a_wrapping_descriptor_is_unsatisfiable():
+    """A descriptor whose sizes would overflow the workspace arithmetic reports a
+    workspace no caller can provide (SIZE_MAX), so neither entry point launches."""
+    lib = _lib.load()
+    d = _lib.FlashBwdDesc()
+    d.q = d.k = d.v = d.o = d.dout = d.dq = d.dk = d.dv = 16
+    d.batch, d.heads_q, d.heads_kv, d.seqlen_q, d.seqlen_k = 1 << 30, 1 << 30, 1 << 30, 1 << 29, 128
+    d.head_dim = d.head_dim_v = 64
+    d.dtype = _lib.PDB_BF16
+    assert lib.pdb_flash_bwd_workspace_size(C.byref(d)) == 2 ** 64 - 1
+    assert lib.pdb_flash_bwd_noalloc(C.byref(d), None) != _lib.PDB_OK

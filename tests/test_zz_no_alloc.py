@@ -36,8 +36,12 @@ def _desc(q, k, v, o, do, lse, dq, dk, dv, scale, causal):
     return d
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("stored_lse", [True, False])
-def test_noalloc_matches_workspace_backward_twice(cuda, stored_lse):
+def test_noalloc_matches_workspace_backward_twice(cuda, stored_lse, D):
+    """head_dim 64 runs the fused single pass (its fp32 dQ accumulator lives in the
+    scratch); head_dim 128 the dK/dV and dQ kernels sharing the scratch's two
+    work-unit counters -- both back to back, with the previous call's leftovers."""
     import torch
 
     from pdum_dsl_b200 import _lib, kernels
@@ -46,10 +50,10 @@ def test_noalloc_matches_workspace_backward_twice(cuda, stored_lse):
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
     for call, (B, H, HKV, T) in enumerate(((2, 4, 2, 300), (1, 2, 2, 513))):  # two calls, different sizes
         g = torch.Generator(device="cpu").manual_seed(100 + call)
-        q = torch.randn(B, H, T, 64, generator=g).to(torch.bfloat16).to(cuda)
-        k, v = (torch.randn(B, HKV, T, 64, generator=g).to(torch.bfloat16).to(cuda) for _ in range(2))
-        do = torch.randn(B, H, T, 64, generator=g).to(torch.bfloat16).to(cuda)
-        scale = 1 / math.sqrt(64)
+        q = torch.randn(B, H, T, D, generator=g).to(torch.bfloat16).to(cuda)
+        k, v = (torch.randn(B, HKV, T, D, generator=g).to(torch.bfloat16).to(cuda) for _ in range(2))
+        do = torch.randn(B, H, T, D, generator=g).to(torch.bfloat16).to(cuda)
+        scale = 1 / math.sqrt(D)
         o, lse = kernels.flash_attention(q, k, v, scale=scale, causal=True, return_lse=True)
         ref = kernels.flash_attention_backward(q, k, v, o, do, lse if stored_lse else None, scale=scale, causal=True)
         got = [torch.empty_like(x) for x in (q, k, v)]
