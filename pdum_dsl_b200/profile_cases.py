@@ -90,6 +90,22 @@ def case_pointwise(n=8192):
     return (lambda: kernels.pointwise(x, prog, out=y)), {"bytes": 8 * n * n}
 
 
+def case_rows(kind):
+    """Config 2: X 8192 x 4096 f32 (gamma / beta for the layernorm)."""
+    import torch
+
+    from . import kernels
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn((8192, 4096), device="cuda", generator=g)
+    y = torch.empty_like(x)
+    gam = 1 + 0.1 * torch.randn(4096, device="cuda", generator=g)
+    bet = 0.1 * torch.randn(4096, device="cuda", generator=g)
+    if kind == "softmax":
+        return (lambda: kernels.row_softmax(x, out=y)), {"bytes": 2 * x.numel() * 4}
+    return (lambda: kernels.layernorm(x, gam, bet, 1e-5, out=y)), {"bytes": 2 * x.numel() * 4}
+
+
 def case_score_program(T=2048, E=64):
     """The den-gradient carve of the attention joint (a row-sum score program)."""
     import torch
@@ -138,6 +154,8 @@ CASES = {
     "contract_single": case_contract_single,
     "pointwise": case_pointwise,
     "score_program": case_score_program,
+    "rowsoftmax_config2": lambda: case_rows("softmax"),
+    "layernorm_config2": lambda: case_rows("layernorm"),
 }
 
 
