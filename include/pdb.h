@@ -240,9 +240,10 @@ int pdb_pointwise_f32(const pdb_pointwise_desc* d, void* stream);
  * statistics and evaluates a pointwise expression over the score space.
  *
  * Index space: rows t < rows, columns s < cols (either of the carve's two
- * score dims may be the row dim), times `batch` independent instances.  Per
- * element (t, s) a program of SSA steps runs over float registers (booleans
- * are 1.0 / 0.0); its step kinds are
+ * score dims may be the row dim), times batch x batch_mid x batch_inner
+ * independent instances (up to three rider dims, e.g. batch, KV head and the
+ * query heads of a GQA group; an operand without a rider has stride 0 along it).  Per element (t, s) a program of SSA steps
+ * runs over float registers (booleans are 1.0 / 0.0); its step kinds are
  *   SCORE   dst = sum_f A_a[t, f] * B_a[s, f]        (score contraction a)
  *   ROW     dst = rowvec[a][t],  COL  dst = colvec[a][s]
  *   TILE    dst = tile[a][t, s]
@@ -253,9 +254,12 @@ int pdb_pointwise_f32(const pdb_pointwise_desc* d, void* stream);
  *   OUT_TILE          out[b, t, s]
  *   OUT_ROW_SUM/MAX/MIN  out[b, t] = reduce over s
  *   OUT_ROW_CONTRACT  out[b, t, x] = sum_s V[t, s] * w[b, s, x]   (x < xdim)
- * f32 throughout (IEEE FMA, the precision of the reference's f32 column).
- * Every stride is an element count; the last stride of each operand may be
- * any value (no contiguity is required). */
+ * (b standing for the three rider indices).  f32 throughout (IEEE FMA, the
+ * precision of the reference's f32 column).  Every stride is an element count
+ * and the strides of each operand start with its three rider strides; no
+ * contiguity is required.  Row sums and row contractions of jobs with few row
+ * blocks split the columns over several CTAs and add the partial results
+ * atomically, so their f32 summation order varies from run to run. */
 enum pdb_sp_opcode {
   PDB_SP_SCORE = 1, PDB_SP_ROW, PDB_SP_COL, PDB_SP_TILE, PDB_SP_IOTA_ROW, PDB_SP_IOTA_COL, PDB_SP_CONST,
   PDB_SP_WHERE,
@@ -263,7 +267,8 @@ enum pdb_sp_opcode {
   PDB_SP_ADD, PDB_SP_SUB, PDB_SP_MUL, PDB_SP_DIV, PDB_SP_MAX, PDB_SP_MIN, PDB_SP_LE, PDB_SP_LT, PDB_SP_GE,
   PDB_SP_GT, PDB_SP_EQ, PDB_SP_NE, PDB_SP_AND, PDB_SP_OR,
   /* unary */
-  PDB_SP_EXP, PDB_SP_LOG, PDB_SP_NEG, PDB_SP_RECIP, PDB_SP_SQRT, PDB_SP_TANH, PDB_SP_NOT, PDB_SP_ABS
+  PDB_SP_EXP, PDB_SP_LOG, PDB_SP_NEG, PDB_SP_RECIP, PDB_SP_SQRT, PDB_SP_TANH, PDB_SP_NOT, PDB_SP_ABS,
+  PDB_SP_FLOOR
 };
 enum pdb_sp_out_mode {
   PDB_SP_OUT_TILE = 0, PDB_SP_OUT_ROW_SUM, PDB_SP_OUT_ROW_MAX, PDB_SP_OUT_ROW_MIN, PDB_SP_OUT_ROW_CONTRACT
@@ -280,27 +285,27 @@ typedef struct {
   double value;
 } pdb_sp_op;
 typedef struct {
-  int64_t batch, rows, cols;
+  int64_t batch, batch_mid, batch_inner, rows, cols;
   int64_t row_start, col_start;
   int32_t n_scores, n_ops, n_regs, result;
   const float* score_a[PDB_SP_MAX_SCORES];
   const float* score_b[PDB_SP_MAX_SCORES];
   int64_t score_feat[PDB_SP_MAX_SCORES];
-  int64_t score_a_stride[PDB_SP_MAX_SCORES][3]; /* (batch, row, feature) */
-  int64_t score_b_stride[PDB_SP_MAX_SCORES][3]; /* (batch, col, feature) */
+  int64_t score_a_stride[PDB_SP_MAX_SCORES][5]; /* (3 riders, row, feature) */
+  int64_t score_b_stride[PDB_SP_MAX_SCORES][5]; /* (3 riders, col, feature) */
   const float* rowvec[PDB_SP_MAX_VECS];
-  int64_t rowvec_stride[PDB_SP_MAX_VECS][2]; /* (batch, row) */
+  int64_t rowvec_stride[PDB_SP_MAX_VECS][4]; /* (3 riders, row) */
   const float* colvec[PDB_SP_MAX_VECS];
-  int64_t colvec_stride[PDB_SP_MAX_VECS][2]; /* (batch, col) */
+  int64_t colvec_stride[PDB_SP_MAX_VECS][4]; /* (3 riders, col) */
   const float* tile[PDB_SP_MAX_TILES];
-  int64_t tile_stride[PDB_SP_MAX_TILES][3]; /* (batch, row, col) */
+  int64_t tile_stride[PDB_SP_MAX_TILES][5]; /* (3 riders, row, col) */
   pdb_sp_op ops[PDB_SP_MAX_OPS];
   int32_t out_mode; /* enum pdb_sp_out_mode */
   int32_t reserved;
   float* out;
-  int64_t out_stride[3]; /* TILE: (batch, row, col); ROW_*: (batch, row); CONTRACT: (batch, row, x) */
+  int64_t out_stride[5]; /* (3 riders, row, col | x); ROW_*: the last is unused */
   const float* w;
-  int64_t w_stride[3]; /* (batch, col, x) */
+  int64_t w_stride[5]; /* (3 riders, col, x) */
   int64_t xdim;
 } pdb_score_program_desc;
 int pdb_score_program_f32(const pdb_score_program_desc* d, void* stream);

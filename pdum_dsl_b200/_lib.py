@@ -205,11 +205,13 @@ class PointwiseDesc(C.Structure):
 SP_OPS = {"score": 1, "row": 2, "col": 3, "tile": 4, "iota_row": 5, "iota_col": 6, "const": 7, "where": 8,
           "add": 9, "sub": 10, "mul": 11, "div": 12, "maximum": 13, "minimum": 14, "le": 15, "lt": 16, "ge": 17,
           "gt": 18, "eq": 19, "ne": 20, "and": 21, "or": 22,
-          "exp": 23, "log": 24, "neg": 25, "recip": 26, "sqrt": 27, "tanh": 28, "not": 29, "abs": 30}
-SP_UNARY = ("exp", "log", "neg", "recip", "sqrt", "tanh", "not", "abs")
+          "exp": 23, "log": 24, "neg": 25, "recip": 26, "sqrt": 27, "tanh": 28, "not": 29, "abs": 30,
+          "floor": 31}
+SP_UNARY = ("exp", "log", "neg", "recip", "sqrt", "tanh", "not", "abs", "floor")
 SP_OUT = {"tile": 0, "row_sum": 1, "row_max": 2, "row_min": 3, "row_contract": 4}
 SP_MAX_OPS, SP_MAX_REGS, SP_MAX_SCORES, SP_MAX_VECS, SP_MAX_TILES = 64, 12, 2, 6, 4
-I64x2 = C.c_int64 * 2
+I64x4 = C.c_int64 * 4
+I64x5 = C.c_int64 * 5
 
 
 class SpOp(C.Structure):
@@ -227,6 +229,8 @@ class SpOp(C.Structure):
 class ScoreProgramDesc(C.Structure):
     _fields_ = [
         ("batch", C.c_int64),
+        ("batch_mid", C.c_int64),
+        ("batch_inner", C.c_int64),
         ("rows", C.c_int64),
         ("cols", C.c_int64),
         ("row_start", C.c_int64),
@@ -238,21 +242,21 @@ class ScoreProgramDesc(C.Structure):
         ("score_a", C.c_void_p * SP_MAX_SCORES),
         ("score_b", C.c_void_p * SP_MAX_SCORES),
         ("score_feat", C.c_int64 * SP_MAX_SCORES),
-        ("score_a_stride", I64x3 * SP_MAX_SCORES),
-        ("score_b_stride", I64x3 * SP_MAX_SCORES),
+        ("score_a_stride", I64x5 * SP_MAX_SCORES),
+        ("score_b_stride", I64x5 * SP_MAX_SCORES),
         ("rowvec", C.c_void_p * SP_MAX_VECS),
-        ("rowvec_stride", I64x2 * SP_MAX_VECS),
+        ("rowvec_stride", I64x4 * SP_MAX_VECS),
         ("colvec", C.c_void_p * SP_MAX_VECS),
-        ("colvec_stride", I64x2 * SP_MAX_VECS),
+        ("colvec_stride", I64x4 * SP_MAX_VECS),
         ("tile", C.c_void_p * SP_MAX_TILES),
-        ("tile_stride", I64x3 * SP_MAX_TILES),
+        ("tile_stride", I64x5 * SP_MAX_TILES),
         ("ops", SpOp * SP_MAX_OPS),
         ("out_mode", C.c_int32),
         ("reserved", C.c_int32),
         ("out", C.c_void_p),
-        ("out_stride", I64x3),
+        ("out_stride", I64x5),
         ("w", C.c_void_p),
-        ("w_stride", I64x3),
+        ("w_stride", I64x5),
         ("xdim", C.c_int64),
     ]
 

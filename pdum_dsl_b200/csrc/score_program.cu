@@ -51,6 +51,7 @@ __device__ __forceinline__ float sp_apply1(int op, float a) {
     case PDB_SP_TANH: return tanhf(a);
     case PDB_SP_NOT: return a != 0.f ? 0.f : 1.f;
     case PDB_SP_ABS: return fabsf(a);
+    case PDB_SP_FLOOR: return floorf(a);
     default: return a;
   }
 }
@@ -83,24 +84,29 @@ __device__ __forceinline__ float reduce_combine(int mode, float a, float b) {
 }
 
 // One score contraction C[t0 + r, s0 + c] = sum_f A[t, f] B[s, f] into R[dst].
-__device__ void sp_score(const pdb_score_program_desc& d, int c, int64_t bidx, int64_t t0, int64_t s0, float* Rd,
-                         float (*As)[SP_ROWS + 1], float (*Bs)[SP_COLS + 1]) {
+// offset of the CTA's rider instance (r0, r1, r2) along an operand's first three strides
+__device__ __forceinline__ int64_t rider_off(const int64_t* st, int64_t r0, int64_t r1, int64_t r2) {
+  return r0 * st[0] + r1 * st[1] + r2 * st[2];
+}
+
+__device__ void sp_score(const pdb_score_program_desc& d, int c, int64_t r0, int64_t r1, int64_t r2, int64_t t0,
+                         int64_t s0, float* Rd, float (*As)[SP_ROWS + 1], float (*Bs)[SP_COLS + 1]) {
   const int tid = threadIdx.x;
   const int tr = tid >> 3, tc = tid & 7;  // rows 2 tr, 2 tr + 1; cols tc + 8 j
-  const float* A = d.score_a[c] + bidx * d.score_a_stride[c][0];
-  const float* B = d.score_b[c] + bidx * d.score_b_stride[c][0];
+  const float* A = d.score_a[c] + rider_off(d.score_a_stride[c], r0, r1, r2);
+  const float* B = d.score_b[c] + rider_off(d.score_b_stride[c], r0, r1, r2);
   const int64_t F = d.score_feat[c];
   float acc[2][4] = {};
   for (int64_t f0 = 0; f0 < F; f0 += SP_FK) {
     for (int e = tid; e < SP_ROWS * SP_FK; e += SP_THREADS) {
       const int r = e / SP_FK, kk = e % SP_FK;
       const int64_t gt = t0 + r, gf = f0 + kk;
-      As[kk][r] = (gt < d.rows && gf < F) ? A[gt * d.score_a_stride[c][1] + gf * d.score_a_stride[c][2]] : 0.f;
+      As[kk][r] = (gt < d.rows && gf < F) ? A[gt * d.score_a_stride[c][3] + gf * d.score_a_stride[c][4]] : 0.f;
     }
     for (int e = tid; e < SP_COLS * SP_FK; e += SP_THREADS) {
       const int r = e / SP_FK, kk = e % SP_FK;
       const int64_t gs = s0 + r, gf = f0 + kk;
-      Bs[kk][r] = (gs < d.cols && gf < F) ? B[gs * d.score_b_stride[c][1] + gf * d.score_b_stride[c][2]] : 0.f;
+      Bs[kk][r] = (gs < d.cols && gf < F) ? B[gs * d.score_b_stride[c][3] + gf * d.score_b_stride[c][4]] : 0.f;
     }
     __syncthreads();
 #pragma unroll 8
@@ -127,7 +133,9 @@ __global__ void __launch_bounds__(SP_THREADS) score_program_kernel(const __grid_
   float* smem = reinterpret_cast<float*>(sp_smem4);
   const pdb_score_program_desc& d = P.d;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t bidx = blockIdx.y;
+  // the three rider indices of this CTA's instance
+  const int64_t r2 = blockIdx.y % d.batch_inner, r1 = (blockIdx.y / d.batch_inner) % d.batch_mid,
+                r0 = blockIdx.y / (d.batch_inner * d.batch_mid);
   const int64_t t0 = (int64_t)blockIdx.x * SP_ROWS;
   // this CTA's column tiles [c_lo, c_hi) of the row block
   const int64_t ntiles = (d.cols + SP_COLS - 1) / SP_COLS;
@@ -154,7 +162,7 @@ __global__ void __launch_bounds__(SP_THREADS) score_program_kernel(const __grid_
       const pdb_sp_op& o = d.ops[k];
       float* Rd = R + o.dst * (SP_ROWS * SP_COLS);
       if (o.op == PDB_SP_SCORE) {
-        sp_score(d, o.a, bidx, t0, s0, Rd, As, Bs);
+        sp_score(d, o.a, r0, r1, r2, t0, s0, Rd, As, Bs);
         continue;
       }
       const float* Ra = R + o.a * (SP_ROWS * SP_COLS);
@@ -171,14 +179,14 @@ __global__ void __launch_bounds__(SP_THREADS) score_program_kernel(const __grid_
           case PDB_SP_IOTA_ROW: v = (float)(t + d.row_start); break;
           case PDB_SP_IOTA_COL: v = (float)(s + d.col_start); break;
           case PDB_SP_ROW:
-            v = in ? d.rowvec[o.a][bidx * d.rowvec_stride[o.a][0] + t * d.rowvec_stride[o.a][1]] : 0.f;
+            v = in ? d.rowvec[o.a][rider_off(d.rowvec_stride[o.a], r0, r1, r2) + t * d.rowvec_stride[o.a][3]] : 0.f;
             break;
           case PDB_SP_COL:
-            v = in ? d.colvec[o.a][bidx * d.colvec_stride[o.a][0] + s * d.colvec_stride[o.a][1]] : 0.f;
+            v = in ? d.colvec[o.a][rider_off(d.colvec_stride[o.a], r0, r1, r2) + s * d.colvec_stride[o.a][3]] : 0.f;
             break;
           case PDB_SP_TILE:
-            v = in ? d.tile[o.a][bidx * d.tile_stride[o.a][0] + t * d.tile_stride[o.a][1] +
-                                 s * d.tile_stride[o.a][2]]
+            v = in ? d.tile[o.a][rider_off(d.tile_stride[o.a], r0, r1, r2) + t * d.tile_stride[o.a][3] +
+                                 s * d.tile_stride[o.a][4]]
                    : 0.f;
             break;
           case PDB_SP_WHERE: v = Ra[e] != 0.f ? Rb[e] : Rc[e]; break;
@@ -196,15 +204,15 @@ __global__ void __launch_bounds__(SP_THREADS) score_program_kernel(const __grid_
         const int e = tid + SP_THREADS * i;
         const int64_t t = t0 + e / SP_COLS, s = s0 + e % SP_COLS;
         if (t < d.rows && s < d.cols)
-          d.out[bidx * d.out_stride[0] + t * d.out_stride[1] + s * d.out_stride[2]] = V[e];
+          d.out[rider_off(d.out_stride, r0, r1, r2) + t * d.out_stride[3] + s * d.out_stride[4]] = V[e];
       }
     } else if (mode == PDB_SP_OUT_ROW_CONTRACT) {
       __syncthreads();  // V complete for every thread
-      const float* W = d.w + bidx * d.w_stride[0];
+      const float* W = d.w + rider_off(d.w_stride, r0, r1, r2);
       for (int e = tid; e < SP_COLS * SP_XMAX; e += SP_THREADS) {
         const int r = e / SP_XMAX, x = e % SP_XMAX;
         const int64_t s = s0 + r;
-        Ws[e] = (s < d.cols && x < d.xdim) ? W[s * d.w_stride[1] + x * d.w_stride[2]] : 0.f;
+        Ws[e] = (s < d.cols && x < d.xdim) ? W[s * d.w_stride[3] + x * d.w_stride[4]] : 0.f;
       }
       __syncthreads();
       const int tr = tid >> 4, tx = tid & 15;  // rows 4 tr + u, x = tx + 16 j
@@ -246,7 +254,7 @@ __global__ void __launch_bounds__(SP_THREADS) score_program_kernel(const __grid_
       for (int j = 0; j < 8; ++j) {
         const int x = tx + 16 * j;
         if (x >= d.xdim) continue;
-        float* o = d.out + bidx * d.out_stride[0] + t * d.out_stride[1] + x * d.out_stride[2];
+        float* o = d.out + rider_off(d.out_stride, r0, r1, r2) + t * d.out_stride[3] + x * d.out_stride[4];
         if (atomic_out) atomicAdd(o, acc[u][j]);
         else *o = acc[u][j];
       }
@@ -256,7 +264,7 @@ __global__ void __launch_bounds__(SP_THREADS) score_program_kernel(const __grid_
     for (int i = 0; i < SP_EPT; ++i) {
       const int64_t t = t0 + warp + 8 * i;
       if (t >= d.rows) continue;
-      float* o = d.out + bidx * d.out_stride[0] + t * d.out_stride[1];
+      float* o = d.out + rider_off(d.out_stride, r0, r1, r2) + t * d.out_stride[3];
       if (atomic_out) atomicAdd(o, red[i]);
       else *o = red[i];
     }
@@ -264,12 +272,17 @@ __global__ void __launch_bounds__(SP_THREADS) score_program_kernel(const __grid_
 }
 
 // zeroes out[b, t (, x)] ahead of a column-split launch that accumulates into it
-__global__ void sp_zero_kernel(float* out, int64_t batch, int64_t rows, int64_t xdim, int64_t s0, int64_t s1,
-                               int64_t s2) {
-  const int64_t total = batch * rows * xdim;
+struct SpZero {
+  float* out;
+  int64_t riders, mid, inner, rows, xdim;
+  int64_t st[5];
+};
+__global__ void sp_zero_kernel(const SpZero z) {
+  const int64_t total = z.riders * z.rows * z.xdim;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t x = e % xdim, t = (e / xdim) % rows, b = e / (xdim * rows);
-    out[b * s0 + t * s1 + x * s2] = 0.f;
+    const int64_t x = e % z.xdim, t = (e / z.xdim) % z.rows, y = e / (z.xdim * z.rows);
+    const int64_t r2 = y % z.inner, r1 = (y / z.inner) % z.mid, r0 = y / (z.inner * z.mid);
+    z.out[r0 * z.st[0] + r1 * z.st[1] + r2 * z.st[2] + t * z.st[3] + x * z.st[4]] = 0.f;
   }
 }
 
@@ -312,7 +325,7 @@ int check_program(const pdb_score_program_desc* d) {
         if (o.c < 0 || o.c >= d->n_regs) return set_error(PDB_ERR_ARG, "step %d: bad operand register", k);
         /* fallthrough */
       default:
-        if (o.op < PDB_SP_SCORE || o.op > PDB_SP_ABS) return set_error(PDB_ERR_ARG, "step %d: unknown opcode %d", k, o.op);
+        if (o.op < PDB_SP_SCORE || o.op > PDB_SP_FLOOR) return set_error(PDB_ERR_ARG, "step %d: unknown opcode %d", k, o.op);
         if (o.a < 0 || o.a >= d->n_regs || (o.op < PDB_SP_EXP && (o.b < 0 || o.b >= d->n_regs)))
           return set_error(PDB_ERR_ARG, "step %d: bad operand register", k);
     }
@@ -327,8 +340,10 @@ using namespace pdb;
 
 extern "C" int pdb_score_program_f32(const pdb_score_program_desc* d, void* stream) {
   if (!d) return set_error(PDB_ERR_ARG, "null descriptor");
-  if (d->batch <= 0 || d->rows <= 0 || d->cols <= 0) return set_error(PDB_ERR_SHAPE, "score program: sizes must be positive");
-  if (d->batch > 65535 || d->rows > (int64_t)0x7fffffff * SP_ROWS)
+  if (d->batch <= 0 || d->batch_mid <= 0 || d->batch_inner <= 0 || d->rows <= 0 || d->cols <= 0)
+    return set_error(PDB_ERR_SHAPE, "score program: sizes must be positive");
+  const int64_t nriders = d->batch * d->batch_mid * d->batch_inner;
+  if (nriders > 65535 || d->rows > (int64_t)0x7fffffff * SP_ROWS)
     return set_error(PDB_ERR_SHAPE, "score program: grid too large");
   if (!d->out) return set_error(PDB_ERR_ARG, "score program: null out");
   if (int st = check_program(d)) return st;
@@ -352,24 +367,27 @@ extern "C" int pdb_score_program_f32(const pdb_score_program_desc* d, void* stre
   if (mode == PDB_SP_OUT_ROW_SUM || mode == PDB_SP_OUT_ROW_CONTRACT) {
     int dev = 0;
     cudaGetDevice(&dev);
-    const int64_t want = (2 * (int64_t)sm_count(dev) + row_blocks * d->batch - 1) / (row_blocks * d->batch);
+    const int64_t nb = row_blocks * nriders;
+    const int64_t want = (2 * (int64_t)sm_count(dev) + nb - 1) / nb;
     const int64_t most = col_tiles / 4 > 1 ? col_tiles / 4 : 1;
     P.csplit = (int)(want < most ? (want > 1 ? want : 1) : most);
     if (P.csplit > 64) P.csplit = 64;
   }
-  dim3 grid((unsigned)row_blocks, (unsigned)d->batch, (unsigned)P.csplit);
+  dim3 grid((unsigned)row_blocks, (unsigned)nriders, (unsigned)P.csplit);
   // contraction outputs wider than SP_XMAX: one launch per 128-column slab of w / out
   const int64_t xdim = mode == PDB_SP_OUT_ROW_CONTRACT ? d->xdim : 1;
   for (int64_t x0 = 0; x0 < xdim; x0 += SP_XMAX) {
     if (mode == PDB_SP_OUT_ROW_CONTRACT) {
-      P.d.w = d->w + x0 * d->w_stride[2];
-      P.d.out = d->out + x0 * d->out_stride[2];
+      P.d.w = d->w + x0 * d->w_stride[4];
+      P.d.out = d->out + x0 * d->out_stride[4];
       P.d.xdim = xdim - x0 < SP_XMAX ? xdim - x0 : SP_XMAX;
     }
     if (P.csplit > 1) {
       const int64_t xd = mode == PDB_SP_OUT_ROW_CONTRACT ? P.d.xdim : 1;
-      sp_zero_kernel<<<256, 256, 0, s>>>(P.d.out, d->batch, d->rows, xd, d->out_stride[0], d->out_stride[1],
-                                         mode == PDB_SP_OUT_ROW_CONTRACT ? d->out_stride[2] : 0);
+      SpZero z{P.d.out, nriders, d->batch_mid, d->batch_inner, d->rows, xd,
+                {d->out_stride[0], d->out_stride[1], d->out_stride[2], d->out_stride[3],
+                 mode == PDB_SP_OUT_ROW_CONTRACT ? d->out_stride[4] : 0}};
+      sp_zero_kernel<<<256, 256, 0, s>>>(z);
     }
     score_program_kernel<<<grid, SP_THREADS, smem, s>>>(P);
     e = cudaGetLastError();

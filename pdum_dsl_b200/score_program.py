@@ -41,7 +41,7 @@ _WRAPS = ("tl.with_charts", "tl.strip_charts", "tl.simplify", "tl.with_labels", 
 _BIG = 1.0e30  # "no such index" for the first-index pre-pass
 
 _BIN = {"add", "sub", "mul", "div", "maximum", "minimum", "le", "lt", "ge", "gt", "eq", "ne", "and", "or"}
-_UN = {"exp", "log", "neg", "sqrt", "tanh", "abs", "not"}
+_UN = {"exp", "log", "neg", "sqrt", "tanh", "abs", "not", "floor"}
 
 
 def _unwrap(n):
@@ -56,6 +56,7 @@ class Pass:
 
     rows: str  # the program's row dim
     cols: str  # the program's column dim (reduced / contracted when the mode reduces)
+    batch: tuple = ()  # up to three rider dims (outer first): independent instances
     steps: list = field(default_factory=list)  # (kind, args tuple, value) SSA, index = value id
     scores: list = field(default_factory=list)  # (a_ref, b_ref, feature dim)
     rowvecs: list = field(default_factory=list)  # refs: ("param", i) | ("temp", k)
@@ -75,7 +76,7 @@ class Pass:
 @dataclass
 class ScoreProgramSpec:
     passes: list
-    temps: list  # per temp: dim name of the vector
+    temps: list  # per temp: its dim names (the pass's riders, then the vector's dim)
     out_dims: tuple
     extents: dict  # dim name -> (start, stop)
     param_dims: list  # per region param: its dim names (type-dim order)
@@ -116,8 +117,8 @@ class _Compiler:
         raise Untranslatable(f"3-D node {n.op}/{f} is not a broadcast product")
 
     # ------------------------------------------------------------ passes
-    def new_pass(self, rows, cols, mode):
-        p = Pass(rows, cols, mode=mode)
+    def new_pass(self, rows, cols, mode, batch=()):
+        p = Pass(rows, cols, batch=tuple(batch), mode=mode)
         self.passes.append(p)
         return p
 
@@ -146,18 +147,20 @@ class _Compiler:
         R, Cc = p.rows, p.cols
         if is_const(n):
             return self.const(p, const_value(n))
+        space = {R, Cc} | set(p.batch)
         i = self.pidx.get(id(n))
         if i is not None:
-            dn = names_of(n)
-            if dn == (R,):
-                return self.step(p, "row", (self._slot(p.rowvecs, ("param", i)),))
-            if dn == (Cc,):
-                return self.step(p, "col", (self._slot(p.colvecs, ("param", i)),))
-            if set(dn) == {R, Cc} and len(dn) == 2:
+            dn = set(names_of(n))
+            if not dn <= space:
+                raise Untranslatable(f"param with dims {names_of(n)} in a {p.batch + (R, Cc)} program")
+            if R in dn and Cc in dn:
                 return self.step(p, "tile", (self._slot(p.tiles, ("param", i)),))
-            raise Untranslatable(f"param with dims {dn} in a ({R}, {Cc}) program")
+            if Cc in dn:
+                return self.step(p, "col", (self._slot(p.colvecs, ("param", i)),))
+            # over the rows, or over riders only (then constant along the rows: stride 0)
+            return self.step(p, "row", (self._slot(p.rowvecs, ("param", i)),))
         dn = names_of(n)
-        if not set(dn) <= {R, Cc}:
+        if not set(dn) <= space:
             if n.op == "tl.reduce":
                 return self._score(p, n)
             raise Untranslatable(f"{n.op} with dims {dn} outside the score space ({R}, {Cc})")
@@ -188,11 +191,14 @@ class _Compiler:
         sides = {}
         for x in fac:
             i = self.param(x)
-            dx = names_of(_unwrap(x))
-            if i is None or len(dx) != 2 or f not in dx:
-                raise Untranslatable("score contraction operands must be 2-D params carrying the feature dim")
-            other = next(d for d in dx if d != f)
-            if other not in (p.rows, p.cols) or other in sides:
+            dx = set(names_of(_unwrap(x)))
+            if i is None or f not in dx:
+                raise Untranslatable("score contraction operands must be params carrying the feature dim")
+            own = dx & {p.rows, p.cols}
+            if len(own) != 1 or not dx - own - {f} <= set(p.batch):
+                raise Untranslatable("score contraction operands do not span the score space")
+            other = own.pop()
+            if other in sides:
                 raise Untranslatable("score contraction operands do not span the score space")
             sides[other] = ("param", i)
         ref = (sides[p.rows], sides[p.cols], f)
@@ -276,13 +282,13 @@ class _Compiler:
                 continue
             other = p.rows if dim == p.cols else p.cols
             # pre-pass over (other, dim): first index along dim where c holds, as a row minimum
-            pre = self.new_pass(other, dim, "row_min")
+            pre = self.new_pass(other, dim, "row_min", p.batch)
             pm: dict = {}
             cv = self.emit(pre, pm, c)
             idx = self.step(pre, "iota_col")
             pre.result = self.step(pre, "where", (cv, idx, self.const(pre, _BIG)))
             k = len(self.temps)
-            self.temps.append(other)
+            self.temps.append(tuple(p.batch) + (other,))
             pre.out = ("temp", k)
             # keep the pre-pass ahead of the pass that reads it
             self.passes.remove(pre)
@@ -347,12 +353,25 @@ def _allocate(p: Pass, max_regs: int) -> None:
     p.out_reg = reg[p.result]
 
 
+def _largest(cands, extents, order):
+    """The candidate dim with the largest extent (ties: the last in ``order``)."""
+    cands = [d for d in order if d in cands]
+    if not cands:
+        raise Untranslatable("no row dim for the score-space program")
+    return max(reversed(cands), key=lambda d: extents[d][1] - extents[d][0])
+
+
 def match_score_program(region, max_ops: int = 64, max_regs: int = 12) -> ScoreProgramSpec:
+    """The carve as score-space program passes.  The row dim is the kept score dim
+    (the largest candidate), the column dim the reduced / contracted one (or the
+    yield's last dim for a tile), and any remaining yield dims (at most three) are
+    riders: independent instances, broadcast (stride 0) in operands that lack them."""
     yld = _unwrap(region.body[-1].args[0])
     if yld.op == "core.tuple":
         raise Untranslatable("tuple yield")
     comp = _Compiler(region)
     out_dims = names_of(yld)
+    ext = comp.extents
     if yld.op == "tl.reduce":
         a = attrs(yld)
         rd = red_dims(yld)
@@ -361,45 +380,64 @@ def match_score_program(region, max_ops: int = 64, max_regs: int = 12) -> ScoreP
         s = rd[0]
         x = _unwrap(yld.args[0])
         xd = names_of(x)
-        if len(xd) == 2:
-            t = next(d for d in xd if d != s)
-            p = comp.new_pass(t, s, "row_" + a["f"])
+        if len(xd) == len(out_dims) + 1 and set(out_dims) | {s} == set(xd) and _is_program(comp, x):
+            t = _largest(set(xd) - {s}, ext, xd)
+            p = comp.new_pass(t, s, "row_" + a["f"], tuple(d for d in out_dims if d != t))
             p.result = comp.emit(p, {}, x)
-        elif len(xd) == 3 and a["f"] == "sum":
+        elif a["f"] == "sum":
             fac = comp.factors(x)
-            if len(fac) != 2 or any(s not in names_of(f) or len(names_of(f)) != 2 for f in fac):
+            if len(fac) != 2 or any(s not in names_of(f) for f in fac):
                 raise Untranslatable("contraction output is not (score-space expression) x (param matrix)")
             # the matrix operand is a param; the other factor is the score-space program
             order = sorted(fac, key=lambda f: comp.param(f) is not None)
-            prog, mats = order[:1], order[1:]
-            if comp.param(mats[0]) is None:
+            prog, mat = order
+            if comp.param(mat) is None:
                 raise Untranslatable("contraction output is not (score-space expression) x (param matrix)")
-            t = next(d for d in names_of(prog[0]) if d != s)
-            xdim = next(d for d in names_of(mats[0]) if d != s)
-            if set(out_dims) != {t, xdim}:
+            pd, md = set(names_of(prog)), set(names_of(mat))
+            xs = md - pd
+            if len(xs) != 1:
+                raise Untranslatable("the contraction's matrix operand must add exactly one output dim")
+            xdim = xs.pop()
+            t = _largest(pd - md - {s}, ext, names_of(prog))
+            batch = tuple(d for d in out_dims if d not in (t, xdim))
+            if set(out_dims) != {t, xdim} | set(batch) or not (pd | md) - {s, t, xdim} <= set(batch):
                 raise Untranslatable("contraction output dims do not match its operands")
-            p = comp.new_pass(t, s, "row_contract")
-            p.result = comp.emit(p, {}, prog[0])
-            p.w, p.x = ("param", comp.param(mats[0])), xdim
+            p = comp.new_pass(t, s, "row_contract", batch)
+            p.result = comp.emit(p, {}, prog)
+            p.w, p.x = ("param", comp.param(mat)), xdim
         else:
             raise Untranslatable("output reduce is not over a score-space expression")
-    elif len(out_dims) == 2:
-        p = comp.new_pass(out_dims[0], out_dims[1], "tile")
+    elif len(out_dims) >= 2:
+        p = comp.new_pass(out_dims[-2], out_dims[-1], "tile", out_dims[:-2])
         p.result = comp.emit(p, {}, yld)
     else:
         raise Untranslatable(f"yield of rank {len(out_dims)} is not a score-space program output")
-    if not any(ps.scores or ps.rowvecs or ps.colvecs or ps.tiles for ps in comp.passes):
-        raise Untranslatable("program reads no operand")
+    if any(len(ps.batch) > 3 for ps in comp.passes):
+        raise Untranslatable("more than three rider dims")
     for ps in comp.passes:
         if len(ps.scores) > 2 or len(ps.rowvecs) > 6 or len(ps.colvecs) > 6 or len(ps.tiles) > 4:
             raise Untranslatable("score program reads more operands than the kernel takes")
         _allocate(ps, max_regs)
         if len(ps.ops) > max_ops:
             raise Untranslatable(f"score program of {len(ps.ops)} steps (at most {max_ops})")
-    src = "; ".join(f"pass {k}: ({ps.rows}, {ps.cols}) {ps.mode} {len(ps.ops)} steps {ps.n_regs} regs "
+    src = "; ".join(f"pass {k}: {ps.batch + (ps.rows, ps.cols)} {ps.mode} {len(ps.ops)} steps {ps.n_regs} regs "
                     f"{len(ps.scores)} contractions" for k, ps in enumerate(comp.passes))
     pdims = [names_of(p) for p in region.params]
     return ScoreProgramSpec(comp.passes, comp.temps, out_dims, comp.extents, pdims, "pdb_score_program_f32 " + src)
+
+
+def _is_program(comp, x) -> bool:
+    """True when x is an elementwise score-space expression (not a broadcast product
+    to be contracted: those have a dim the output lacks besides the reduced one)."""
+    x = _unwrap(x)
+    if x.op in ("tl.repeat", "tl.repeat_like") or f_of(x) in ("mul", "mul.d0", "mul.d1"):
+        try:
+            fac = comp.factors(x)
+        except Untranslatable:
+            return True
+        return not (len(fac) == 2 and any(comp.param(f) is not None for f in fac)
+                    and len(names_of(x)) > max(len(names_of(f)) for f in fac))
+    return True
 
 
 # ------------------------------------------------------------------ execution
@@ -412,9 +450,9 @@ def run_score_program(spec: ScoreProgramSpec, tensors):
     from . import _lib
 
     ext = {k: v[1] - v[0] for k, v in spec.extents.items()}
-    dev = tensors[0].device
+    dev = tensors[0].device if tensors else torch.device("cuda", torch.cuda.current_device())
     ts = [t if t.dtype == torch.float32 else t.float() for t in tensors]
-    temps = [torch.empty(ext[d], dtype=torch.float32, device=dev) for d in spec.temps]
+    temps = [torch.empty(tuple(ext[d] for d in dims), dtype=torch.float32, device=dev) for dims in spec.temps]
     lib = _lib.load()
     stream = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     out = None
@@ -423,31 +461,39 @@ def run_score_program(spec: ScoreProgramSpec, tensors):
         kind, i = ref
         if kind == "param":
             return ts[i], spec.param_dims[i]
-        return temps[i], (spec.temps[i],)
+        return temps[i], spec.temps[i]
 
     def stride(ref, dim):
         t, names = view(ref)
-        return t.stride(names.index(dim))
+        return t.stride(names.index(dim)) if dim in names else 0
 
     for ps in spec.passes:
+        bd = list(ps.batch)
+        while len(bd) < 3:
+            bd.insert(0, None)
+
+        def bstr(ref):
+            return tuple(stride(ref, b) if b is not None else 0 for b in bd)
+
         d = _lib.ScoreProgramDesc()
-        d.batch, d.rows, d.cols = 1, ext[ps.rows], ext[ps.cols]
+        d.batch, d.batch_mid, d.batch_inner = (ext[b] if b is not None else 1 for b in bd)
+        d.rows, d.cols = ext[ps.rows], ext[ps.cols]
         d.row_start, d.col_start = spec.extents[ps.rows][0], spec.extents[ps.cols][0]
         for k, (aref, bref, f) in enumerate(ps.scores):
             d.score_a[k], d.score_b[k] = view(aref)[0].data_ptr(), view(bref)[0].data_ptr()
-            d.score_a_stride[k] = _lib.I64x3(0, stride(aref, ps.rows), stride(aref, f))
-            d.score_b_stride[k] = _lib.I64x3(0, stride(bref, ps.cols), stride(bref, f))
+            d.score_a_stride[k] = _lib.I64x5(*bstr(aref), stride(aref, ps.rows), stride(aref, f))
+            d.score_b_stride[k] = _lib.I64x5(*bstr(bref), stride(bref, ps.cols), stride(bref, f))
             d.score_feat[k] = ext[f]
         d.n_scores = len(ps.scores)
         for k, ref in enumerate(ps.rowvecs):
             d.rowvec[k] = view(ref)[0].data_ptr()
-            d.rowvec_stride[k] = _lib.I64x2(0, stride(ref, ps.rows))
+            d.rowvec_stride[k] = _lib.I64x4(*bstr(ref), stride(ref, ps.rows))
         for k, ref in enumerate(ps.colvecs):
             d.colvec[k] = view(ref)[0].data_ptr()
-            d.colvec_stride[k] = _lib.I64x2(0, stride(ref, ps.cols))
+            d.colvec_stride[k] = _lib.I64x4(*bstr(ref), stride(ref, ps.cols))
         for k, ref in enumerate(ps.tiles):
             d.tile[k] = view(ref)[0].data_ptr()
-            d.tile_stride[k] = _lib.I64x3(0, stride(ref, ps.rows), stride(ref, ps.cols))
+            d.tile_stride[k] = _lib.I64x5(*bstr(ref), stride(ref, ps.rows), stride(ref, ps.cols))
         for k, (kind, dst, a, b, c, value) in enumerate(ps.ops):
             o = d.ops[k]
             o.op, o.dst, o.a, o.b, o.c, o.value = _lib.SP_OPS[kind], dst, a, b, c, value
@@ -455,18 +501,22 @@ def run_score_program(spec: ScoreProgramSpec, tensors):
         d.out_mode = _lib.SP_OUT[ps.mode]
         if ps.out[0] == "temp":
             o_t = temps[ps.out[1]]
-            d.out_stride = _lib.I64x3(0, o_t.stride(0), 0)
+            tref = ("temp", ps.out[1])
+            d.out_stride = _lib.I64x5(*bstr(tref), stride(tref, ps.rows), 0)
         else:
             on = spec.out_dims
             o_t = torch.empty(tuple(ext[n] for n in on), dtype=torch.float32, device=dev)
             second = ps.cols if ps.mode == "tile" else ps.x if ps.mode == "row_contract" else None
-            d.out_stride = _lib.I64x3(0, o_t.stride(on.index(ps.rows)),
-                                      o_t.stride(on.index(second)) if second else 0)
+
+            def ostr(n):
+                return o_t.stride(on.index(n)) if n is not None and n in on else 0
+
+            d.out_stride = _lib.I64x5(ostr(bd[0]), ostr(bd[1]), ostr(bd[2]), ostr(ps.rows), ostr(second))
             out = o_t
         d.out = o_t.data_ptr()
         if ps.mode == "row_contract":
             d.w = view(ps.w)[0].data_ptr()
-            d.w_stride = _lib.I64x3(0, stride(ps.w, ps.cols), stride(ps.w, ps.x))
+            d.w_stride = _lib.I64x5(*bstr(ps.w), stride(ps.w, ps.cols), stride(ps.w, ps.x))
             d.xdim = ext[ps.x]
         _lib.check(lib.pdb_score_program_f32(C.byref(d), stream), "pdb_score_program_f32")
     return out

@@ -87,6 +87,38 @@ def _reference_carve_values(plan, region, tens):
     return per
 
 
+def _widened_joint(kind):
+    from pdum_dsl_b200.regions import attention_region
+
+    kw = {"riders": dict(B=2, H=2, T=40, D=16, causal=True, scale=0.3),
+          "gqa": dict(B=1, H=2, T=33, D=16, causal=True, scale=0.3, group=2),
+          "window": dict(T=72, D=16, causal=True, window=20, scale=0.3),
+          "block": dict(T=72, D=16, causal=False, block=24, scale=0.3)}[kind]
+    return _joint(attention_region(**kw))
+
+
+@pytest.mark.parametrize("kind", ["riders", "gqa", "window", "block"])
+def test_widened_joints_carve_by_carve_all_on_device(cuda, dsl, kind):
+    """Joints of widened regions (batch / head riders, a GQA group, sliding-window and
+    block-diagonal masks): plan_model carves them differently (rider carves are rank 3-5),
+    and every carve still runs on the device, matching run_region of the joint."""
+    import torch
+    from pdum.tl.dialect import run_region
+    from pdum.tl.partition import plan_model
+
+    from pdum_dsl_b200.plan import device_assignment, execute_model_plan
+
+    rg = _widened_joint(kind)
+    plan = plan_model(rg.region)
+    n = sum(c.root is not None for c in plan.carves)
+    assert device_assignment(plan) == ["device"] * n
+    arrs, tens = _inputs(rg.region, 6)
+    want = run_region(rg.region, list(tens))
+    got, _ = execute_model_plan(plan, rg.region, [torch.tensor(a, dtype=torch.float32, device=cuda) for a in arrs])
+    for g, w, what in zip(got, want, ("out", "dq", "dk", "dv")):
+        assert_f32(g.cpu().numpy(), w.to_numpy(order=w.names), what=f"{kind} {what}")
+
+
 @pytest.mark.parametrize("T,E", [(96, 16), (160, 64)])
 def test_each_carve_matches_run_region_on_the_reference_boundary_values(cuda, dsl, T, E):
     """Every carve alone (score-space programs, the flash carve and the GEMM carves),

@@ -27,6 +27,21 @@ def test_every_carve_of_the_flash_joint_lowers(dsl):
     assert any(c.group.confidence == "red" for c in plan.carves)  # the max-adjoint scan is among them
 
 
+@pytest.mark.parametrize("kw", [dict(B=2, H=2, T=16, D=8, causal=True, scale=0.3),
+                                dict(B=1, H=2, T=16, D=8, causal=True, scale=0.3, group=2),
+                                dict(T=16, D=8, causal=True, window=5), dict(T=16, D=8, causal=False, block=4)])
+def test_every_carve_of_widened_joints_lowers(dsl, kw):
+    """Rider joints carve into rank-3..5 pieces (map chains, red scans, contractions with
+    riders); block masks bring floor / div into the carves: all lower."""
+    from pdum.tl.partition import plan_model
+
+    from pdum_dsl_b200.plan import device_assignment
+    from pdum_dsl_b200.regions import attention_region
+
+    plan = plan_model(_joint(attention_region(**kw)).region)
+    assert device_assignment(plan) == ["device"] * len(plan.carves)
+
+
 def test_score_program_shapes(dsl):
     from pdum.tl.partition import plan_model
     from pdum.tl.zoo.tiles import flash_tile
