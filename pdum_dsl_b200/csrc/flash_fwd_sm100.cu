@@ -65,6 +65,7 @@ struct FwdParams {
   const int32_t* key_hi;
   int mask_monotone;
   int lpt;          // heaviest-first snake schedule (else head-major pairs)
+  int DV;           // the value / output head dim (<= the kernel's D; the TMA maps zero-fill the rest)
   int num_mblocks;  // 256-row blocks per head
   float scale_log2;  // scale * log2(e)
   int* err;
@@ -455,8 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) {
 #pragma unroll
-        for (int bx = 0; bx < D / 64; ++bx)
-          tma_store_4d(&tm_o, stg + bx * 4096, bx * 64, ti.t0 + x * BM + q4 * 32, ti.h, ti.b);
+        for (int bx = 0; bx < D / 64; ++bx)  // boxes wholly past the value head dim are not stored
+          if (bx * 64 < p.DV) tma_store_4d(&tm_o, stg + bx * 4096, bx * 64, ti.t0 + x * BM + q4 * 32, ti.h, ti.b);
         bulk_commit();
         bulk_wait_read_all();
         mbar_arrive(&bar->stg_free[q4]);
@@ -750,7 +751,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (store) {
           uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          for (int i = 0; i < 4; ++i)  // columns past the value head dim are padding (zero by construction)
+            if (ch * 32 + i * 8 < p.DV) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
       }
       warp_arrive_after_tc(&bar->o_empty[x]);
@@ -775,19 +777,23 @@ template <int D>
 int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   CUtensorMap tq, tk, tv;
   const uint32_t box[4] = {64, 128, 1, 1};
+  // The maps carry the true head dims: feature columns from head_dim (q, k) or
+  // head_dim_v (v) up to D are zero-filled by the TMA, so they add nothing to the
+  // scores and produce zero output columns, which the stores drop.
   {
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)d.seqlen_q, (uint64_t)d.heads_q, (uint64_t)d.batch};
+    const uint64_t dims[4] = {(uint64_t)d.head_dim, (uint64_t)d.seqlen_q, (uint64_t)d.heads_q, (uint64_t)d.batch};
     const uint64_t str[3] = {(uint64_t)d.q_stride[2] * 2, (uint64_t)d.q_stride[1] * 2, (uint64_t)d.q_stride[0] * 2};
     if (int st = encode_tma_4d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return st;
   }
   {
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)d.seqlen_k, (uint64_t)d.heads_kv, (uint64_t)d.batch};
+    const uint64_t dk[4] = {(uint64_t)d.head_dim, (uint64_t)d.seqlen_k, (uint64_t)d.heads_kv, (uint64_t)d.batch};
+    const uint64_t dv[4] = {(uint64_t)d.head_dim_v, (uint64_t)d.seqlen_k, (uint64_t)d.heads_kv, (uint64_t)d.batch};
     const uint64_t sk[3] = {(uint64_t)d.k_stride[2] * 2, (uint64_t)d.k_stride[1] * 2, (uint64_t)d.k_stride[0] * 2};
     const uint64_t sv[3] = {(uint64_t)d.v_stride[2] * 2, (uint64_t)d.v_stride[1] * 2, (uint64_t)d.v_stride[0] * 2};
-    if (int st = encode_tma_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.k, dims, sk, box, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (int st = encode_tma_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.k, dk, sk, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return st;
-    if (int st = encode_tma_4d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.v, dims, sv, box, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (int st = encode_tma_4d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.v, dv, sv, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return st;
   }
   FwdParams p;
@@ -798,6 +804,7 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   for (int i = 0; i < 3; ++i) p.o_stride[i] = d.o_stride[i];
   p.T = (int)d.seqlen_q;
   p.S = (int)d.seqlen_k;
+  p.DV = (int)d.head_dim_v;
   p.H = (int)d.heads_q;
   p.HKV = (int)d.heads_kv;
   p.B = (int)d.batch;
@@ -829,7 +836,7 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   } else {
   CUtensorMap to;  // O stores: 32-row boxes, one per softmax warp
   {
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)d.seqlen_q, (uint64_t)d.heads_q, (uint64_t)d.batch};
+    const uint64_t dims[4] = {(uint64_t)d.head_dim_v, (uint64_t)d.seqlen_q, (uint64_t)d.heads_q, (uint64_t)d.batch};
     const uint64_t so[3] = {(uint64_t)d.o_stride[2] * 2, (uint64_t)d.o_stride[1] * 2, (uint64_t)d.o_stride[0] * 2};
     const uint32_t obox[4] = {64, 32, 1, 1};
     if (int st = encode_tma_4d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.o, dims, so, obox, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -846,14 +853,20 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
 }  // namespace
 
 int flash_fwd_bf16_sm100(const pdb_flash_desc& d, cudaStream_t stream) {
-  if (d.head_dim != d.head_dim_v || (d.head_dim != 64 && d.head_dim != 128))
-    return set_error(PDB_ERR_UNSUPPORTED, "bf16 flash: head_dim == head_dim_v in {64, 128} required (got %lld, %lld)",
+  // head dims up to 64 run the D = 64 kernel, up to 128 the D = 128 kernel (the
+  // tensor maps zero-fill the feature columns between the true head dim and D);
+  // rows of q / k / v / o must be 16-byte multiples (TMA), so both dims are
+  // multiples of 8, and at least 64 (the TMA box is 64 features wide)
+  const int64_t dmax = d.head_dim > d.head_dim_v ? d.head_dim : d.head_dim_v;
+  if (d.head_dim % 8 || d.head_dim_v % 8 || d.head_dim < 64 || d.head_dim_v < 64 || dmax > 128)
+    return set_error(PDB_ERR_UNSUPPORTED,
+                     "bf16 flash: head dims must be multiples of 8 in [64, 128] (got %lld, %lld)",
                      (long long)d.head_dim, (long long)d.head_dim_v);
   if (d.seqlen_q > 0x7fffffffLL - 512 || d.seqlen_k > 0x7fffffffLL - 512 || d.q_start > 0x3fffffffLL)
     return set_error(PDB_ERR_SHAPE, "bf16 flash: sequence too long");
   if ((reinterpret_cast<uintptr_t>(d.o) & 15u) || (d.o_stride[0] & 7) || (d.o_stride[1] & 7) || (d.o_stride[2] & 7))
     return set_error(PDB_ERR_ALIGN, "bf16 flash: o must be 16-byte aligned with strides multiple of 8 elements");
-  return d.head_dim == 64 ? launch<64>(d, stream) : launch<128>(d, stream);
+  return dmax <= 64 ? launch<64>(d, stream) : launch<128>(d, stream);
 }
 
 }  // namespace pdb

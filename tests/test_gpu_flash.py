@@ -211,3 +211,37 @@ def test_bf16_config4_gqa_slices(cuda):
                                   v[b, hk].double().cpu().numpy(), scale=1 / math.sqrt(128), causal=True,
                                   row_block=1024)
         assert_bf16(_np(o[b, h]), ro, what=f"head ({b},{h})")
+
+
+@pytest.mark.parametrize("D,DV,causal", [(96, 96, True), (128, 64, True), (64, 128, False), (80, 112, True),
+                                         (72, 72, False)])
+def test_bf16_head_dims_between_the_builds(cuda, D, DV, causal):
+    """Head dims other than 64 / 128 (and e != o) on the tensor-core kernels: the
+    tensor maps zero-fill the features up to the kernel's 64 or 128."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device="cpu").manual_seed(D * 3 + DV)
+    q = torch.randn(1, 3, 300, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, 3, 300, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, 3, 300, DV, generator=g).to(torch.bfloat16)
+    o = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), scale=1 / math.sqrt(D), causal=causal)
+    kernels.check_device_errors()
+    assert o.shape == (1, 3, 300, DV)
+    ro, *_ = OA.attention_fwd(q.double().numpy(), k.double().numpy(), v.double().numpy(), scale=1 / math.sqrt(D),
+                              causal=causal)
+    assert_bf16(_np(o), ro, what=f"D={D} DV={DV}")
+
+
+def test_f32_head_dims_up_to_256(cuda):
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    g = torch.Generator(device="cpu").manual_seed(256)
+    q, k = (torch.randn(1, 2, 150, 256, generator=g) for _ in range(2))
+    v = torch.randn(1, 2, 150, 192, generator=g)
+    o = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), scale=1 / 16, causal=True)
+    ro, *_ = OA.attention_fwd(q.double().numpy(), k.double().numpy(), v.double().numpy(), scale=1 / 16, causal=True)
+    assert_f32(_np(o), ro)
