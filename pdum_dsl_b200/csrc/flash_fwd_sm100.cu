@@ -109,6 +109,14 @@ struct TileInfo {
   int b, h, hk, t0, j0, nA, nB;
 };
 
+// Registers written by tcgen05.ld are valid only after tcgen05.wait::ld; this
+// empty asm makes every later use of r[0..N) depend on a point after the wait.
+template <int N>
+__device__ __forceinline__ void regs_after_wait(uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // The exponential phase of one 32-score chunk: P = exp2(s c - m) as 16 bf16
 // pairs (packed f32x2 FMA for the argument, MUFU ex2 per score, cvt.rn.bf16x2
 // to pack) and the pairs' f32 row sums on two chains.
@@ -368,23 +376,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           lim = row_hi - kb < lim ? row_hi - kb : lim;
         }
         const bool need_mask = __any_sync(0xffffffffu, lim < BN || lo_rel > 0);
-        // all 128 scores of the row in registers: one TMEM round trip
+        // the 128 scores of the row in registers, in two halves: the second half's
+        // TMEM loads are in flight while the first half is masked and maxed
         uint32_t sr[BN];
-#pragma unroll
-        for (int ch = 0; ch < BN / 32; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
-        tmem_wait_ld();
-        if (need_mask) {
-#pragma unroll
-          for (int i = 0; i < BN; ++i)
-            if (i >= lim || i < lo_rel) sr[i] = __float_as_uint(-INFINITY);
-        }
         float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;  // 4 independent chains
 #pragma unroll
-        for (int i = 0; i < BN; i += 8) {
-          mxa = max3(mxa, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
-          mxb = max3(mxb, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
-          mxc = max3(mxc, __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
-          mxd = max3(mxd, __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
+        for (int ch = 0; ch < 2; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
+        tmem_wait_ld();
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          if (hf == 0) {
+#pragma unroll
+            for (int ch = 2; ch < 4; ++ch)
+              tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
+          } else {
+            tmem_wait_ld();
+            regs_after_wait<BN / 2>(sr + BN / 2);  // no use of the second half moves above its wait
+          }
+          uint32_t* h = sr + hf * (BN / 2);
+          if (need_mask) {
+#pragma unroll
+            for (int i = 0; i < BN / 2; ++i)
+              if (hf * (BN / 2) + i >= lim || hf * (BN / 2) + i < lo_rel) h[i] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int i = 0; i < BN / 2; i += 8) {
+            mxa = max3(mxa, __uint_as_float(h[i]), __uint_as_float(h[i + 1]));
+            mxb = max3(mxb, __uint_as_float(h[i + 2]), __uint_as_float(h[i + 3]));
+            mxc = max3(mxc, __uint_as_float(h[i + 4]), __uint_as_float(h[i + 5]));
+            mxd = max3(mxd, __uint_as_float(h[i + 6]), __uint_as_float(h[i + 7]));
+          }
         }
         const float mt = fmaxf(max3(mxa, mxb, mxc), mxd) * c;
         m_true = fmaxf(m_true, mt);
