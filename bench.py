@@ -249,6 +249,15 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def _dsl_on_path():
+    """The reference DSL (pdum.dsl / pdum.tl) the drop-in runner plans against: an
+    installed copy, or the importable copy kept in baseline/_ref."""
+    for pkg in ("dsl", "tensorlib"):
+        src = REPO / "baseline" / "_ref" / "packages" / pkg / "src"
+        if src.is_dir() and str(src) not in sys.path:
+            sys.path.insert(0, str(src))
+
+
 def _region(units):
     """The attention region of a (1, units, S, D) job, spelled as the DSL spells it."""
     from pdum_dsl_b200.regions import attention_region
@@ -265,9 +274,7 @@ def _e2e(q, k, v, o, flop_job, world, stream, steps):
     oh = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
     api = "compile_tile(attention_region(...), dtype='bf16')(values, out=host) [pinned host buffers]"
     try:
-        from oracle.make_ref_shim import ensure_importable
-
-        ensure_importable()
+        _dsl_on_path()
         from pdum_dsl_b200.tile import compile_tile
 
         run = compile_tile(_region(q.shape[1]), dtype="bf16")

@@ -110,11 +110,10 @@ def case_score_program(T=2048, E=64):
     """The den-gradient carve of the attention joint (a row-sum score program)."""
     import torch
 
-    from oracle.make_ref_shim import ensure_importable
-
-    if not ensure_importable():
-        raise SystemExit("score_program needs the reference DSL copy (python oracle/make_ref_shim.py)")
-    from pdum.tl.autodiff import grad
+    try:
+        from pdum.tl.autodiff import grad
+    except ImportError:
+        raise SystemExit("score_program needs the reference DSL (pdum.dsl / pdum.tl) importable") from None
     from pdum.tl.partition import plan_model
     from pdum.tl.zoo.tiles import flash_tile
 
