@@ -119,7 +119,8 @@ def _dist():
     return world, rank, local
 
 
-GATHER_SLABS = 2  # slabs of the overlapped final gather (N > 1)
+GATHER_SLABS = 4  # slabs of the overlapped final gather (N > 1)
+GATHER_SM_MARGIN = 16  # SMs the forward leaves to NCCL's all-gather kernels while they overlap
 
 
 def _shard(world, rank, scaling):
@@ -314,8 +315,10 @@ def _gather_inclusive(q, k, v, ranges, world, stream, flop_job):
         j += n
     comm = torch.cuda.Stream(dev)
 
+    # the forward leaves SMs to NCCL so the gather of slab c runs while slab c + 1 computes
+    # (the persistent kernel otherwise holds every SM until it retires)
     def attend(qs, ks, vs, os_):
-        return kernels.flash_attention(qs, ks, vs, causal=True, out=os_)
+        return kernels.flash_attention(qs, ks, vs, causal=True, out=os_, sm_margin=GATHER_SM_MARGIN)
 
     step = lambda: gather_overlapped(attend, ins, outs, comm_stream=comm)  # noqa: E731
     ms, _ = _timed(step, 5, 2, stream, world)
@@ -331,7 +334,9 @@ def _gather_inclusive(q, k, v, ranges, world, stream, flop_job):
             "predicted_gather_ms": 1e3 * alpha_beta_seconds(moved, NVLINK_BPS, NCCL_LATENCY_S),
             "model": "placement.traffic all-gather ((p-1)/p x output bytes), alpha-beta at "
                      f"{NVLINK_BPS / 1e9:.0f} GB/s per direction + {NCCL_LATENCY_S * 1e6:.0f} us",
-            "note": "forward + all_gather_into_tensor per slab on a side stream (NCCL, no multicast loads)"}
+            "sm_margin": GATHER_SM_MARGIN,
+            "note": "forward + all_gather_into_tensor per slab on a side stream (NCCL, no multicast loads); "
+                    "the forward leaves sm_margin SMs to NCCL so the gathers overlap the next slab"}
 
 
 def run_ours(args):

@@ -118,7 +118,8 @@ typedef struct {
   const int32_t* key_lo; /* nullable: per query row, first visible key */
   const int32_t* key_hi; /* per query row, one past the last visible key */
   int32_t mask_monotone;
-  int32_t reserved;
+  int32_t sm_margin; /* bf16 path: SMs the persistent grid leaves free (e.g. for a collective
+                        that overlaps this launch); 0 = use every SM */
 } pdb_flash_desc;
 int pdb_flash_fwd(const pdb_flash_desc* d, void* stream);
 

@@ -111,7 +111,7 @@ class FlashDesc(C.Structure):
         ("key_lo", C.c_void_p),
         ("key_hi", C.c_void_p),
         ("mask_monotone", C.c_int32),
-        ("reserved", C.c_int32),
+        ("sm_margin", C.c_int32),
     ]
 
 

@@ -842,7 +842,8 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int64_t pairs = (nblk + 1) / 2;
-  const int sms = sm_count(dev);
+  int sms = sm_count(dev) - (d.sm_margin > 0 ? d.sm_margin : 0);
+  if (sms < 1) sms = 1;
   // a job of fewer than 4 waves of pairs schedules single tiles heaviest first
   p.lpt = pairs < 4 * (int64_t)sms ? 1 : 0;
   const int64_t units = p.lpt ? nblk : pairs;

@@ -91,7 +91,8 @@ def _s3(t: torch.Tensor):
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float | None = None,
                     causal: bool = False, q_start: int = 0, out: torch.Tensor | None = None,
-                    return_lse: bool = False, return_artifacts: bool = False, key_intervals=None):
+                    return_lse: bool = False, return_artifacts: bool = False, key_intervals=None,
+                    sm_margin: int = 0):
     """softmax(scale * q k^T [causal: s <= t + q_start]) v.
 
     q (B, Hq, T, D), k/v (B, Hkv, S, D|Dv) with Hq a multiple of Hkv (GQA);
@@ -99,7 +100,9 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale:
     (D, Dv multiples of 8 in [64, 128]); f32 runs the IEEE CUDA-core kernel (any D, Dv <= 256).  Returns o, or
     (o, lse) / (o, m, den) with the per-row float32 statistics.
     ``key_intervals`` (a ``recognize.KeyIntervals`` of T rows) is a general
-    closed mask: row t sees keys lo[t] <= s < hi[t] (``causal`` must be False)."""
+    closed mask: row t sees keys lo[t] <= s < hi[t] (``causal`` must be False).
+    ``sm_margin`` SMs are left free by the persistent bf16 grid (for a collective
+    that runs alongside, e.g. the all-gather of the previous slab's output)."""
     _need_cuda(q, k, v)
     if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
         raise TypeError(f"flash_attention: q/k/v must share dtype float32 or bfloat16, got {q.dtype}/{k.dtype}/{v.dtype}")
@@ -126,6 +129,7 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale:
     d.batch, d.heads_q, d.heads_kv, d.seqlen_q, d.seqlen_k, d.head_dim, d.head_dim_v = B, H, HKV, T, S, D, DV
     d.q_stride, d.k_stride, d.v_stride, d.o_stride = _s3(q4), _s3(k4), _s3(v4), _s3(o)
     d.q_start, d.scale, d.causal, d.dtype = int(q_start), float(scale), int(bool(causal)), _DTYPES[q.dtype]
+    d.sm_margin = int(sm_margin)
     keep = None
     if key_intervals is not None:
         if causal:
