@@ -133,9 +133,12 @@ int pdb_flash_fwd(const pdb_flash_desc* d, void* stream);
  * Workspace (float32) holds D and, for head_dim 64, the dQ accumulator; its
  * size in bytes comes from pdb_flash_bwd_workspace_size.  If lse is NULL the
  * kernel recomputes it (the "recompute" variant of the template); otherwise it
- * is the forward's stored lse ("stored" variant).  head_dim 64 runs one fused
- * pass whose dQ sums per-key-block parts with fp32 reductions in L2, so dq's
- * last bits may differ run to run (dk, dv and head_dim 128 are reproducible). */
+ * is the forward's stored lse ("stored" variant).  head_dim and head_dim_v
+ * are multiples of 8 in [64, 128] and may differ.  head_dim == head_dim_v == 64
+ * runs one fused pass whose dQ sums per-key-block parts with fp32 reductions in
+ * L2, so dq's last bits may differ run to run; every other shape runs the
+ * 128-wide dK/dV and dQ passes, with tensor maps that zero-fill the features
+ * past each dim (reproducible).  Other dims return PDB_ERR_SHAPE. */
 typedef struct {
   const void* q;
   const void* k;

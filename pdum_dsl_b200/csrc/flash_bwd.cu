@@ -57,6 +57,7 @@ struct BwdParams {
   int B;
   int* ctr;      // work-unit counter of a persistent kernel (zeroed by the prologue)
   int* err;
+  int ncols0, ncols1;  // true feature columns of out0 / out1 (<= D; the TMA maps zero-fill the rest)
 };
 
 
@@ -86,7 +87,8 @@ __device__ __forceinline__ void mma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uin
 
 // rows of a TMEM accumulator (columns [c0, c0 + NC)) -> bf16 global, scaled
 template <int NC>
-__device__ __forceinline__ void store_cols_bf16(uint32_t t_src, float mul, __nv_bfloat16* row, bool store) {
+__device__ __forceinline__ void store_cols_bf16(uint32_t t_src, float mul, __nv_bfloat16* row, bool store,
+                                                int ncols = NC) {
 #pragma unroll
   for (int ch = 0; ch < NC / 32; ++ch) {
     uint32_t r[32];
@@ -98,7 +100,8 @@ __device__ __forceinline__ void store_cols_bf16(uint32_t t_src, float mul, __nv_
     if (store) {
       uint4* dst = reinterpret_cast<uint4*>(row + ch * 32);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      for (int i = 0; i < 4; ++i)  // columns past ncols are zero padding of the head dim: not stored
+        if (ch * 32 + i * 8 < ncols) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
     }
   }
 }
@@ -394,12 +397,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           : static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] + (int64_t)s * p.s0[2];
       if (n_items == 0) {  // a key block past every query row: dK = dV = 0
         if (store)
-          for (int i = 0; i < D; i += 8) *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
+          for (int i = 0; i < (x == 0 ? p.ncols1 : p.ncols0); i += 8)
+            *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
         continue;
       }
       if (!(ok = mbar_wait(&bar->o_full, nkv & 1, abort, p.err))) break;
       tc_fence_after();
-      store_cols_bf16<D>(tmem + lane_off + 256 + x * D, x == 0 ? 1.0f : p.scale, dst, store);
+      store_cols_bf16<D>(tmem + lane_off + 256 + x * D, x == 0 ? 1.0f : p.scale, dst, store,
+                         x == 0 ? p.ncols1 : p.ncols0);
       warp_arrive_after_tc(&bar->acc_free);
       gi += n_items;
       ++nkv;
@@ -599,7 +604,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = mbar_wait(&bar->o_full, nqd & 1, abort, p.err))) break;
       tc_fence_after();
       // each warpgroup writes half of the dQ columns
-      store_cols_bf16<D / 2>(tmem + lane_off + 256 + x * (D / 2), p.scale, dq + x * (D / 2), t < p.T);
+      store_cols_bf16<D / 2>(tmem + lane_off + 256 + x * (D / 2), p.scale, dq + x * (D / 2), t < p.T,
+                             p.ncols0 - x * (D / 2));
       warp_arrive_after_tc(&bar->acc_free);
       gi += n_kv;
       ++nqd;
@@ -1194,7 +1200,7 @@ WsLayout ws_layout(const pdb_flash_bwd_desc& d) {
   off = align256(off + rows * 4);
   w.ctr = off;  // two work-unit counters
   off = align256(off + 8);
-  if (d.head_dim == 64) {  // fp32 dQ accumulator of the fused pass, rows padded like lse2
+  if (d.head_dim == 64 && d.head_dim_v == 64) {  // fp32 dQ accumulator of the fused pass, rows padded like lse2
     w.dqacc = off;
     off = align256(off + rows * 64 * 4);
   }
@@ -1273,10 +1279,13 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
   }
   // dK/dV kernel: 64-row query tiles, 128-key blocks; dQ kernel: 128-row query blocks, 64-key tiles
   CUtensorMap tk128, tv128, tq128, tdo128;
-  if (int st = map_bf16(&tk128, d.k, D, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, 128)) return st;
-  if (int st = map_bf16(&tv128, d.v, D, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, 128)) return st;
-  if (int st = map_bf16(&tq128, d.q, D, d.seqlen_q, d.heads_q, d.batch, d.q_stride, 128)) return st;
-  if (int st = map_bf16(&tdo128, d.dout, D, d.seqlen_q, d.heads_q, d.batch, d.do_stride, 128)) return st;
+  // the maps carry the true head dims (e for q / k, e_v for v / dO): features between
+  // them and D are zero-filled, so they add nothing to the scores or the gradients
+  const int E = (int)d.head_dim, EV = (int)d.head_dim_v;
+  if (int st = map_bf16(&tk128, d.k, E, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, 128)) return st;
+  if (int st = map_bf16(&tv128, d.v, EV, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, 128)) return st;
+  if (int st = map_bf16(&tq128, d.q, E, d.seqlen_q, d.heads_q, d.batch, d.q_stride, 128)) return st;
+  if (int st = map_bf16(&tdo128, d.dout, EV, d.seqlen_q, d.heads_q, d.batch, d.do_stride, 128)) return st;
   BwdParams p{};
   p.nlse2 = lse2;
   p.dsum = dsum;
@@ -1335,13 +1344,15 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     return PDB_OK;
   } else {
     CUtensorMap tq64, tdo64, tk64, tv64;  // 64-row boxes: dK/dV query items, dQ key items
-    if (int st = map_bf16(&tq64, d.q, D, d.seqlen_q, d.heads_q, d.batch, d.q_stride, QT)) return st;
-    if (int st = map_bf16(&tdo64, d.dout, D, d.seqlen_q, d.heads_q, d.batch, d.do_stride, QT)) return st;
-    if (int st = map_bf16(&tk64, d.k, D, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, KT)) return st;
-    if (int st = map_bf16(&tv64, d.v, D, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, KT)) return st;
+    if (int st = map_bf16(&tq64, d.q, E, d.seqlen_q, d.heads_q, d.batch, d.q_stride, QT)) return st;
+    if (int st = map_bf16(&tdo64, d.dout, EV, d.seqlen_q, d.heads_q, d.batch, d.do_stride, QT)) return st;
+    if (int st = map_bf16(&tk64, d.k, E, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, KT)) return st;
+    if (int st = map_bf16(&tv64, d.v, EV, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, KT)) return st;
     {  // dK, dV
       p.out0 = d.dk;
       p.out1 = d.dv;
+      p.ncols0 = E;
+      p.ncols1 = EV;
       for (int i = 0; i < 3; ++i) {
         p.s0[i] = d.dk_stride[i];
         p.s1[i] = d.dv_stride[i];
@@ -1361,6 +1372,8 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     {  // dQ
       p.out0 = d.dq;
       p.out1 = nullptr;
+      p.ncols0 = E;
+      p.ncols1 = 0;
       for (int i = 0; i < 3; ++i) p.s0[i] = d.dq_stride[i];
       p.n_blocks = (int)(tpad / 128);
       const int64_t grid = (int64_t)p.n_blocks * d.heads_q * d.batch;
@@ -1399,8 +1412,13 @@ extern "C" int pdb_flash_bwd(const pdb_flash_bwd_desc* d, void* stream) {
   if (!d->o || !d->dout || !d->dq || !d->dk || !d->dv) return set_error(PDB_ERR_ARG, "null o / dout / dq / dk / dv");
   if (d->dtype != PDB_BF16)
     return set_error(PDB_ERR_UNSUPPORTED, "flash backward: bf16 only (dtype %d)", d->dtype);
-  if (d->head_dim != d->head_dim_v || (d->head_dim != 64 && d->head_dim != 128))
-    return set_error(PDB_ERR_UNSUPPORTED, "flash backward: head_dim == head_dim_v in {64, 128} required");
+  // both head dims 64: the fused pass; otherwise multiples of 8 in [64, 128] run the
+  // D = 128 passes with the tensor maps zero-filling the features up to 128
+  const bool fused = d->head_dim == 64 && d->head_dim_v == 64;
+  if (d->head_dim % 8 || d->head_dim_v % 8 || d->head_dim < 64 || d->head_dim_v < 64 || d->head_dim > 128 ||
+      d->head_dim_v > 128)
+    return set_error(PDB_ERR_UNSUPPORTED, "flash backward: head dims must be multiples of 8 in [64, 128] (got %lld, %lld)",
+                     (long long)d->head_dim, (long long)d->head_dim_v);
   if (d->seqlen_q > (1 << 30) || d->seqlen_k > (1 << 30)) return set_error(PDB_ERR_SHAPE, "sequence too long");
   const WsLayout w = ws_layout(*d);
   if (!d->workspace || d->workspace_bytes < w.total)
@@ -1442,7 +1460,7 @@ extern "C" int pdb_flash_bwd(const pdb_flash_bwd_desc* d, void* stream) {
     if (int st = flash_fwd_bf16_sm100(f, s)) return st;
     lse = f.lse;
   }
-  return d->head_dim == 64 ? launch_bwd<64>(*d, lse, w, s) : launch_bwd<128>(*d, lse, w, s);
+  return fused ? launch_bwd<64>(*d, lse, w, s) : launch_bwd<128>(*d, lse, w, s);
 }
 
 // ---------------------------------------------------------------------------

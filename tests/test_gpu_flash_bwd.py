@@ -69,6 +69,35 @@ def test_bwd_shapes_vs_oracle(cuda, B, H, HKV, T, D, causal):
     assert_bf16(_np(gv), rv, what="dv")
 
 
+@pytest.mark.parametrize("E,EV,causal", [(96, 96, True), (128, 64, True), (64, 128, False), (80, 112, True),
+                                          (72, 72, False)])
+def test_bwd_head_dims_vs_oracle(cuda, E, EV, causal):
+    """Head dims that are multiples of 8 in [64, 128], q.k and v widths apart: the
+    128-wide passes read zero-filled features past each dim and store only the
+    live columns."""
+    import torch
+
+    from pdum_dsl_b200 import kernels
+
+    B, H, HKV, T = 1, 4, 2, 200
+    g = torch.Generator(device="cpu").manual_seed(E * 131 + EV)
+    q = torch.randn(B, H, T, E, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, HKV, T, E, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, HKV, T, EV, generator=g).to(torch.bfloat16)
+    do = torch.randn(B, H, T, EV, generator=g).to(torch.bfloat16)
+    scale = 1 / math.sqrt(E)
+    o, lse = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), scale=scale, causal=causal,
+                                     return_lse=True)
+    gq, gk, gv = kernels.flash_attention_backward(q.to(cuda), k.to(cuda), v.to(cuda), o, do.to(cuda), lse,
+                                                  scale=scale, causal=causal)
+    kernels.check_device_errors()
+    assert gq.shape == q.shape and gk.shape == k.shape and gv.shape == v.shape
+    rq, rk, rv = OA.attention_bwd(*(x.double().numpy() for x in (q, k, v, do)), scale=scale, causal=causal)
+    assert_bf16(_np(gq), rq, what="dq")
+    assert_bf16(_np(gk), rk, what="dk")
+    assert_bf16(_np(gv), rv, what="dv")
+
+
 def test_bwd_config5_slices(cuda):
     """Config 5 (B4 H16 S2048 D64 causal): full-size launch, sampled heads vs the oracle."""
     import torch
