@@ -96,9 +96,9 @@ int pdb_layernorm_f32(const pdb_layernorm_desc* d, void* stream);
  * key_lo and its last row's key_hi; otherwise every key tile is visited and
  * the per-row bounds alone mask.
  * dtype PDB_BF16: bf16 q/k/v/o, fp32 accumulate, tcgen05/TMEM tensor cores
- * (head_dim, head_dim_v multiples of 8 in [64, 128], possibly different: the
+ * (head_dim, head_dim_v multiples of 8 up to 128, possibly different: the
  * kernels are built for 64 and 128 features and the tensor maps zero-fill the
- * columns in between).  dtype PDB_F32: f32 everything, ieee
+ * columns past each dim).  dtype PDB_F32: f32 everything, ieee
  * FMA path (any head_dim, head_dim_v <= 256), the precision of the reference's
  * f32 column (triton_tile.py:684-690 refuses tf32). */
 typedef struct {
@@ -134,7 +134,7 @@ int pdb_flash_fwd(const pdb_flash_desc* d, void* stream);
  * size in bytes comes from pdb_flash_bwd_workspace_size.  If lse is NULL the
  * kernel recomputes it (the "recompute" variant of the template); otherwise it
  * is the forward's stored lse ("stored" variant).  head_dim and head_dim_v
- * are multiples of 8 in [64, 128] and may differ.  head_dim == head_dim_v == 64
+ * are multiples of 8 up to 128 and may differ.  Both <= 64
  * runs one fused pass whose dQ sums per-key-block parts with fp32 reductions in
  * L2, so dq's last bits may differ run to run; every other shape runs the
  * 128-wide dK/dV and dQ passes, with tensor maps that zero-fill the features

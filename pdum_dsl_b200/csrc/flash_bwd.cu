@@ -1053,14 +1053,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   }
 }
 
-// dQ (bf16) = scale * the fp32 accumulator of the fused pass, rows t < T.
+// dQ (bf16) = scale * the fp32 accumulator of the fused pass, rows t < T, features < E.
 // Eight features per thread (two 16-byte loads, one 16-byte store).
 __global__ void bwd_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t s0,
-                                      int64_t s1, int64_t s2, int H, int T, int Tpad, float scale, int64_t n) {
+                                      int64_t s1, int64_t s2, int H, int T, int Tpad, int E, float scale,
+                                      int64_t n) {
   grid_dep_wait();  // the fused pass (and its bulk reductions) has completed
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int ch = (int)(i & 7);
+  if (ch * 8 >= E) return;  // features past the head dim are zero padding
   const int64_t r = i >> 3;
   const int t = (int)(r % T);
   const int64_t bh = r / T;
@@ -1200,7 +1202,7 @@ WsLayout ws_layout(const pdb_flash_bwd_desc& d) {
   off = align256(off + rows * 4);
   w.ctr = off;  // two work-unit counters
   off = align256(off + 8);
-  if (d.head_dim == 64 && d.head_dim_v == 64) {  // fp32 dQ accumulator of the fused pass, rows padded like lse2
+  if (d.head_dim <= 64 && d.head_dim_v <= 64) {  // fp32 dQ accumulator of the fused pass, rows padded like lse2
     w.dqacc = off;
     off = align256(off + rows * 64 * 4);
   }
@@ -1261,7 +1263,7 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       while (tpr < 32 && tpr * 8 < d.head_dim_v) tpr *= 2;
     }
     const int64_t threads = rows * tpr;
-    if (D == 64 && vec) {
+    if (D == 64 && vec && d.head_dim_v == 64) {
       int64_t blocks = (rows + 63) / 64;
       const int64_t resident = 8LL * sm_count(dev);
       if (blocks > resident) blocks = resident;
@@ -1331,15 +1333,16 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     if (e != cudaSuccess) return cuda_status(e, "bwd fused64 smem attribute");
     const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
     CUtensorMap tdk32, tdv32;  // dK / dV stores: 32-row boxes, one per drain warp
-    if (int st = map_bf16(&tdk32, d.dk, D, d.seqlen_k, d.heads_kv, d.batch, d.dk_stride, 32)) return st;
-    if (int st = map_bf16(&tdv32, d.dv, D, d.seqlen_k, d.heads_kv, d.batch, d.dv_stride, 32)) return st;
+    // the store maps carry the true dims: the TMA drops the zero columns past them
+    if (int st = map_bf16(&tdk32, d.dk, E, d.seqlen_k, d.heads_kv, d.batch, d.dk_stride, 32)) return st;
+    if (int st = map_bf16(&tdv32, d.dv, EV, d.seqlen_k, d.heads_kv, d.batch, d.dv_stride, 32)) return st;
     e = launch_overlapped(bwd_fused64_kernel, pgrid, kFusedThreads, smem, stream, tq128, tk128, tv128, tdo128, tdq,
                           tdk32, tdv32, p);
     if (e != cudaSuccess) return cuda_status(e, "bwd fused64 launch");
     const int64_t n = d.batch * d.heads_q * d.seqlen_q * 8;
     e = launch_overlapped(bwd_dq_convert_kernel, (n + 255) / 256, 256, 0, stream, (const float*)dqacc,
                           static_cast<__nv_bfloat16*>(d.dq), d.dq_stride[0], d.dq_stride[1], d.dq_stride[2],
-                          (int)d.heads_q, (int)d.seqlen_q, (int)tpad, (float)d.scale, n);
+                          (int)d.heads_q, (int)d.seqlen_q, (int)tpad, E, (float)d.scale, n);
     if (e != cudaSuccess) return cuda_status(e, "bwd dq convert launch");
     return PDB_OK;
   } else {
@@ -1412,12 +1415,11 @@ extern "C" int pdb_flash_bwd(const pdb_flash_bwd_desc* d, void* stream) {
   if (!d->o || !d->dout || !d->dq || !d->dk || !d->dv) return set_error(PDB_ERR_ARG, "null o / dout / dq / dk / dv");
   if (d->dtype != PDB_BF16)
     return set_error(PDB_ERR_UNSUPPORTED, "flash backward: bf16 only (dtype %d)", d->dtype);
-  // both head dims 64: the fused pass; otherwise multiples of 8 in [64, 128] run the
-  // D = 128 passes with the tensor maps zero-filling the features up to 128
-  const bool fused = d->head_dim == 64 && d->head_dim_v == 64;
-  if (d->head_dim % 8 || d->head_dim_v % 8 || d->head_dim < 64 || d->head_dim_v < 64 || d->head_dim > 128 ||
-      d->head_dim_v > 128)
-    return set_error(PDB_ERR_UNSUPPORTED, "flash backward: head dims must be multiples of 8 in [64, 128] (got %lld, %lld)",
+  // both head dims <= 64: the fused pass; otherwise (multiples of 8 up to 128) the
+  // D = 128 passes; the tensor maps zero-fill the features between each dim and D
+  const bool fused = d->head_dim <= 64 && d->head_dim_v <= 64;
+  if (d->head_dim % 8 || d->head_dim_v % 8 || d->head_dim > 128 || d->head_dim_v > 128)
+    return set_error(PDB_ERR_UNSUPPORTED, "flash backward: head dims must be multiples of 8 up to 128 (got %lld, %lld)",
                      (long long)d->head_dim, (long long)d->head_dim_v);
   if (d->seqlen_q > (1 << 30) || d->seqlen_k > (1 << 30)) return set_error(PDB_ERR_SHAPE, "sequence too long");
   const WsLayout w = ws_layout(*d);

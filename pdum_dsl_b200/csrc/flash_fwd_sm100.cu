@@ -876,13 +876,13 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
 
 int flash_fwd_bf16_sm100(const pdb_flash_desc& d, cudaStream_t stream) {
   // head dims up to 64 run the D = 64 kernel, up to 128 the D = 128 kernel (the
-  // tensor maps zero-fill the feature columns between the true head dim and D);
-  // rows of q / k / v / o must be 16-byte multiples (TMA), so both dims are
-  // multiples of 8, and at least 64 (the TMA box is 64 features wide)
+  // tensor maps zero-fill the feature columns between the true head dim and D,
+  // including the part of a 64-wide box past a dim below 64); rows of q / k / v /
+  // o must be 16-byte multiples (TMA), so both dims are multiples of 8
   const int64_t dmax = d.head_dim > d.head_dim_v ? d.head_dim : d.head_dim_v;
-  if (d.head_dim % 8 || d.head_dim_v % 8 || d.head_dim < 64 || d.head_dim_v < 64 || dmax > 128)
+  if (d.head_dim % 8 || d.head_dim_v % 8 || dmax > 128)
     return set_error(PDB_ERR_UNSUPPORTED,
-                     "bf16 flash: head dims must be multiples of 8 in [64, 128] (got %lld, %lld)",
+                     "bf16 flash: head dims must be multiples of 8 up to 128 (got %lld, %lld)",
                      (long long)d.head_dim, (long long)d.head_dim_v);
   if (d.seqlen_q > 0x7fffffffLL - 512 || d.seqlen_k > 0x7fffffffLL - 512 || d.q_start > 0x3fffffffLL)
     return set_error(PDB_ERR_SHAPE, "bf16 flash: sequence too long");

@@ -105,7 +105,7 @@ def compile_grad(rg, *, dtype: str = "bf16"):
 
     ``values``: numpy arrays positional per joint param (the forward's params,
     then the seed ``dO``), each in its param's type-dim order.  The backward
-    kernels are bf16 (fp32 accumulate), head dims multiples of 8 in [64, 128]."""
+    kernels are bf16 (fp32 accumulate), head dims multiples of 8 up to 128."""
     if dtype != "bf16":
         raise Untranslatable("the attention backward kernels are bf16")
     runner = _GradRunner(rg, dtype)

@@ -214,7 +214,7 @@ def test_bf16_config4_gqa_slices(cuda):
 
 
 @pytest.mark.parametrize("D,DV,causal", [(96, 96, True), (128, 64, True), (64, 128, False), (80, 112, True),
-                                         (72, 72, False)])
+                                         (72, 72, False), (32, 32, True), (16, 48, False), (56, 128, True)])
 def test_bf16_head_dims_between_the_builds(cuda, D, DV, causal):
     """Head dims other than 64 / 128 (and e != o) on the tensor-core kernels: the
     tensor maps zero-fill the features up to the kernel's 64 or 128."""

@@ -83,8 +83,9 @@ def test_compile_tile_checks_launch_and_dtype(dsl):
     assert run.grid == 2 and "flash_f32_kernel" in run.source
     with pytest.raises(Untranslatable, match="not an output dim"):
         compile_tile(f.naive, (("s", 32),))
+    assert "flash_fwd" in compile_tile(f.naive, dtype="bf16").source  # E=32: the 64-wide build, zero-filled
     with pytest.raises(Untranslatable, match="head dims"):
-        compile_tile(f.naive, dtype="bf16")  # E=32 has no tcgen05 build
+        compile_tile(flash_tile(T=128, E=20, OD=20, SI=2).naive, dtype="bf16")  # rows not 16-byte multiples
     assert compile_tile(attention_region(T=300, D=64, causal=True), dtype="bf16").grid == 2
 
 
