@@ -96,9 +96,9 @@ int pdb_layernorm_f32(const pdb_layernorm_desc* d, void* stream);
  * key_lo and its last row's key_hi; otherwise every key tile is visited and
  * the per-row bounds alone mask.
  * dtype PDB_BF16: bf16 q/k/v/o, fp32 accumulate, tcgen05/TMEM tensor cores
- * (head_dim, head_dim_v multiples of 8 up to 128, possibly different: the
- * kernels are built for 64 and 128 features and the tensor maps zero-fill the
- * columns past each dim).  dtype PDB_F32: f32 everything, ieee
+ * (head_dim, head_dim_v multiples of 8 up to 256, possibly different: the
+ * kernels are built for 64, 128 and 256 features and the tensor maps zero-fill
+ * the columns past each dim).  dtype PDB_F32: f32 everything, ieee
  * FMA path (any head_dim, head_dim_v <= 256), the precision of the reference's
  * f32 column (triton_tile.py:684-690 refuses tf32). */
 typedef struct {

@@ -872,23 +872,434 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Head dims up to 256 (e and e_v in (128, 256]): one 128-row query tile per
+// work tile.  TMEM: S0 [0,128) S1 [128,256) O [256,512) -- the O accumulator
+// takes 256 columns, so there is room for two score buffers but not for a
+// second query tile.  The score MMA of key tile j+1 is issued into the other
+// buffer before the PV of key tile j, so the softmax of tile j+1 finds its
+// scores ready when it finishes tile j; P (bf16) overwrites the first 64
+// columns of its own S buffer, and the score MMA of tile j+2 into that buffer
+// is issued after the PV that reads it (tcgen05 ops of one thread run in
+// order).  Shared memory: Q (128 x 256, 64 KB) and a ring of five 32 KB slots
+// (128 keys x 128 features each), through which K and V halves stream in the
+// order the MMAs consume them: K0, then per key tile j: K(j+1), V(j).
+//   warp 0        TMA producer        warp 1   MMA issuer (one thread)
+//   warp 2        TMEM allocator      warps 4..7  softmax + epilogue
+constexpr int kThreads256 = 256;
+constexpr int kSlots256 = 5;
+constexpr int kSlotBytes256 = 2 * kBoxBytes;  // 128 rows x 128 bf16
+constexpr int kQ256 = 0;
+constexpr int kRing256 = 4 * kBoxBytes;
+constexpr int kBar256 = kRing256 + kSlots256 * kSlotBytes256;
+constexpr int kSmem256 = kBar256 + 1024 + 1024;
+
+struct __align__(8) Barriers256 {
+  uint64_t q_full, q_empty;
+  uint64_t slot_full[kSlots256], slot_empty[kSlots256];
+  uint64_t s_full[2];  // score MMA into buffer b done -> softmax
+  uint64_t p_full[2];  // P in buffer b written -> PV (4 warp arrivals)
+  uint64_t pv_done;    // one completion per key tile's PV: O is quiescent up to it
+  uint64_t o_full, o_empty;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// 128-row work tiles: ordinal -> (b, h, row block), key tiles j0 .. j0 + n - 1.
+__device__ __forceinline__ TileInfo tile_info128(int tile, const FwdParams& p) {
+  TileInfo ti;
+  int bh, mblk;
+  if (p.lpt) {
+    const int nbh = p.H * p.B;
+    bh = tile % nbh;
+    mblk = p.num_mblocks - 1 - tile / nbh;
+  } else {
+    bh = tile / p.num_mblocks;
+    const int r = tile % p.num_mblocks;
+    mblk = (r & 1) ? (r >> 1) : p.num_mblocks - 1 - (r >> 1);
+  }
+  ti.b = bh / p.H;
+  ti.h = bh % p.H;
+  ti.hk = ti.h / (p.H / p.HKV);
+  ti.t0 = mblk * BM;
+  const int n_kv = (p.S + BN - 1) / BN;
+  const int first = ti.t0 < p.T ? ti.t0 : p.T - 1;
+  int last_row = ti.t0 + BM - 1;
+  if (last_row > p.T - 1) last_row = p.T - 1;
+  ti.j0 = 0;
+  if (p.key_lo && p.mask_monotone) ti.j0 = __ldg(p.key_lo + first) / BN;
+  int c = n_kv;
+  if (p.causal) c = (last_row + p.q_start) / BN + 1;
+  else if (p.key_lo && p.mask_monotone) c = (__ldg(p.key_hi + last_row) + BN - 1) / BN;
+  c = c < n_kv ? c : n_kv;
+  ti.nA = ti.nB = c - ti.j0 > 1 ? c - ti.j0 : 1;
+  return ti;
+}
+
+template <bool kKeyMask>
+__global__ void __launch_bounds__(kThreads256, 1)
+    flash_fwd_d256_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+  constexpr int D = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Barriers256* bar = reinterpret_cast<Barriers256*>(smem + kBar256);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = p.num_mblocks * p.H * p.B;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 1);
+    mbar_init(&bar->q_empty, 1);
+    for (int i = 0; i < kSlots256; ++i) {
+      mbar_init(&bar->slot_full[i], 1);
+      mbar_init(&bar->slot_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->s_full[i], 1);
+      mbar_init(&bar->p_full[i], BM / 32);
+    }
+    mbar_init(&bar->pv_done, 1);
+    mbar_init(&bar->o_full, 1);
+    mbar_init(&bar->o_empty, BM / 32);
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+  const uint32_t sQ = smem_u32(smem + kQ256), sRing = smem_u32(smem + kRing256);
+
+  if (warp < 4) {
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- producer
+      prefetch_tensormap(&tm_q);
+      prefetch_tensormap(&tm_k);
+      prefetch_tensormap(&tm_v);
+      uint32_t g = 0, tt = 0;  // slot loads issued, tiles started
+      // one 32 KB slot: 128 keys x features [128 h, 128 h + 128) of K or V
+      auto load_half = [&](const CUtensorMap* m, int h, int key0, int hk, int b) -> bool {
+        const uint32_t slot = g % kSlots256, ph = (g / kSlots256) & 1;
+        if (!mbar_wait(&bar->slot_empty[slot], ph ^ 1, abort, p.err)) return false;
+        mbar_expect_tx(&bar->slot_full[slot], kSlotBytes256);
+        uint8_t* dst = smem + kRing256 + slot * kSlotBytes256;
+        tma_load_4d(dst, m, &bar->slot_full[slot], h * 128, key0, hk, b);
+        tma_load_4d(dst + kBoxBytes, m, &bar->slot_full[slot], h * 128 + 64, key0, hk, b);
+        ++g;
+        return true;
+      };
+      bool ok = true;
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0;
+           tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
+        const TileInfo ti = tile_info128(tile, p);
+        if (!(ok = mbar_wait(&bar->q_empty, (tt & 1) ^ 1, abort, p.err))) break;
+        mbar_expect_tx(&bar->q_full, 4 * kBoxBytes);
+        for (int i = 0; i < 4; ++i)
+          tma_load_4d(smem + kQ256 + i * kBoxBytes, &tm_q, &bar->q_full, i * 64, ti.t0, ti.h, ti.b);
+        const int n = ti.nA;
+        ok = load_half(&tm_k, 0, ti.j0 * BN, ti.hk, ti.b) && load_half(&tm_k, 1, ti.j0 * BN, ti.hk, ti.b);
+        for (int j = 0; ok && j < n; ++j) {
+          const int key0 = (ti.j0 + j) * BN;
+          if (j + 1 < n)
+            ok = load_half(&tm_k, 0, key0 + BN, ti.hk, ti.b) && load_half(&tm_k, 1, key0 + BN, ti.hk, ti.b);
+          ok = ok && load_half(&tm_v, 0, key0, ti.hk, ti.b) && load_half(&tm_v, 1, key0, ti.hk, ti.b);
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      // -------------------------------------------------------- MMA issuer
+      const uint32_t tO = tmem + 256;
+      uint32_t g = 0, tt = 0, sc = 0;  // slots consumed, tiles, score tiles issued
+      constexpr uint32_t idesc_s = idesc_bf16(BM, BN, 0, 0);
+      constexpr uint32_t idesc_o = idesc_bf16(BM, 128, 0, 1);
+      auto take_slot = [&](uint32_t& saddr, uint32_t& slot) -> bool {
+        slot = g % kSlots256;
+        if (!mbar_wait(&bar->slot_full[slot], (g / kSlots256) & 1, abort, p.err)) return false;
+        tc_fence_after();
+        saddr = sRing + slot * kSlotBytes256;
+        ++g;
+        return true;
+      };
+      // S_b = Q K^T over 256 features (16 K16 steps, K in two slots)
+      auto qk = [&](uint32_t b) -> bool {
+        for (int h = 0; h < 2; ++h) {
+          uint32_t ks, slot;
+          if (!take_slot(ks, slot)) return false;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int kk = h * 8 + i;
+            const uint32_t qoff = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+            const uint32_t koff = (i >> 2) * kBoxBytes + (i & 3) * 32;
+            mma_ss(tmem + b * 128, sdesc_sw128(sQ + qoff, 16, 1024), sdesc_sw128(ks + koff, 16, 1024), idesc_s,
+                   kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&bar->slot_empty[slot]);
+        }
+        tc_commit(&bar->s_full[b]);
+        return true;
+      };
+      // O[:, 128 h .. 128 h + 128) += P_b V_h, P from TMEM (the first 64 columns of S_b)
+      auto pv = [&](uint32_t b, bool acc) -> bool {
+        for (int h = 0; h < 2; ++h) {
+          uint32_t vs, slot;
+          if (!take_slot(vs, slot)) return false;
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk)
+            mma_ts(tO + h * 128, tmem + b * 128 + kk * 8, sdesc_sw128(vs + kk * 2048, kBoxBytes, 1024), idesc_o,
+                   (acc || kk > 0) ? 1u : 0u);
+          tc_commit(&bar->slot_empty[slot]);
+        }
+        tc_commit(&bar->pv_done);
+        return true;
+      };
+      bool ok = true;
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0;
+           tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
+        const TileInfo ti = tile_info128(tile, p);
+        const int n = ti.nA;
+        if (!(ok = mbar_wait(&bar->q_full, tt & 1, abort, p.err))) break;
+        if (!(ok = qk(sc & 1))) break;
+        if (n == 1) tc_commit(&bar->q_empty);
+        for (int j = 0; ok && j < n; ++j) {
+          const uint32_t s = sc + j;
+          if (j + 1 < n) {
+            if (!(ok = qk((s + 1) & 1))) break;
+            if (j + 2 == n) tc_commit(&bar->q_empty);  // every score MMA of this tile has been issued
+          }
+          if (!(ok = mbar_wait(&bar->p_full[s & 1], (s >> 1) & 1, abort, p.err))) break;
+          if (j == 0 && !(ok = mbar_wait(&bar->o_empty, (tt & 1) ^ 1, abort, p.err))) break;
+          tc_fence_after();
+          if (!(ok = pv(s & 1, j > 0))) break;
+        }
+        if (!ok) break;
+        tc_commit(&bar->o_full);
+        sc += n;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tO = tmem + lane_off + 256;
+    const float c = p.scale_log2;
+    uint32_t gs = 0, tt = 0;  // score tiles read, work tiles
+    bool ok = true;
+    for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0;
+         tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
+      const TileInfo ti = tile_info128(tile, p);
+      const int t = ti.t0 + row;
+      const int n = ti.nA;
+      int row_lo = 0, row_hi = p.S;
+      if constexpr (kKeyMask) {
+        const int tc = t < p.T ? t : p.T - 1;
+        row_lo = __ldg(p.key_lo + tc);
+        row_hi = __ldg(p.key_hi + tc);
+      }
+      float m_used = -INFINITY, m_true = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j, ++gs) {
+        const uint32_t b = gs & 1;
+        const uint32_t tS = tmem + lane_off + b * 128;
+        if (!(ok = mbar_wait(&bar->s_full[b], (gs >> 1) & 1, abort, p.err))) break;
+        tc_fence_after();
+        const int kb = (ti.j0 + j) * BN;
+        int lim = p.S - kb;
+        if (p.causal) {
+          const int lc = t + p.q_start + 1 - kb;
+          lim = lc < lim ? lc : lim;
+        }
+        int lo_rel = 0;
+        if constexpr (kKeyMask) {
+          lo_rel = row_lo - kb;
+          lim = row_hi - kb < lim ? row_hi - kb : lim;
+        }
+        const bool need_mask = __any_sync(0xffffffffu, lim < BN || lo_rel > 0);
+        uint32_t sr[BN];
+        float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
+        tmem_wait_ld();
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          if (hf == 0) {
+#pragma unroll
+            for (int ch = 2; ch < 4; ++ch)
+              tmem_ld32(tS + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + ch * 32));
+          } else {
+            tmem_wait_ld();
+            regs_after_wait<BN / 2>(sr + BN / 2);
+          }
+          uint32_t* hv = sr + hf * (BN / 2);
+          if (need_mask) {
+#pragma unroll
+            for (int i = 0; i < BN / 2; ++i)
+              if (hf * (BN / 2) + i >= lim || hf * (BN / 2) + i < lo_rel) hv[i] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int i = 0; i < BN / 2; i += 8) {
+            mxa = max3(mxa, __uint_as_float(hv[i]), __uint_as_float(hv[i + 1]));
+            mxb = max3(mxb, __uint_as_float(hv[i + 2]), __uint_as_float(hv[i + 3]));
+            mxc = max3(mxc, __uint_as_float(hv[i + 4]), __uint_as_float(hv[i + 5]));
+            mxd = max3(mxd, __uint_as_float(hv[i + 6]), __uint_as_float(hv[i + 7]));
+          }
+        }
+        const float mt = fmaxf(max3(mxa, mxb, mxc), mxd) * c;
+        m_true = fmaxf(m_true, mt);
+        if (j == 0) {
+          m_used = mt;
+        } else if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
+          const float m_new = fmaxf(m_used, mt);
+          const float alpha = m_used == -INFINITY ? 0.f : ex2(m_used - m_new);
+          m_used = m_new;
+          l *= alpha;
+          // O holds the PVs up to key tile j - 1 once that PV has completed
+          if (!(ok = mbar_wait(&bar->pv_done, (gs - 1) & 1, abort, p.err))) break;
+          tc_fence_after();
+          uint32_t r[32];
+#pragma unroll 1
+          for (int ch = 0; ch < D / 32; ++ch) {
+            tmem_ld32(tO + ch * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tO + ch * 32, r);
+          }
+        }
+        const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+        const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(neg_m, neg_m);
+        uint64_t sum_a = 0, sum_b = 0;
+#pragma unroll
+        for (int ch = 0; ch < BN / 32; ++ch) {
+          uint32_t pk[16];
+          exp_chunk(sr + ch * 32, c2, nm2, sum_a, sum_b, pk);
+          tmem_st16(tS + ch * 16, pk);
+        }
+        float sa0, sa1, sb0, sb1;
+        f2_unpack(sum_a, sa0, sa1);
+        f2_unpack(sum_b, sb0, sb1);
+        l += (sa0 + sa1) + (sb0 + sb1);
+        tmem_wait_st();
+        warp_arrive_after_tc(&bar->p_full[b]);
+      }
+      if (!ok || !(ok = mbar_wait(&bar->o_full, tt & 1, abort, p.err))) break;
+      tc_fence_after();
+      const float inv_l = 1.0f / l;
+      const bool store = t < p.T;
+      const int64_t bhq = (int64_t)ti.b * p.H + ti.h;
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.o) + (int64_t)ti.b * p.o_stride[0] +
+                            (int64_t)ti.h * p.o_stride[1] + (int64_t)t * p.o_stride[2];
+#pragma unroll 1
+      for (int ch = 0; ch < D / 32; ++ch) {
+        if (ch * 32 >= p.DV) break;  // columns past the value head dim are zero padding
+        uint32_t r[32];
+        tmem_ld32(tO + ch * 32, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pk[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
+        if (store) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (ch * 32 + i * 8 < p.DV) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+      warp_arrive_after_tc(&bar->o_empty);
+      if (store) {
+        const int64_t idx = bhq * p.T + t;
+        constexpr float kLn2 = 0.6931471805599453f;
+        if (p.lse) p.lse[idx] = (m_used + __log2f(l)) * kLn2;
+        if (p.m) p.m[idx] = m_true * kLn2;
+        if (p.den) p.den[idx] = l * ex2(m_used - m_true);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+int launch256(const pdb_flash_desc& d, cudaStream_t stream) {
+  CUtensorMap tq, tk, tv;
+  const uint32_t box[4] = {64, 128, 1, 1};
+  {  // the maps carry the true head dims; features up to 256 are zero-filled
+    const uint64_t dims[4] = {(uint64_t)d.head_dim, (uint64_t)d.seqlen_q, (uint64_t)d.heads_q, (uint64_t)d.batch};
+    const uint64_t str[3] = {(uint64_t)d.q_stride[2] * 2, (uint64_t)d.q_stride[1] * 2, (uint64_t)d.q_stride[0] * 2};
+    if (int st = encode_tma_4d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+    const uint64_t dk[4] = {(uint64_t)d.head_dim, (uint64_t)d.seqlen_k, (uint64_t)d.heads_kv, (uint64_t)d.batch};
+    const uint64_t dv[4] = {(uint64_t)d.head_dim_v, (uint64_t)d.seqlen_k, (uint64_t)d.heads_kv, (uint64_t)d.batch};
+    const uint64_t sk[3] = {(uint64_t)d.k_stride[2] * 2, (uint64_t)d.k_stride[1] * 2, (uint64_t)d.k_stride[0] * 2};
+    const uint64_t sv[3] = {(uint64_t)d.v_stride[2] * 2, (uint64_t)d.v_stride[1] * 2, (uint64_t)d.v_stride[0] * 2};
+    if (int st = encode_tma_4d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.k, dk, sk, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+    if (int st = encode_tma_4d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.v, dv, sv, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+  }
+  FwdParams p;
+  p.o = d.o;
+  p.lse = d.lse;
+  p.m = d.m;
+  p.den = d.den;
+  for (int i = 0; i < 3; ++i) p.o_stride[i] = d.o_stride[i];
+  p.T = (int)d.seqlen_q;
+  p.S = (int)d.seqlen_k;
+  p.DV = (int)d.head_dim_v;
+  p.H = (int)d.heads_q;
+  p.HKV = (int)d.heads_kv;
+  p.B = (int)d.batch;
+  p.q_start = (int)d.q_start;
+  p.causal = d.causal ? 1 : 0;
+  p.key_lo = d.key_lo;
+  p.key_hi = d.key_hi;
+  p.mask_monotone = d.mask_monotone ? 1 : 0;
+  p.num_mblocks = (int)((d.seqlen_q + BM - 1) / BM);
+  p.scale_log2 = (float)(d.scale * 1.4426950408889634);
+  p.err = device_error_flag();
+  const int64_t ntile = (int64_t)p.num_mblocks * d.heads_q * d.batch;
+  if (ntile > 0x7fffffffLL) return set_error(PDB_ERR_SHAPE, "bf16 flash: grid too large");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int sms = sm_count(dev) - (d.sm_margin > 0 ? d.sm_margin : 0);
+  if (sms < 1) sms = 1;
+  // fewer than 4 waves of tile pairs: single tiles heaviest first (else head-major pairs)
+  p.lpt = (ntile + 1) / 2 < 4 * (int64_t)sms ? 1 : 0;
+  const int64_t units = p.lpt ? ntile : (ntile + 1) / 2;
+  const int64_t grid = units < sms ? units : sms;
+  auto kern = p.key_lo ? flash_fwd_d256_kernel<true> : flash_fwd_d256_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem256);
+  if (e != cudaSuccess) return cuda_status(e, "bf16 flash d256: set smem attribute");
+  kern<<<(unsigned)grid, kThreads256, kSmem256, stream>>>(tq, tk, tv, p);
+  return cuda_status(cudaGetLastError(), "bf16 flash d256 launch");
+}
+
 }  // namespace
 
 int flash_fwd_bf16_sm100(const pdb_flash_desc& d, cudaStream_t stream) {
-  // head dims up to 64 run the D = 64 kernel, up to 128 the D = 128 kernel (the
+  // head dims up to 64 run the D = 64 kernel, up to 128 the D = 128 kernel, up to
+  // 256 the single-query-tile D = 256 kernel (the
   // tensor maps zero-fill the feature columns between the true head dim and D,
   // including the part of a 64-wide box past a dim below 64); rows of q / k / v /
   // o must be 16-byte multiples (TMA), so both dims are multiples of 8
   const int64_t dmax = d.head_dim > d.head_dim_v ? d.head_dim : d.head_dim_v;
-  if (d.head_dim % 8 || d.head_dim_v % 8 || dmax > 128)
+  if (d.head_dim % 8 || d.head_dim_v % 8 || dmax > 256)
     return set_error(PDB_ERR_UNSUPPORTED,
-                     "bf16 flash: head dims must be multiples of 8 up to 128 (got %lld, %lld)",
+                     "bf16 flash: head dims must be multiples of 8 up to 256 (got %lld, %lld)",
                      (long long)d.head_dim, (long long)d.head_dim_v);
   if (d.seqlen_q > 0x7fffffffLL - 512 || d.seqlen_k > 0x7fffffffLL - 512 || d.q_start > 0x3fffffffLL)
     return set_error(PDB_ERR_SHAPE, "bf16 flash: sequence too long");
   if ((reinterpret_cast<uintptr_t>(d.o) & 15u) || (d.o_stride[0] & 7) || (d.o_stride[1] & 7) || (d.o_stride[2] & 7))
     return set_error(PDB_ERR_ALIGN, "bf16 flash: o must be 16-byte aligned with strides multiple of 8 elements");
-  return dmax <= 64 ? launch<64>(d, stream) : launch<128>(d, stream);
+  return dmax <= 64 ? launch<64>(d, stream) : dmax <= 128 ? launch<128>(d, stream) : launch256(d, stream);
 }
 
 }  // namespace pdb

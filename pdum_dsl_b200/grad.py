@@ -41,6 +41,10 @@ class _GradRunner:
         if self.spec.mask is not None:
             raise Untranslatable("the fused backward takes causal or unmasked attention; a general mask's "
                                  "joint runs carve by carve (plan_model + execute_model_plan)")
+        for i, d in ((self.spec.q, self.spec.e), (self.spec.v, self.spec.o)):
+            x = next(t.stop - t.start for t in region.params[i].type.dims if t.name == d)
+            if x % 8 or x > 128:
+                raise Untranslatable(f"the bf16 backward takes head dims that are multiples of 8 up to 128, got {x}")
         self.n_params = len(region.params)
         self.do_index = self.n_params - 1  # the seed is passed last (RegionGrad docstring)
         pnames = {rg.names[id(p)]: i for i, p in enumerate(region.params) if id(p) in rg.names}

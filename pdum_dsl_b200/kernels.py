@@ -97,7 +97,7 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale:
 
     q (B, Hq, T, D), k/v (B, Hkv, S, D|Dv) with Hq a multiple of Hkv (GQA);
     2-D and 3-D inputs drop the leading dims.  bf16 runs the tcgen05 kernel
-    (D, Dv multiples of 8 up to 128); f32 runs the IEEE CUDA-core kernel (any D, Dv <= 256).  Returns o, or
+    (D, Dv multiples of 8 up to 256); f32 runs the IEEE CUDA-core kernel (any D, Dv <= 256).  Returns o, or
     (o, lse) / (o, m, den) with the per-row float32 statistics.
     ``key_intervals`` (a ``recognize.KeyIntervals`` of T rows) is a general
     closed mask: row t sees keys lo[t] <= s < hi[t] (``causal`` must be False).

@@ -364,9 +364,9 @@ def compile_tile(region, launch: tuple = (), prune: tuple = (), *, dtype: str = 
     if isinstance(spec, AttentionSpec) and dtype == "bf16":
         D = _extent(region, spec.q, spec.e)
         DV = _extent(region, spec.v, spec.o)
-        if any(x % 8 or x > 128 for x in (D, DV)):
-            raise Untranslatable(f"bf16 flash needs head dims that are multiples of 8 up to 128, got {D}, {DV} "
-                                 "(the f32 column takes any head dims up to 256)")
+        if any(x % 8 or x > 256 for x in (D, DV)):
+            raise Untranslatable(f"bf16 flash needs head dims that are multiples of 8 up to 256, got {D}, {DV} "
+                                 "(rows of 16-byte multiples for the tensor maps)")
     if isinstance(spec, AttentionSpec) and (_extent(region, spec.q, spec.e) > 256 or
                                             _extent(region, spec.v, spec.o) > 256):
         raise Untranslatable("flash head dims above 256 are not built")

@@ -86,7 +86,7 @@ def test_shape_validation_happens_before_any_launch():
     assert lib.pdb_flash_fwd(C.byref(f), None) == _lib.PDB_ERR_SHAPE
     f.q_start, f.dtype, f.head_dim, f.head_dim_v = 0, _lib.PDB_BF16, 44, 48  # rows not 16-byte multiples
     assert lib.pdb_flash_fwd(C.byref(f), None) == _lib.PDB_ERR_UNSUPPORTED
-    f.head_dim = 136  # above the 128-wide build
+    f.head_dim = 264  # above the 256-wide build
     assert lib.pdb_flash_fwd(C.byref(f), None) == _lib.PDB_ERR_UNSUPPORTED
     f.dtype = 7
     assert lib.pdb_flash_fwd(C.byref(f), None) == _lib.PDB_ERR_UNSUPPORTED

@@ -77,7 +77,8 @@ def test_bf16_flash_matches_reference(cuda, case):
 @pytest.mark.parametrize("B,H,HKV,T,S,D,causal", [
     (1, 1, 1, 128, 128, 64, True), (1, 1, 1, 256, 256, 128, True), (2, 3, 3, 300, 300, 64, True),
     (1, 4, 1, 513, 513, 128, True), (1, 2, 2, 64, 1000, 128, False), (1, 1, 1, 1, 1, 64, False),
-    (1, 2, 2, 1, 77, 64, True), (3, 2, 1, 257, 129, 64, False)])
+    (1, 2, 2, 1, 77, 64, True), (3, 2, 1, 257, 129, 64, False), (1, 2, 1, 300, 300, 256, True),
+    (2, 2, 2, 129, 1000, 256, False), (1, 1, 1, 1, 1, 256, False), (1, 3, 3, 700, 700, 256, True)])
 def test_bf16_shapes_vs_oracle(cuda, B, H, HKV, T, S, D, causal):
     import torch
 
@@ -96,18 +97,20 @@ def test_bf16_shapes_vs_oracle(cuda, B, H, HKV, T, S, D, causal):
     np.testing.assert_allclose(_np(lse), rlse, atol=2e-3, rtol=1e-4)
 
 
-def test_bf16_large_scores_rescale(cuda):
-    """Wide scores (x8, the reference's adversarial family) and a dominant key row (x40)."""
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_bf16_large_scores_rescale(cuda, D):
+    """Wide scores (x8, the reference's adversarial family) and a dominant key row (x40):
+    the running max jumps mid-row, so the O accumulator is rescaled."""
     import torch
 
     from pdum_dsl_b200 import kernels
 
     g = torch.Generator(device="cpu").manual_seed(11)
-    q = (8 * torch.randn(1, 2, 512, 64, generator=g)).to(torch.bfloat16)
-    k = torch.randn(1, 2, 512, 64, generator=g)
+    q = (8 * torch.randn(1, 2, 512, D, generator=g) * math.sqrt(64 / D)).to(torch.bfloat16)
+    k = torch.randn(1, 2, 512, D, generator=g)
     k[:, :, 300] *= 40
     k = k.to(torch.bfloat16)
-    v = torch.randn(1, 2, 512, 64, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, 2, 512, D, generator=g).to(torch.bfloat16)
     for causal in (True, False):
         o = kernels.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), scale=0.125, causal=causal)
         ro, *_ = OA.attention_fwd(q.double().numpy(), k.double().numpy(), v.double().numpy(), scale=0.125,
@@ -214,10 +217,12 @@ def test_bf16_config4_gqa_slices(cuda):
 
 
 @pytest.mark.parametrize("D,DV,causal", [(96, 96, True), (128, 64, True), (64, 128, False), (80, 112, True),
-                                         (72, 72, False), (32, 32, True), (16, 48, False), (56, 128, True)])
+                                         (72, 72, False), (32, 32, True), (16, 48, False), (56, 128, True),
+                                         (256, 256, True), (192, 256, False), (136, 200, True), (256, 64, True),
+                                         (64, 256, False)])
 def test_bf16_head_dims_between_the_builds(cuda, D, DV, causal):
-    """Head dims other than 64 / 128 (and e != o) on the tensor-core kernels: the
-    tensor maps zero-fill the features up to the kernel's 64 or 128."""
+    """Head dims other than 64 / 128 / 256 (and e != o) on the tensor-core kernels: the
+    tensor maps zero-fill the features up to the kernel's 64, 128 or 256."""
     import torch
 
     from pdum_dsl_b200 import kernels

@@ -38,7 +38,7 @@ def test_masked_flash_matches_run_region(cuda, dsl, case):
     (assert_bf16 if dtype == "bf16" else assert_f32)(got, want, what=case)
 
 
-@pytest.mark.parametrize("dtype,D", [("f32", 64), ("bf16", 64), ("bf16", 128)])
+@pytest.mark.parametrize("dtype,D", [("f32", 64), ("bf16", 64), ("bf16", 128), ("bf16", 256)])
 def test_sliding_window_long_rows_vs_oracle(cuda, dsl, dtype, D):
     """A longer sliding window (S=2000, W=300, two heads): the kernels visit only each
     block's live key tiles, and the rows of a block whose window starts past the block's
