@@ -147,6 +147,7 @@ CASES = {
     "fwd_b2": lambda: case_fwd(2, 32, 4096, 128),
     "fwd_d64": lambda: case_fwd(8, 32, 4096, 64),
     "fwd_d64_b4": lambda: case_fwd(4, 32, 4096, 64),
+    "fwd_d256": lambda: case_fwd(2, 16, 4096, 256),
     "bwd_config5": lambda: case_bwd(4, 16, 2048, 64),
     "bwd_d128": lambda: case_bwd(4, 16, 2048, 128),
     "f32_flash_config1": case_f32_flash,
