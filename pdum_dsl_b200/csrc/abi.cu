@@ -100,6 +100,8 @@ extern "C" int pdb_check_error(void* stream) {
   if (h != 0) {
     int z = 0;
     cudaMemcpy(flag, &z, sizeof(int), cudaMemcpyHostToDevice);
+    if ((h & pdb::kErrTimeout) == 0)
+      return pdb::set_error(PDB_ERR_CUDA, "a kernel refused its shared-memory window (flag 0x%x)", h);
     return pdb::set_error(PDB_ERR_TIMEOUT, "a bounded device wait expired (flag 0x%x)", h);
   }
   return PDB_OK;

@@ -24,6 +24,7 @@ int* device_error_flag();
 // %globaltimer (ns).  Kernels here finish in milliseconds; 2 s means a bug.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 constexpr int kErrTimeout = 1;
+constexpr int kErrSmemWindow = 2;  // a kernel found its dynamic shared memory too badly aligned to lay out its tiles
 
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;

@@ -27,6 +27,7 @@
 // D = 128 passes use no atomics (bit-reproducible); the fused pass's dQ sums
 // its per-key-block parts in whatever order the reductions land.
 #include <cfloat>
+#include <cstdlib>
 #include <mutex>
 #include <utility>
 
@@ -605,6 +606,593 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       // each warpgroup writes half of the dQ columns
       store_cols_bf16<D / 2>(tmem + lane_off + 256 + x * (D / 2), p.scale, dq + x * (D / 2), t < p.T,
+                             p.ncols0 - x * (D / 2));
+      warp_arrive_after_tc(&bar->acc_free);
+      gi += n_kv;
+      ++nqd;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+  grid_dep_wait();  // complete only after the dK/dV grid this one overlapped has completed
+}
+
+// dK / dV with 128-query items.  Unit = 128 keys of one (batch, KV head);
+// items = (query head of the group, 128-row query tile), so the score MMAs
+// run at N = 128.  TMEM: two 128-column slots take turns -- S^T of item g in
+// slot g & 1, dP^T of item g in the other -- and dV [256, 384), dK [384, 512).
+// The compute warpgroups split an item's queries (warpgroup x: queries
+// [64x, 64x+64)).  Phase 1 forms P^T = exp2(S^T c + nlse2) and writes it
+// (bf16 pairs) into its own first 32 columns of the S^T slot, the A operand of
+// dV += P^T dO; phase 2 reads dP^T, whose slot is then free for S^T of the
+// next item, and writes dS^T = P^T (dP^T - D) to shared memory (K-major,
+// 128-byte swizzle), the A operand of dK += dS^T Q.  Per item the MMA issuer
+// sends
+//   S^T(g+1) [once dP^T(g) is in registers], dK(g) [after dS^T(g)],
+//   dV(g) [after P^T(g)], dP^T(g+1) [into the slot dV(g) read, behind it]
+// so the next item's scores are formed while this item's gradients are.
+// Q / dO (and the per-query nlse2 / D) pass through two stages each; Q is
+// released by dK, dO by dV.
+struct __align__(8) BarsK {
+  uint64_t fixed_full, fixed_empty;  // K / V of the unit
+  uint64_t q_full[2], q_empty[2];    // Q + nlse2 / D of an item
+  uint64_t do_full[2], do_empty[2];
+  uint64_t st_full[2], dpt_full[2];  // S^T(g), dP^T(g) complete
+  uint64_t dp_free[2];               // dP^T(g) in registers (its slot may take S^T(g+1))
+  uint64_t pt_full[2];               // P^T(g) written to TMEM
+  uint64_t ds_full[2];               // dS^T(g) written to shared memory
+  uint64_t ds_free;                  // dK(g) complete: the dS^T buffer may be rewritten
+  uint64_t o_full, acc_free;
+  UnitQueue uq;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr int kKv128Tiles = 32768 * 7;                    // K, V, Q x 2, dO x 2, dS^T
+constexpr int kKv128Smem = kKv128Tiles + 2 * 256 * 4 + (int)sizeof(BarsK);  // + nlse2 / D per stage + barriers
+constexpr int kMaxDynSmem = 227 * 1024;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dkdv128_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                       const BwdParams p) {
+  constexpr int D = 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // the tiles need 1024-byte alignment and the launch has little slack above the layout:
+  // refuse (error word, no access) rather than overrun if the window starts badly aligned
+  if ((smem - smem_raw) + kKv128Smem > kMaxDynSmem) {
+    if (threadIdx.x == 0 && p.err) atomicOr(p.err, kErrSmemWindow);
+    return;
+  }
+  constexpr int kT = 128 * D * 2;
+  constexpr uint32_t kBox = 128 * 128;
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + kT;
+  uint8_t* sQ = smem + 2 * kT;   // 2 stages
+  uint8_t* sDO = smem + 4 * kT;  // 2 stages
+  uint8_t* sDS = smem + 6 * kT;
+  float* sVec = reinterpret_cast<float*>(smem + kKv128Tiles);  // per stage: nlse2[128], dsum[128]
+  BarsK* bar = reinterpret_cast<BarsK*>(smem + kKv128Tiles + 2 * 256 * 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = p.H / p.HKV;
+  const int n_qt = p.Tpad / 128;
+  const int n_bh = p.B * p.HKV;
+  const int n_units = p.n_blocks * n_bh;
+  auto unit_info = [&](int u, int& b, int& hk, int& s0, int& qt0, int& per_head) {
+    const int nblk = u / n_bh, bhk = u % n_bh;  // ascending key block = descending work (causal)
+    b = bhk / p.HKV;
+    hk = bhk % p.HKV;
+    s0 = nblk * 128;
+    qt0 = 0;
+    if (p.causal) {
+      const int first = s0 - p.q_start;  // first query row that can see key s0
+      qt0 = first > 0 ? first / 128 : 0;
+    }
+    per_head = n_qt - qt0 > 0 ? n_qt - qt0 : 0;
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->fixed_full, 1);
+    mbar_init(&bar->fixed_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->q_full[i], 1);
+      mbar_init(&bar->q_empty[i], 1);
+      mbar_init(&bar->do_full[i], 1);
+      mbar_init(&bar->do_empty[i], 1);
+      mbar_init(&bar->st_full[i], 1);
+      mbar_init(&bar->dpt_full[i], 1);
+      mbar_init(&bar->dp_free[i], 8);  // one arrival per compute warp
+      mbar_init(&bar->pt_full[i], 8);
+      mbar_init(&bar->ds_full[i], 8);
+      mbar_init(&bar->uq.full[i], 1);
+      mbar_init(&bar->uq.empty[i], 9);  // the MMA thread + 8 compute warps
+    }
+    mbar_init(&bar->ds_free, 1);
+    mbar_init(&bar->o_full, 1);
+    mbar_init(&bar->acc_free, 8);
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  grid_dep_wait();    // the prologue (D, nlse2, zeroed counters) has completed
+  grid_dep_launch();  // the dQ grid may take SMs as this grid's CTAs retire
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+  constexpr int kNB = D / 64;
+  constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);  // S^T, dP^T: M = 128 keys, N = 128 queries
+  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);    // dV, dK: M = 128 keys, N = D, B MN-major
+  constexpr uint32_t kDV = 256, kDK = 384;
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- producer
+      uint32_t gi = 0, nu = 0, nkv = 0;
+      for (;; ++nu) {
+        int u = atomicAdd(p.ctr, 1);
+        if (u >= n_units) u = -1;
+        if (fetch_unit(&bar->uq, nu, u, abort, p.err) < 0) break;
+        int b, hk, s0, qt0, per_head;
+        unit_info(u, b, hk, s0, qt0, per_head);
+        const int n_items = per_head * group;
+        if (n_items == 0) continue;
+        if (!mbar_wait(&bar->fixed_empty, (nkv & 1) ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->fixed_full, 2 * kT);
+        for (int i = 0; i < kNB; ++i) {
+          tma_load_4d(sK + i * kBox, &tm_k, &bar->fixed_full, i * 64, s0, hk, b);
+          tma_load_4d(sV + i * kBox, &tm_v, &bar->fixed_full, i * 64, s0, hk, b);
+        }
+        ++nkv;
+        bool ok = true;
+        for (int it = 0; it < n_items; ++it, ++gi) {
+          const int st = gi & 1;
+          const uint32_t ph = ((gi >> 1) & 1) ^ 1;
+          const int h = hk * group + it / per_head;
+          const int t0 = (qt0 + it % per_head) * 128;
+          if (!(ok = mbar_wait(&bar->q_empty[st], ph, abort, p.err))) break;
+          mbar_expect_tx(&bar->q_full[st], kT + 2 * 128 * 4);
+          for (int i = 0; i < kNB; ++i)
+            tma_load_4d(sQ + st * kT + i * kBox, &tm_q, &bar->q_full[st], i * 64, t0, h, b);
+          const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
+          bulk_load(sVec + st * 256, p.nlse2 + vrow, 128 * 4, &bar->q_full[st]);
+          bulk_load(sVec + st * 256 + 128, p.dsum + vrow, 128 * 4, &bar->q_full[st]);
+          if (!(ok = mbar_wait(&bar->do_empty[st], ph, abort, p.err))) break;
+          mbar_expect_tx(&bar->do_full[st], kT);
+          for (int i = 0; i < kNB; ++i)
+            tma_load_4d(sDO + st * kT + i * kBox, &tm_do, &bar->do_full[st], i * 64, t0, h, b);
+        }
+        if (!ok) break;
+      }
+    } else if (warp == 1 && lane == 0) {
+      // -------------------------------------------------------- MMA issuer
+      uint32_t gi = 0, nu = 0, nkv = 0;
+      bool ok = true;
+      for (;; ++nu) {
+        const int u = take_unit(&bar->uq, nu, abort, p.err, false);
+        if (u < 0) break;
+        int b, hk, s0, qt0, per_head;
+        unit_info(u, b, hk, s0, qt0, per_head);
+        const int n_items = per_head * group;
+        if (n_items == 0) continue;
+        auto issue_st = [&](int it) -> bool {  // S^T(g) into slot g & 1, once dP^T(g-1) left it
+          const uint32_t g = gi + it;
+          if (!mbar_wait(&bar->q_full[g & 1], (g >> 1) & 1, abort, p.err)) return false;
+          if (g > 0 && !mbar_wait(&bar->dp_free[(g - 1) & 1], ((g - 1) >> 1) & 1, abort, p.err)) return false;
+          tc_fence_after();
+          mma_kmajor<D>(tmem + (g & 1) * 128, smem_u32(sK), kBox, smem_u32(sQ + (g & 1) * kT), kBox, idS);
+          tc_commit(&bar->st_full[g & 1]);
+          return true;
+        };
+        auto issue_dpt = [&](int it) -> bool {  // dP^T(g) into slot (g + 1) & 1
+          const uint32_t g = gi + it;
+          if (!mbar_wait(&bar->do_full[g & 1], (g >> 1) & 1, abort, p.err)) return false;
+          tc_fence_after();
+          mma_kmajor<D>(tmem + ((g + 1) & 1) * 128, smem_u32(sV), kBox, smem_u32(sDO + (g & 1) * kT), kBox, idS);
+          tc_commit(&bar->dpt_full[g & 1]);
+          if (it == n_items - 1) tc_commit(&bar->fixed_empty);  // K/V no longer needed: load the next unit's
+          return true;
+        };
+        if (!(ok = mbar_wait(&bar->fixed_full, nkv & 1, abort, p.err))) break;
+        ok = issue_st(0) && issue_dpt(0);
+        for (int it = 0; ok && it < n_items; ++it) {
+          const uint32_t g = gi + it;
+          const int st = g & 1;
+          if (it + 1 < n_items && !(ok = issue_st(it + 1))) break;
+          if (!(ok = mbar_wait(&bar->ds_full[st], (g >> 1) & 1, abort, p.err))) break;
+          if (it == 0 && nkv > 0 && !(ok = mbar_wait(&bar->acc_free, (nkv - 1) & 1, abort, p.err))) break;
+          tc_fence_after();
+          const uint32_t bq = smem_u32(sQ + st * kT), bdo = smem_u32(sDO + st * kT), ads = smem_u32(sDS);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
+            mma_ss(tmem + kDK, sdesc_sw128(ads + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024),
+                   sdesc_sw128(bq + kk * 2048, kBox, 1024), idG, (it > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&bar->q_empty[st]);
+          tc_commit(&bar->ds_free);
+          if (!(ok = mbar_wait(&bar->pt_full[st], (g >> 1) & 1, abort, p.err))) break;
+          tc_fence_after();
+          const uint32_t a = tmem + st * 128;  // P^T of queries [0, 64) in columns [0, 32), [64, 128) in [64, 96)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO
+            mma_ts(tmem + kDV, a + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_sw128(bdo + kk * 2048, kBox, 1024), idG,
+                   (it > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&bar->do_empty[st]);
+          if (it + 1 < n_items && !(ok = issue_dpt(it + 1))) break;
+        }
+        if (!ok) break;
+        tc_commit(&bar->o_full);
+        gi += n_items;
+        ++nkv;
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
+    const int x = warp >= 8 ? 1 : 0;  // queries [64x, 64x + 64) of every item
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;  // key row within the block (TMEM lane)
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
+    const uint32_t ds_row = smem_u32(sDS + x * kBox + row * 128);
+    uint32_t gi = 0, nu = 0, nkv = 0;
+    bool ok = true;
+    for (;; ++nu) {
+      const int u = take_unit(&bar->uq, nu, abort, p.err, true);
+      if (u < 0) break;
+      int b, hk, s0, qt0, per_head;
+      unit_info(u, b, hk, s0, qt0, per_head);
+      const int n_items = per_head * group;
+      const int s = s0 + row;
+      for (int it = 0; it < n_items; ++it) {
+        const uint32_t g = gi + it;
+        const int st = g & 1;
+        const uint32_t ph = (g >> 1) & 1;
+        const int t0 = (qt0 + it % per_head) * 128;
+        if (!(ok = mbar_wait(&bar->q_full[st], ph, abort, p.err))) break;
+        if (!(ok = mbar_wait(&bar->st_full[st], ph, abort, p.err))) break;
+        tc_fence_after();
+        const int lo = p.causal ? s - p.q_start - t0 - x * 64 : -(1 << 30);  // query columns below lo are masked
+        const bool need_mask = __any_sync(0xffffffffu, lo > 0);
+        const uint32_t sl = smem_u32(sVec + st * 256 + x * 64), sd = smem_u32(sVec + st * 256 + 128 + x * 64);
+        // phase 1: P^T = exp2(S^T c + nlse2), kept in registers as f32 and written to TMEM as bf16
+        uint32_t pr[64];
+        {
+          const uint32_t ts = tmem + lane_off + st * 128 + x * 64;
+          tmem_ld32(ts, *reinterpret_cast<uint32_t(*)[32]>(pr));
+          tmem_ld32(ts + 32, *reinterpret_cast<uint32_t(*)[32]>(pr + 32));
+          tmem_wait_ld();
+          uint32_t pp[32];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const float4 l4 = lds128(sl + 16 * q);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int cc = 4 * q + 2 * h2;
+              const uint64_t s2 = (uint64_t)pr[cc] | ((uint64_t)pr[cc + 1] << 32);
+              const uint64_t l2 = h2 ? f2_pack(l4.z, l4.w) : f2_pack(l4.x, l4.y);
+              float x0, x1;
+              f2_unpack(f2_fma(s2, c2, l2), x0, x1);
+              float p0 = ex2(x0), p1 = ex2(x1);
+              if (need_mask) {
+                p0 = cc >= lo ? p0 : 0.f;
+                p1 = cc + 1 >= lo ? p1 : 0.f;
+              }
+              pr[cc] = __float_as_uint(p0);
+              pr[cc + 1] = __float_as_uint(p1);
+              pp[2 * q + h2] = pack_bf16(p0, p1);
+            }
+          }
+          tmem_st32(ts, pp);
+          tmem_wait_st();
+          warp_arrive_after_tc(&bar->pt_full[st]);
+        }
+        // phase 2: dS^T = P^T (dP^T - D) to shared memory
+        if (!(ok = mbar_wait(&bar->dpt_full[st], ph, abort, p.err))) break;
+        tc_fence_after();
+        uint32_t dr[64];
+        {
+          const uint32_t td = tmem + lane_off + ((g + 1) & 1) * 128 + x * 64;
+          tmem_ld32(td, *reinterpret_cast<uint32_t(*)[32]>(dr));
+          tmem_ld32(td + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
+          tmem_wait_ld();
+          warp_arrive_after_tc(&bar->dp_free[st]);
+        }
+        uint32_t dd[32];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const float4 d4 = lds128(sd + 16 * q);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int cc = 4 * q + 2 * h2;
+            const uint64_t p2 = (uint64_t)pr[cc] | ((uint64_t)pr[cc + 1] << 32);
+            const uint64_t g2 = (uint64_t)dr[cc] | ((uint64_t)dr[cc + 1] << 32);
+            const uint64_t dd2 = h2 ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y);
+            float g0, g1;
+            f2_unpack(f2_mul(p2, f2_sub(g2, dd2)), g0, g1);
+            dd[2 * q + h2] = pack_bf16(g0, g1);
+          }
+        }
+        if (g > 0 && !(ok = mbar_wait(&bar->ds_free, (g - 1) & 1, abort, p.err))) break;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)  // 128-byte swizzled row of 64 queries for key `row`
+          sts128(ds_row + ((ch ^ (row & 7)) << 4), dd[4 * ch], dd[4 * ch + 1], dd[4 * ch + 2], dd[4 * ch + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->ds_full[st]);
+      }
+      if (!ok) break;
+      const bool store = s < p.S;
+      // warpgroup 0 writes dV, warpgroup 1 writes dK
+      __nv_bfloat16* dst = x == 0
+          ? static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] + (int64_t)s * p.s1[2]
+          : static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] + (int64_t)s * p.s0[2];
+      if (n_items == 0) {  // a key block past every query row: dK = dV = 0
+        if (store)
+          for (int i = 0; i < (x == 0 ? p.ncols1 : p.ncols0); i += 8)
+            *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
+        continue;
+      }
+      if (!(ok = mbar_wait(&bar->o_full, nkv & 1, abort, p.err))) break;
+      tc_fence_after();
+      store_cols_bf16<D>(tmem + lane_off + (x == 0 ? kDV : kDK), x == 0 ? 1.0f : p.scale, dst, store,
+                         x == 0 ? p.ncols1 : p.ncols0);
+      warp_arrive_after_tc(&bar->acc_free);
+      gi += n_items;
+      ++nkv;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dQ with 128-key items.  Unit = 128 query rows of one (batch, head); items =
+// 128-key tiles, so both score MMAs run at N = 128.  TMEM: S of item g in slot
+// g & 1 ([0,128) or [128,256)), dP of every item in [256,384), dQ in
+// [384,512).  The two compute warpgroups split an item's keys (warpgroup x:
+// keys [64x, 64x+64)) and write their dS (bf16 pairs) into their own first 32
+// columns of the item's S slot, where dQ += dS K reads it.  Because dP has a
+// slot of its own that is free as soon as the compute warps hold dP in
+// registers, the tensor core runs dQ(g-1), S(g+1) and dP(g+1) while item g's
+// exponentials are formed: per item the MMA issuer sends
+//   dP(g+1) [after item g's dP is in registers], dQ(g) [after dS(g)], S(g+2)
+// and S(g+2) overwrites the slot dQ(g) read, issued behind it.
+// K stays resident until its dQ completes (three stages), V until its dP (two).
+struct __align__(8) BarsQ {
+  uint64_t fixed_full, fixed_empty;  // Q / dO of the unit
+  uint64_t k_full[3], k_empty[3];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[2];   // S(g), dP(g) complete
+  uint64_t dp_free[2];  // compute warps hold dP(g) (and S(g)) in registers
+  uint64_t p_full[2];   // dS(g) written to TMEM
+  uint64_t o_full, acc_free;
+  UnitQueue uq;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr int kDq128KStages = 3, kDq128VStages = 2;
+constexpr int kDq128Smem = 2 * 32768 + (kDq128KStages + kDq128VStages) * 32768;  // + barriers + alignment
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dq128_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                     const BwdParams p) {
+  constexpr int D = 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kT = 128 * D * 2;  // one 128-row tile of Q, dO, K or V
+  constexpr uint32_t kBox = 128 * 128;
+  uint8_t* sQ = smem;
+  uint8_t* sDO = smem + kT;
+  uint8_t* sK = smem + 2 * kT;                    // kDq128KStages
+  uint8_t* sV = sK + kDq128KStages * kT;          // kDq128VStages
+  BarsQ* bar = reinterpret_cast<BarsQ*>(sV + kDq128VStages * kT);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_bh = p.B * p.H;
+  const int n_units = p.n_blocks * n_bh;
+  const int n_all = (p.S + 127) / 128;
+  auto unit_info = [&](int u, int& b, int& h, int& t0, int& n_kv) {
+    const int mblk = p.n_blocks - 1 - u / n_bh, bh = u % n_bh;  // heaviest first
+    b = bh / p.H;
+    h = bh % p.H;
+    t0 = mblk * 128;
+    n_kv = n_all;
+    if (p.causal) {
+      int last = t0 + 127;
+      if (last > p.T - 1) last = p.T - 1;
+      const int n = (last + p.q_start) / 128 + 1;
+      n_kv = n < n_all ? (n > 0 ? n : 0) : n_all;
+    }
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->fixed_full, 1);
+    mbar_init(&bar->fixed_empty, 1);
+    for (int i = 0; i < kDq128KStages; ++i) {
+      mbar_init(&bar->k_full[i], 1);
+      mbar_init(&bar->k_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->v_full[i], 1);
+      mbar_init(&bar->v_empty[i], 1);
+      mbar_init(&bar->s_full[i], 1);
+      mbar_init(&bar->dp_free[i], 8);  // one arrival per compute warp
+      mbar_init(&bar->p_full[i], 8);
+      mbar_init(&bar->uq.full[i], 1);
+      mbar_init(&bar->uq.empty[i], 9);
+    }
+    mbar_init(&bar->o_full, 1);
+    mbar_init(&bar->acc_free, 8);
+    bar->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  volatile int* abort = &bar->abort;
+  constexpr int kNB = D / 64;
+  constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);  // S, dP: M = 128 rows, N = 128 keys
+  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);    // dQ: N = D, B = K tile MN-major
+  constexpr uint32_t kDP = 256, kDQ = 384;              // TMEM columns
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- producer
+      uint32_t gi = 0, nu = 0, nqd = 0;
+      for (;; ++nu) {
+        int u = atomicAdd(p.ctr + 1, 1);
+        if (u >= n_units) u = -1;
+        if (fetch_unit(&bar->uq, nu, u, abort, p.err) < 0) break;
+        int b, h, t0, n_kv;
+        unit_info(u, b, h, t0, n_kv);
+        if (n_kv == 0) continue;
+        const int hk = h / (p.H / p.HKV);
+        if (!mbar_wait(&bar->fixed_empty, (nqd & 1) ^ 1, abort, p.err)) break;
+        mbar_expect_tx(&bar->fixed_full, 2 * kT);
+        for (int i = 0; i < kNB; ++i) {
+          tma_load_4d(sQ + i * kBox, &tm_q, &bar->fixed_full, i * 64, t0, h, b);
+          tma_load_4d(sDO + i * kBox, &tm_do, &bar->fixed_full, i * 64, t0, h, b);
+        }
+        ++nqd;
+        bool ok = true;
+        for (int j = 0; j < n_kv; ++j, ++gi) {
+          const int ks = gi % kDq128KStages, vs = gi & 1;
+          if (!(ok = mbar_wait(&bar->k_empty[ks], ((gi / kDq128KStages) & 1) ^ 1, abort, p.err))) break;
+          mbar_expect_tx(&bar->k_full[ks], kT);
+          for (int i = 0; i < kNB; ++i)
+            tma_load_4d(sK + ks * kT + i * kBox, &tm_k, &bar->k_full[ks], i * 64, j * 128, hk, b);
+          if (!(ok = mbar_wait(&bar->v_empty[vs], ((gi >> 1) & 1) ^ 1, abort, p.err))) break;
+          mbar_expect_tx(&bar->v_full[vs], kT);
+          for (int i = 0; i < kNB; ++i)
+            tma_load_4d(sV + vs * kT + i * kBox, &tm_v, &bar->v_full[vs], i * 64, j * 128, hk, b);
+        }
+        if (!ok) break;
+      }
+    } else if (warp == 1 && lane == 0) {
+      // -------------------------------------------------------- MMA issuer
+      uint32_t gi = 0, nu = 0, nqd = 0;
+      bool ok = true;
+      for (;; ++nu) {
+        const int u = take_unit(&bar->uq, nu, abort, p.err, false);
+        if (u < 0) break;
+        int b, h, t0, n_kv;
+        unit_info(u, b, h, t0, n_kv);
+        if (n_kv == 0) continue;
+        auto issue_s = [&](int j) -> bool {  // S(g) into slot g & 1
+          const uint32_t g = gi + j;
+          const int ks = g % kDq128KStages;
+          if (!mbar_wait(&bar->k_full[ks], (g / kDq128KStages) & 1, abort, p.err)) return false;
+          tc_fence_after();
+          mma_kmajor<D>(tmem + (g & 1) * 128, smem_u32(sQ), kBox, smem_u32(sK + ks * kT), kBox, idS);
+          return true;
+        };
+        auto issue_dp = [&](int j) -> bool {  // dP(g) into [256, 384) once item g-1's dP is in registers
+          const uint32_t g = gi + j;
+          const int vs = g & 1;
+          if (!mbar_wait(&bar->v_full[vs], (g >> 1) & 1, abort, p.err)) return false;
+          if (g > 0 && !mbar_wait(&bar->dp_free[(g - 1) & 1], ((g - 1) >> 1) & 1, abort, p.err)) return false;
+          tc_fence_after();
+          mma_kmajor<D>(tmem + kDP, smem_u32(sDO), kBox, smem_u32(sV + vs * kT), kBox, idS);
+          tc_commit(&bar->v_empty[vs]);
+          tc_commit(&bar->s_full[g & 1]);
+          if (j == n_kv - 1) tc_commit(&bar->fixed_empty);  // Q / dO no longer needed: load the next unit's
+          return true;
+        };
+        if (!(ok = mbar_wait(&bar->fixed_full, nqd & 1, abort, p.err))) break;
+        ok = issue_s(0) && issue_dp(0);
+        if (ok && n_kv > 1) ok = issue_s(1);
+        for (int j = 0; ok && j < n_kv; ++j) {
+          const uint32_t g = gi + j;
+          if (j + 1 < n_kv && !(ok = issue_dp(j + 1))) break;
+          if (!(ok = mbar_wait(&bar->p_full[g & 1], (g >> 1) & 1, abort, p.err))) break;
+          if (j == 0 && nqd > 0 && !(ok = mbar_wait(&bar->acc_free, (nqd - 1) & 1, abort, p.err))) break;
+          tc_fence_after();
+          // dQ += dS K: dS of keys [0, 64) in the slot's columns [0, 32), of keys [64, 128) in [64, 96)
+          const uint32_t a = tmem + (g & 1) * 128;
+          const uint32_t bk = smem_u32(sK + (g % kDq128KStages) * kT);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ts(tmem + kDQ, a + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_sw128(bk + kk * 2048, kBox, 1024), idG,
+                   (j > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&bar->k_empty[g % kDq128KStages]);
+          if (j + 2 < n_kv) ok = issue_s(j + 2);
+        }
+        if (!ok) break;
+        tc_commit(&bar->o_full);
+        gi += n_kv;
+        ++nqd;
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
+    const int x = warp >= 8 ? 1 : 0;  // keys [64x, 64x + 64) of every item
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const float c = p.scale_log2;
+    uint32_t gi = 0, nu = 0, nqd = 0;
+    bool ok = true;
+    for (;; ++nu) {
+      const int u = take_unit(&bar->uq, nu, abort, p.err, true);
+      if (u < 0) break;
+      int b, h, t0, n_kv;
+      unit_info(u, b, h, t0, n_kv);
+      const int t = t0 + row;
+      __nv_bfloat16* dq = static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)h * p.s0[1] +
+                          (int64_t)t * p.s0[2];
+      if (n_kv == 0) {  // no key is visible to these rows: dQ = 0
+        if (t < p.T)
+          for (int i = 0; i < D / 2; i += 8) *reinterpret_cast<uint4*>(dq + x * (D / 2) + i) = make_uint4(0, 0, 0, 0);
+        continue;
+      }
+      const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t;
+      const float l2 = p.nlse2[vrow];  // -inf on padded rows -> P = 0
+      const float dsum = p.dsum[vrow];
+      for (int j = 0; j < n_kv; ++j) {
+        const uint32_t g = gi + j;
+        if (!(ok = mbar_wait(&bar->s_full[g & 1], (g >> 1) & 1, abort, p.err))) break;
+        tc_fence_after();
+        const uint32_t ts = tmem + lane_off + (g & 1) * 128 + x * 64;
+        const uint32_t td = tmem + lane_off + kDP + x * 64;
+        const int lim = p.causal ? t + p.q_start + 1 - j * 128 - x * 64 : (1 << 30);  // key columns >= lim masked
+        uint32_t sr[64], dr[64];
+        tmem_ld32(ts, *reinterpret_cast<uint32_t(*)[32]>(sr));
+        tmem_ld32(ts + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+        tmem_ld32(td, *reinterpret_cast<uint32_t(*)[32]>(dr));
+        tmem_ld32(td + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
+        tmem_wait_ld();
+        warp_arrive_after_tc(&bar->dp_free[g & 1]);
+        uint32_t pp[32], dd[32];
+        p_ds_64(sr, dr, c, [&](int) { return l2; }, [&](int) { return dsum; }, [&](int col) { return col < lim; }, pp,
+                dd);
+        tmem_st32(ts, dd);
+        tmem_wait_st();
+        warp_arrive_after_tc(&bar->p_full[g & 1]);
+      }
+      if (!ok) break;
+      if (!(ok = mbar_wait(&bar->o_full, nqd & 1, abort, p.err))) break;
+      tc_fence_after();
+      // each warpgroup writes half of the dQ columns
+      store_cols_bf16<D / 2>(tmem + lane_off + kDQ + x * (D / 2), p.scale, dq + x * (D / 2), t < p.T,
                              p.ncols0 - x * (D / 2));
       warp_arrive_after_tc(&bar->acc_free);
       gi += n_kv;
@@ -1363,11 +1951,20 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       p.n_blocks = (int)((d.seqlen_k + 127) / 128);
       const int64_t grid = (int64_t)p.n_blocks * d.heads_kv * d.batch;
       {
-        cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
-        if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
         p.ctr = ctr;
         const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-        e = launch_overlapped(bwd_dkdv_kernel<D>, pgrid, kThreads, smem_kv, stream, tq64, tk128, tv128, tdo64, p);
+        cudaError_t e;
+        static const bool old_kv = getenv("PDB_BWD_DKDV64") != nullptr;
+        if (old_kv) {
+          e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
+          if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
+          e = launch_overlapped(bwd_dkdv_kernel<D>, pgrid, kThreads, smem_kv, stream, tq64, tk128, tv128, tdo64, p);
+        } else {
+          e = cudaFuncSetAttribute(bwd_dkdv128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+          if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
+          e = launch_overlapped(bwd_dkdv128_kernel, pgrid, kThreads, kMaxDynSmem, stream, tq128, tk128, tv128, tdo128,
+                                p);
+        }
         if (e != cudaSuccess) return cuda_status(e, "bwd dkdv launch");
       }
       if (int st = cuda_status(cudaGetLastError(), "bwd dkdv launch")) return st;
@@ -1381,11 +1978,20 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       p.n_blocks = (int)(tpad / 128);
       const int64_t grid = (int64_t)p.n_blocks * d.heads_q * d.batch;
       {
-        cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
-        if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
         p.ctr = ctr;
         const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-        e = launch_overlapped(bwd_dq_kernel<D>, pgrid, kThreads, smem_q, stream, tq128, tk64, tv64, tdo128, p);
+        cudaError_t e;
+        static const bool old_dq = getenv("PDB_BWD_DQ64") != nullptr;
+        if (old_dq) {
+          e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
+          if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
+          e = launch_overlapped(bwd_dq_kernel<D>, pgrid, kThreads, smem_q, stream, tq128, tk64, tv64, tdo128, p);
+        } else {
+          const int smem = kDq128Smem + (int)sizeof(BarsQ) + 1024;
+          e = cudaFuncSetAttribute(bwd_dq128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+          if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
+          e = launch_overlapped(bwd_dq128_kernel, pgrid, kThreads, smem, stream, tq128, tk128, tv128, tdo128, p);
+        }
         if (e != cudaSuccess) return cuda_status(e, "bwd dq launch");
       }
       if (int st = cuda_status(cudaGetLastError(), "bwd dq launch")) return st;
