@@ -13,21 +13,21 @@
 //   D = 64: bwd_fused64 (dK, dV and dQ in one persistent pass; dQ parts are
 //                added into an fp32 accumulator in L2 by TMA bulk reductions)
 //                and bwd_dq_convert (dQ = scale * accumulator, to bf16)
-//   D = 128: bwd_dkdv and bwd_dq, two persistent passes:
-//   bwd_dkdv     per (batch, KV head, 128-key block): for every query tile of
-//                every query head of the group it forms S^T = K Q^T and
-//                dP^T = V dO^T in TMEM, P^T = exp2(S^T c + nlse2),
-//                dS^T = P^T (dP^T - D) (one thread per key row), writes both
-//                back to TMEM as bf16 and accumulates dV += P^T dO,
+//   D = 128: bwd_dkdv128 and bwd_dq128, two persistent passes with 128-wide
+//                items, so every score MMA is M = N = 128:
+//   bwd_dkdv128  per (batch, KV head, 128-key block): for every 128-row query
+//                tile of every query head of the group it forms S^T = K Q^T
+//                and dP^T = V dO^T in TMEM, P^T = exp2(S^T c + nlse2) (bf16,
+//                back to TMEM), dS^T = P^T (dP^T - D) (bf16, to shared
+//                memory; one thread per key row) and accumulates dV += P^T dO,
 //                dK += dS^T Q in TMEM; GQA sums over the group in place.
-//   bwd_dq       per (batch, head, 128-row block): S = Q K^T, dP = dO V^T,
-//                dS = P (dP - D), dQ += dS K over the key tiles.
+//   bwd_dq128    per (batch, head, 128-row block): S = Q K^T, dP = dO V^T,
+//                dS = P (dP - D), dQ += dS K over 128-key tiles.
 // dQ = scale dS K, dK = scale dS^T Q; everything accumulates in fp32 (TMEM,
 // and for the fused pass's dQ, fp32 in L2) and is rounded to bf16 once.  The
 // D = 128 passes use no atomics (bit-reproducible); the fused pass's dQ sums
 // its per-key-block parts in whatever order the reductions land.
 #include <cfloat>
-#include <cstdlib>
 #include <mutex>
 #include <utility>
 
@@ -77,15 +77,6 @@ __device__ __forceinline__ void mma_kmajor(uint32_t d_tmem, uint32_t a_saddr, ui
   }
 }
 
-// D (128 x D) (+)= A_tmem (128 x K, bf16 packed pairs) * B_smem (K rows x D, MN-major, box `b_box` bytes)
-template <int K>
-__device__ __forceinline__ void mma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_saddr, uint32_t b_box,
-                                           uint32_t idesc, bool acc) {
-#pragma unroll
-  for (int kk = 0; kk < K / 16; ++kk)
-    mma_ts(d_tmem, a_tmem + kk * 8, sdesc_sw128(b_saddr + kk * 2048, b_box, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
-}
-
 // rows of a TMEM accumulator (columns [c0, c0 + NC)) -> bf16 global, scaled
 template <int NC>
 __device__ __forceinline__ void store_cols_bf16(uint32_t t_src, float mul, __nv_bfloat16* row, bool store,
@@ -128,10 +119,6 @@ __device__ __forceinline__ void p_ds_64(const uint32_t (&sr)[64], const uint32_t
   }
 }
 
-constexpr int QT = 64;   // query rows per dK/dV work item
-constexpr int KT = 64;   // keys per dQ work item
-constexpr int kStages = 3;
-
 // Persistent scheduling of the backward kernels.  The work units (a 128-key
 // block for dK/dV, a 128-row query block for dQ) differ in size under the
 // causal mask (1 to n items); one CTA per unit left SMs idle ~40 % of the time
@@ -163,464 +150,7 @@ __device__ __forceinline__ int take_unit(UnitQueue* uq, uint32_t n, volatile int
   return u;
 }
 
-struct __align__(8) BarsG {
-  uint64_t fixed_full, fixed_empty;                    // K/V (dK/dV kernel) or Q/dO (dQ kernel), one buffer
-  uint64_t op_full[kStages], op_empty[kStages];        // streamed operand ring
-  uint64_t s_full[2], p_full[2];                        // score buffers, alternating items
-  uint64_t o_full, acc_free;
-  UnitQueue uq;
-  uint32_t tmem_base;
-  int abort;
-};
-
 // ------------------------------------------------------------------ dK / dV
-// Unit = 128 keys of one (batch, KV head).  Work items: (query head of the
-// group, 64-row query tile).  TMEM buffer x in {0, 1}: S^T [128x, 128x+64),
-// dP^T [128x+64, 128x+128) (P^T / dS^T written back as bf16 into their first
-// 32 columns); dV [256, 256+D), dK [256+D, 256+2D).  Items alternate between
-// the buffers (running item count g: x = g mod 2) and compute warpgroup x
-// handles buffer x, so one warpgroup computes while the tensor core runs the
-// other's MMAs.  Persistent like the D = 64 kernels; the next unit's K/V load
-// once the unit's last score MMA has been issued.
-template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
-    bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                    const BwdParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kKV = 128 * D * 2;  // K or V tile
-  constexpr int kQ = QT * D * 2;    // Q or dO tile
-  constexpr uint32_t kBoxKV = 128 * 128, kBoxQ = QT * 128;
-  uint8_t* sK = smem;
-  uint8_t* sV = smem + kKV;
-  uint8_t* sQ = smem + 2 * kKV;                 // kStages
-  uint8_t* sDO = sQ + kStages * kQ;             // kStages
-  float* sVec = reinterpret_cast<float*>(sDO + kStages * kQ);  // kStages x (nlse2[64], dsum[64])
-  BarsG* bar = reinterpret_cast<BarsG*>(reinterpret_cast<uint8_t*>(sVec) + kStages * 2 * QT * 4);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int group = p.H / p.HKV;
-  const int n_qt = p.Tpad / QT;
-  const int n_bh = p.B * p.HKV;
-  const int n_units = p.n_blocks * n_bh;
-  auto unit_info = [&](int u, int& b, int& hk, int& s0, int& qt0, int& per_head) {
-    const int nblk = u / n_bh, bhk = u % n_bh;  // ascending key block = descending work (causal)
-    b = bhk / p.HKV;
-    hk = bhk % p.HKV;
-    s0 = nblk * 128;
-    qt0 = 0;
-    if (p.causal) {
-      const int first = s0 - p.q_start;  // first query row that can see key s0
-      qt0 = first > 0 ? first / QT : 0;
-    }
-    per_head = n_qt - qt0 > 0 ? n_qt - qt0 : 0;
-  };
-
-  if (threadIdx.x == 0) {
-    mbar_init(&bar->fixed_full, 1);
-    mbar_init(&bar->fixed_empty, 1);
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&bar->op_full[i], 1);
-      mbar_init(&bar->op_empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar->s_full[i], 1);
-      mbar_init(&bar->p_full[i], 4);  // one arrival per compute warp
-      mbar_init(&bar->uq.full[i], 1);
-      mbar_init(&bar->uq.empty[i], 9);  // the MMA thread + 8 compute warps
-    }
-    mbar_init(&bar->o_full, 1);
-    mbar_init(&bar->acc_free, 8);
-    bar->abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == 2) {
-    tmem_alloc(&bar->tmem_base, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  grid_dep_wait();    // the prologue (D, nlse2, zeroed counters) has completed
-  grid_dep_launch();  // the dQ grid may take SMs as this grid's CTAs retire
-  const uint32_t tmem = bar->tmem_base;
-  volatile int* abort = &bar->abort;
-  constexpr int kNB = D / 64;
-  constexpr uint32_t idS = idesc_bf16(128, QT, 0, 0);  // S^T, dP^T: M = 128 keys, N = 64 queries
-  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);   // dV, dK: M = 128 keys, N = D, B MN-major
-
-  if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");
-    if (warp == 0 && lane == 0) {
-      // ---------------------------------------------------------- producer
-      uint32_t gi = 0, nu = 0, nkv = 0;
-      for (;; ++nu) {
-        int u = atomicAdd(p.ctr, 1);
-        if (u >= n_units) u = -1;
-        if (fetch_unit(&bar->uq, nu, u, abort, p.err) < 0) break;
-        int b, hk, s0, qt0, per_head;
-        unit_info(u, b, hk, s0, qt0, per_head);
-        const int n_items = per_head * group;
-        if (n_items == 0) continue;
-        if (!mbar_wait(&bar->fixed_empty, (nkv & 1) ^ 1, abort, p.err)) break;
-        mbar_expect_tx(&bar->fixed_full, 2 * kKV);
-        for (int i = 0; i < kNB; ++i) {
-          tma_load_4d(sK + i * kBoxKV, &tm_k, &bar->fixed_full, i * 64, s0, hk, b);
-          tma_load_4d(sV + i * kBoxKV, &tm_v, &bar->fixed_full, i * 64, s0, hk, b);
-        }
-        ++nkv;
-        bool ok = true;
-        for (int it = 0; it < n_items; ++it, ++gi) {
-          const int st = gi % kStages;
-          const int h = hk * group + it / per_head;
-          const int t0 = (qt0 + it % per_head) * QT;
-          if (!(ok = mbar_wait(&bar->op_empty[st], ((gi / kStages) & 1) ^ 1, abort, p.err))) break;
-          mbar_expect_tx(&bar->op_full[st], 2 * kQ + 2 * QT * 4);
-          for (int i = 0; i < kNB; ++i) {
-            tma_load_4d(sQ + st * kQ + i * kBoxQ, &tm_q, &bar->op_full[st], i * 64, t0, h, b);
-            tma_load_4d(sDO + st * kQ + i * kBoxQ, &tm_do, &bar->op_full[st], i * 64, t0, h, b);
-          }
-          const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t0;
-          bulk_load(sVec + st * 2 * QT, p.nlse2 + vrow, QT * 4, &bar->op_full[st]);
-          bulk_load(sVec + st * 2 * QT + QT, p.dsum + vrow, QT * 4, &bar->op_full[st]);
-        }
-        if (!ok) break;
-      }
-    } else if (warp == 1 && lane == 0) {
-      // -------------------------------------------------------- MMA issuer
-      uint32_t gi = 0, nu = 0, nkv = 0;
-      bool ok = true;
-      for (;; ++nu) {
-        const int u = take_unit(&bar->uq, nu, abort, p.err, false);
-        if (u < 0) break;
-        int b, hk, s0, qt0, per_head;
-        unit_info(u, b, hk, s0, qt0, per_head);
-        const int n_items = per_head * group;
-        if (n_items == 0) continue;
-        // score MMAs of item it into buffer x = g & 1; its previous occupant (item
-        // g - 2) was consumed by accumulations issued before this call
-        auto issue_s = [&](int it) -> bool {
-          const uint32_t g = gi + it;
-          const int st = g % kStages, x = g & 1;
-          if (!mbar_wait(&bar->op_full[st], (g / kStages) & 1, abort, p.err)) return false;
-          tc_fence_after();
-          mma_kmajor<D>(tmem + x * 128, smem_u32(sK), kBoxKV, smem_u32(sQ + st * kQ), kBoxQ, idS);        // S^T
-          mma_kmajor<D>(tmem + x * 128 + 64, smem_u32(sV), kBoxKV, smem_u32(sDO + st * kQ), kBoxQ, idS);  // dP^T
-          tc_commit(&bar->s_full[x]);
-          if (it == n_items - 1) tc_commit(&bar->fixed_empty);  // K/V no longer needed: load the next unit's
-          return true;
-        };
-        if (!(ok = mbar_wait(&bar->fixed_full, nkv & 1, abort, p.err))) break;
-        if (ok && n_items > 0) ok = issue_s(0);
-        if (ok && n_items > 1) ok = issue_s(1);
-        for (int it = 0; ok && it < n_items; ++it) {
-          const uint32_t g = gi + it;
-          const int st = g % kStages, x = g & 1;
-          if (!(ok = mbar_wait(&bar->p_full[x], (g >> 1) & 1, abort, p.err))) break;
-          if (it == 0 && nkv > 0 && !(ok = mbar_wait(&bar->acc_free, (nkv - 1) & 1, abort, p.err))) break;
-          tc_fence_after();
-          mma_tmem_a<QT>(tmem + 256, tmem + x * 128, smem_u32(sDO + st * kQ), kBoxQ, idG, it > 0);      // dV += P^T dO
-          mma_tmem_a<QT>(tmem + 256 + D, tmem + x * 128 + 64, smem_u32(sQ + st * kQ), kBoxQ, idG, it > 0);  // dK += dS^T Q
-          tc_commit(&bar->op_empty[st]);
-          if (it + 2 < n_items) ok = issue_s(it + 2);
-        }
-        if (!ok) break;
-        tc_commit(&bar->o_full);
-        gi += n_items;
-        ++nkv;
-      }
-    }
-  } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
-    const int x = warp >= 8 ? 1 : 0;
-    const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;  // key row within the block (TMEM lane)
-    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const uint32_t tb = tmem + lane_off + x * 128;
-    const float c = p.scale_log2;
-    uint32_t gi = 0, nu = 0, nkv = 0;
-    bool ok = true;
-    for (;; ++nu) {
-      const int u = take_unit(&bar->uq, nu, abort, p.err, true);
-      if (u < 0) break;
-      int b, hk, s0, qt0, per_head;
-      unit_info(u, b, hk, s0, qt0, per_head);
-      const int n_items = per_head * group;
-      const int s = s0 + row;
-      for (int it = (int)((x - gi) & 1u); it < n_items; it += 2) {  // items of buffer x
-        const uint32_t g = gi + it;
-        const int st = g % kStages;
-        const int t0 = (qt0 + it % per_head) * QT;
-        if (!(ok = mbar_wait(&bar->op_full[st], (g / kStages) & 1, abort, p.err))) break;
-        if (!(ok = mbar_wait(&bar->s_full[x], (g >> 1) & 1, abort, p.err))) break;
-        tc_fence_after();
-        const float* lse2 = sVec + st * 2 * QT;
-        const float* dsum = lse2 + QT;
-        const int lo = p.causal ? s - p.q_start - t0 : -1;  // query columns below lo cannot see key s
-        // two halves of 32 query columns; per-column nlse2 / D read as float4 from shared memory
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t sr[32], dr[32];
-          tmem_ld32(tb + hf * 32, sr);
-          tmem_ld32(tb + 64 + hf * 32, dr);
-          tmem_wait_ld();
-          uint32_t pp[16], dd[16];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 l4 = lds128(smem_u32(lse2 + hf * 32) + 16 * q);
-            const float4 d4 = lds128(smem_u32(dsum + hf * 32) + 16 * q);
-            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-            float pv[4], gv[4];
-#pragma unroll
-            for (int uu = 0; uu < 4; ++uu) {
-              const int col = hf * 32 + 4 * q + uu;
-              float pr = ex2(fmaf(__uint_as_float(sr[4 * q + uu]), c, lv[uu]));
-              pr = col >= lo ? pr : 0.f;
-              pv[uu] = pr;
-              gv[uu] = pr * (__uint_as_float(dr[4 * q + uu]) - dv4[uu]);
-            }
-            pp[2 * q] = pack_bf16(pv[0], pv[1]);
-            pp[2 * q + 1] = pack_bf16(pv[2], pv[3]);
-            dd[2 * q] = pack_bf16(gv[0], gv[1]);
-            dd[2 * q + 1] = pack_bf16(gv[2], gv[3]);
-          }
-          tmem_st16(tb + hf * 16, pp);
-          tmem_st16(tb + 64 + hf * 16, dd);
-        }
-        tmem_wait_st();
-        warp_arrive_after_tc(&bar->p_full[x]);
-      }
-      if (!ok) break;
-      const bool store = s < p.S;
-      // warpgroup 0 writes dV, warpgroup 1 writes dK
-      __nv_bfloat16* dst = x == 0
-          ? static_cast<__nv_bfloat16*>(p.out1) + (int64_t)b * p.s1[0] + (int64_t)hk * p.s1[1] + (int64_t)s * p.s1[2]
-          : static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)hk * p.s0[1] + (int64_t)s * p.s0[2];
-      if (n_items == 0) {  // a key block past every query row: dK = dV = 0
-        if (store)
-          for (int i = 0; i < (x == 0 ? p.ncols1 : p.ncols0); i += 8)
-            *reinterpret_cast<uint4*>(dst + i) = make_uint4(0, 0, 0, 0);
-        continue;
-      }
-      if (!(ok = mbar_wait(&bar->o_full, nkv & 1, abort, p.err))) break;
-      tc_fence_after();
-      store_cols_bf16<D>(tmem + lane_off + 256 + x * D, x == 0 ? 1.0f : p.scale, dst, store,
-                         x == 0 ? p.ncols1 : p.ncols0);
-      warp_arrive_after_tc(&bar->acc_free);
-      gi += n_items;
-      ++nkv;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// dQ.  Unit = 128 query rows of one (batch, head); items = 64-key tiles.
-// TMEM buffer x: S [128x, 128x+64), dP [128x+64, 128x+128) (dS written back as
-// bf16 into the first 32 columns); dQ [256, 256+D).  Persistent; the next
-// unit's Q/dO load once the unit's last score MMA has been issued.
-template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
-    bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                  const BwdParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kQ = 128 * D * 2;
-  constexpr int kKV = KT * D * 2;
-  constexpr uint32_t kBoxQ = 128 * 128, kBoxKV = KT * 128;
-  uint8_t* sQ = smem;
-  uint8_t* sDO = smem + kQ;
-  uint8_t* sK = smem + 2 * kQ;          // kStages
-  uint8_t* sV = sK + kStages * kKV;     // kStages
-  BarsG* bar = reinterpret_cast<BarsG*>(sV + kStages * kKV);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_bh = p.B * p.H;
-  const int n_units = p.n_blocks * n_bh;
-  const int n_all = (p.S + KT - 1) / KT;
-  auto unit_info = [&](int u, int& b, int& h, int& t0, int& n_kv) {
-    const int mblk = p.n_blocks - 1 - u / n_bh, bh = u % n_bh;  // heaviest first
-    b = bh / p.H;
-    h = bh % p.H;
-    t0 = mblk * 128;
-    n_kv = n_all;
-    if (p.causal) {
-      int last = t0 + 127;
-      if (last > p.T - 1) last = p.T - 1;
-      const int n = (last + p.q_start) / KT + 1;
-      n_kv = n < n_all ? (n > 0 ? n : 0) : n_all;
-    }
-  };
-
-  if (threadIdx.x == 0) {
-    mbar_init(&bar->fixed_full, 1);
-    mbar_init(&bar->fixed_empty, 1);
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&bar->op_full[i], 1);
-      mbar_init(&bar->op_empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar->s_full[i], 1);
-      mbar_init(&bar->p_full[i], 4);  // one arrival per compute warp
-      mbar_init(&bar->uq.full[i], 1);
-      mbar_init(&bar->uq.empty[i], 9);
-    }
-    mbar_init(&bar->o_full, 1);
-    mbar_init(&bar->acc_free, 8);
-    bar->abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == 2) {
-    tmem_alloc(&bar->tmem_base, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = bar->tmem_base;
-  volatile int* abort = &bar->abort;
-  constexpr int kNB = D / 64;
-  constexpr uint32_t idS = idesc_bf16(128, KT, 0, 0);  // S, dP: M = 128 rows, N = 64 keys
-  constexpr uint32_t idG = idesc_bf16(128, D, 0, 1);   // dQ: N = D, B = K tile MN-major
-
-  if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");
-    if (warp == 0 && lane == 0) {
-      uint32_t gi = 0, nu = 0, nqd = 0;
-      for (;; ++nu) {
-        int u = atomicAdd(p.ctr + 1, 1);
-        if (u >= n_units) u = -1;
-        if (fetch_unit(&bar->uq, nu, u, abort, p.err) < 0) break;
-        int b, h, t0, n_kv;
-        unit_info(u, b, h, t0, n_kv);
-        if (n_kv == 0) continue;
-        const int hk = h / (p.H / p.HKV);
-        if (!mbar_wait(&bar->fixed_empty, (nqd & 1) ^ 1, abort, p.err)) break;
-        mbar_expect_tx(&bar->fixed_full, 2 * kQ);
-        for (int i = 0; i < kNB; ++i) {
-          tma_load_4d(sQ + i * kBoxQ, &tm_q, &bar->fixed_full, i * 64, t0, h, b);
-          tma_load_4d(sDO + i * kBoxQ, &tm_do, &bar->fixed_full, i * 64, t0, h, b);
-        }
-        ++nqd;
-        bool ok = true;
-        for (int j = 0; j < n_kv; ++j, ++gi) {
-          const int st = gi % kStages;
-          if (!(ok = mbar_wait(&bar->op_empty[st], ((gi / kStages) & 1) ^ 1, abort, p.err))) break;
-          mbar_expect_tx(&bar->op_full[st], 2 * kKV);
-          for (int i = 0; i < kNB; ++i) {
-            tma_load_4d(sK + st * kKV + i * kBoxKV, &tm_k, &bar->op_full[st], i * 64, j * KT, hk, b);
-            tma_load_4d(sV + st * kKV + i * kBoxKV, &tm_v, &bar->op_full[st], i * 64, j * KT, hk, b);
-          }
-        }
-        if (!ok) break;
-      }
-    } else if (warp == 1 && lane == 0) {
-      uint32_t gi = 0, nu = 0, nqd = 0;
-      bool ok = true;
-      for (;; ++nu) {
-        const int u = take_unit(&bar->uq, nu, abort, p.err, false);
-        if (u < 0) break;
-        int b, h, t0, n_kv;
-        unit_info(u, b, h, t0, n_kv);
-        if (n_kv == 0) continue;
-        auto issue_s = [&](int j) -> bool {
-          const uint32_t g = gi + j;
-          const int st = g % kStages, x = g & 1;
-          if (!mbar_wait(&bar->op_full[st], (g / kStages) & 1, abort, p.err)) return false;
-          tc_fence_after();
-          mma_kmajor<D>(tmem + x * 128, smem_u32(sQ), kBoxQ, smem_u32(sK + st * kKV), kBoxKV, idS);        // S
-          mma_kmajor<D>(tmem + x * 128 + 64, smem_u32(sDO), kBoxQ, smem_u32(sV + st * kKV), kBoxKV, idS);  // dP
-          tc_commit(&bar->s_full[x]);
-          if (j == n_kv - 1) tc_commit(&bar->fixed_empty);  // Q/dO no longer needed: load the next unit's
-          return true;
-        };
-        if (!(ok = mbar_wait(&bar->fixed_full, nqd & 1, abort, p.err))) break;
-        if (ok && n_kv > 0) ok = issue_s(0);
-        if (ok && n_kv > 1) ok = issue_s(1);
-        for (int j = 0; ok && j < n_kv; ++j) {
-          const uint32_t g = gi + j;
-          const int st = g % kStages, x = g & 1;
-          if (!(ok = mbar_wait(&bar->p_full[x], (g >> 1) & 1, abort, p.err))) break;
-          if (j == 0 && nqd > 0 && !(ok = mbar_wait(&bar->acc_free, (nqd - 1) & 1, abort, p.err))) break;
-          tc_fence_after();
-          mma_tmem_a<KT>(tmem + 256, tmem + x * 128, smem_u32(sK + st * kKV), kBoxKV, idG, j > 0);  // dQ += dS K
-          tc_commit(&bar->op_empty[st]);
-          if (j + 2 < n_kv) ok = issue_s(j + 2);
-        }
-        if (!ok) break;
-        tc_commit(&bar->o_full);
-        gi += n_kv;
-        ++nqd;
-      }
-    }
-  } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
-    const int x = warp >= 8 ? 1 : 0;
-    const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const uint32_t tb = tmem + lane_off + x * 128;
-    const float c = p.scale_log2;
-    uint32_t gi = 0, nu = 0, nqd = 0;
-    bool ok = true;
-    for (;; ++nu) {
-      const int u = take_unit(&bar->uq, nu, abort, p.err, true);
-      if (u < 0) break;
-      int b, h, t0, n_kv;
-      unit_info(u, b, h, t0, n_kv);
-      const int t = t0 + row;
-      __nv_bfloat16* dq = static_cast<__nv_bfloat16*>(p.out0) + (int64_t)b * p.s0[0] + (int64_t)h * p.s0[1] +
-                          (int64_t)t * p.s0[2];
-      if (n_kv == 0) {  // no key is visible to these rows: dQ = 0
-        if (t < p.T)
-          for (int i = 0; i < D / 2; i += 8) *reinterpret_cast<uint4*>(dq + x * (D / 2) + i) = make_uint4(0, 0, 0, 0);
-        continue;
-      }
-      const int64_t vrow = ((int64_t)b * p.H + h) * p.Tpad + t;
-      const float l2 = p.nlse2[vrow];  // -inf on padded rows -> P = 0
-      const float dsum = p.dsum[vrow];
-      for (int j = (int)((x - gi) & 1u); j < n_kv; j += 2) {  // items of buffer x
-        const uint32_t g = gi + j;
-        if (!(ok = mbar_wait(&bar->s_full[x], (g >> 1) & 1, abort, p.err))) break;
-        tc_fence_after();
-        const int lim = p.causal ? t + p.q_start + 1 - j * KT : (1 << 30);  // key columns >= lim masked
-        uint32_t sr[64], dr[64];
-        tmem_ld32(tb, *reinterpret_cast<uint32_t(*)[32]>(sr));
-        tmem_ld32(tb + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-        tmem_ld32(tb + 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
-        tmem_ld32(tb + 96, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
-        tmem_wait_ld();
-        uint32_t pp[32], dd[32];
-        p_ds_64(sr, dr, c, [&](int) { return l2; }, [&](int) { return dsum; }, [&](int col) { return col < lim; }, pp,
-                dd);
-        tmem_st32(tb, dd);
-        tmem_wait_st();
-        warp_arrive_after_tc(&bar->p_full[x]);
-      }
-      if (!ok) break;
-      if (!(ok = mbar_wait(&bar->o_full, nqd & 1, abort, p.err))) break;
-      tc_fence_after();
-      // each warpgroup writes half of the dQ columns
-      store_cols_bf16<D / 2>(tmem + lane_off + 256 + x * (D / 2), p.scale, dq + x * (D / 2), t < p.T,
-                             p.ncols0 - x * (D / 2));
-      warp_arrive_after_tc(&bar->acc_free);
-      gi += n_kv;
-      ++nqd;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-  grid_dep_wait();  // complete only after the dK/dV grid this one overlapped has completed
-}
-
 // dK / dV with 128-query items.  Unit = 128 keys of one (batch, KV head);
 // items = (query head of the group, 128-row query tile), so the score MMAs
 // run at N = 128.  TMEM: two 128-column slots take turns -- S^T of item g in
@@ -1867,7 +1397,7 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
         D == 64 ? reinterpret_cast<float*>(ws + w.dqacc) : nullptr);
     if (int st = cuda_status(cudaGetLastError(), "bwd prep launch")) return st;
   }
-  // dK/dV kernel: 64-row query tiles, 128-key blocks; dQ kernel: 128-row query blocks, 64-key tiles
+  // 128-row boxes for every operand: 128-key / 128-row units and 128-wide items in both D = 128 passes
   CUtensorMap tk128, tv128, tq128, tdo128;
   // the maps carry the true head dims (e for q / k, e_v for v / dO): features between
   // them and D are zero-filled, so they add nothing to the scores or the gradients
@@ -1890,12 +1420,6 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
   p.scale_log2 = (float)(d.scale * 1.4426950408889634);
   p.B = (int)d.batch;
   p.err = device_error_flag();
-  // the kernels are persistent (one CTA per SM); >= 120 KB of shared memory also keeps a
-  // second CTA of another launch off the SM while the 512-column TMEM allocation is held
-  const int need_kv = 2 * (128 * D * 2) + kStages * 2 * (QT * D * 2) + kStages * 2 * QT * 4 + 256 + 1024;
-  const int need_q = 2 * (128 * D * 2) + kStages * 2 * (KT * D * 2) + 256 + 1024;
-  const int smem_kv = need_kv > 120 * 1024 ? need_kv : 120 * 1024;
-  const int smem_q = need_q > 120 * 1024 ? need_q : 120 * 1024;
   if constexpr (D == 64) {  // one fused pass for dK, dV and dQ, then dQ scaled and rounded
     float* dqacc = reinterpret_cast<float*>(ws + w.dqacc);
     CUtensorMap tdq;
@@ -1934,11 +1458,6 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
     if (e != cudaSuccess) return cuda_status(e, "bwd dq convert launch");
     return PDB_OK;
   } else {
-    CUtensorMap tq64, tdo64, tk64, tv64;  // 64-row boxes: dK/dV query items, dQ key items
-    if (int st = map_bf16(&tq64, d.q, E, d.seqlen_q, d.heads_q, d.batch, d.q_stride, QT)) return st;
-    if (int st = map_bf16(&tdo64, d.dout, EV, d.seqlen_q, d.heads_q, d.batch, d.do_stride, QT)) return st;
-    if (int st = map_bf16(&tk64, d.k, E, d.seqlen_k, d.heads_kv, d.batch, d.k_stride, KT)) return st;
-    if (int st = map_bf16(&tv64, d.v, EV, d.seqlen_k, d.heads_kv, d.batch, d.v_stride, KT)) return st;
     {  // dK, dV
       p.out0 = d.dk;
       p.out1 = d.dv;
@@ -1953,18 +1472,10 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       {
         p.ctr = ctr;
         const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-        cudaError_t e;
-        static const bool old_kv = getenv("PDB_BWD_DKDV64") != nullptr;
-        if (old_kv) {
-          e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
-          if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
-          e = launch_overlapped(bwd_dkdv_kernel<D>, pgrid, kThreads, smem_kv, stream, tq64, tk128, tv128, tdo64, p);
-        } else {
-          e = cudaFuncSetAttribute(bwd_dkdv128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
-          if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
-          e = launch_overlapped(bwd_dkdv128_kernel, pgrid, kThreads, kMaxDynSmem, stream, tq128, tk128, tv128, tdo128,
-                                p);
-        }
+        cudaError_t e = cudaFuncSetAttribute(bwd_dkdv128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kMaxDynSmem);
+        if (e != cudaSuccess) return cuda_status(e, "bwd dkdv smem attribute");
+        e = launch_overlapped(bwd_dkdv128_kernel, pgrid, kThreads, kMaxDynSmem, stream, tq128, tk128, tv128, tdo128, p);
         if (e != cudaSuccess) return cuda_status(e, "bwd dkdv launch");
       }
       if (int st = cuda_status(cudaGetLastError(), "bwd dkdv launch")) return st;
@@ -1980,18 +1491,10 @@ int launch_bwd(const pdb_flash_bwd_desc& d, const float* lse, const WsLayout& w,
       {
         p.ctr = ctr;
         const int64_t pgrid = grid < sm_count(dev) ? grid : sm_count(dev);
-        cudaError_t e;
-        static const bool old_dq = getenv("PDB_BWD_DQ64") != nullptr;
-        if (old_dq) {
-          e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
-          if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
-          e = launch_overlapped(bwd_dq_kernel<D>, pgrid, kThreads, smem_q, stream, tq128, tk64, tv64, tdo128, p);
-        } else {
-          const int smem = kDq128Smem + (int)sizeof(BarsQ) + 1024;
-          e = cudaFuncSetAttribute(bwd_dq128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-          if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
-          e = launch_overlapped(bwd_dq128_kernel, pgrid, kThreads, smem, stream, tq128, tk128, tv128, tdo128, p);
-        }
+        const int smem = kDq128Smem + (int)sizeof(BarsQ) + 1024;
+        cudaError_t e = cudaFuncSetAttribute(bwd_dq128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return cuda_status(e, "bwd dq smem attribute");
+        e = launch_overlapped(bwd_dq128_kernel, pgrid, kThreads, smem, stream, tq128, tk128, tv128, tdo128, p);
         if (e != cudaSuccess) return cuda_status(e, "bwd dq launch");
       }
       if (int st = cuda_status(cudaGetLastError(), "bwd dq launch")) return st;
