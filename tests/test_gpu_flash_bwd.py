@@ -37,7 +37,9 @@ def test_bwd_matches_autodiff_joint(cuda, stored_lse):
     kernels.check_device_errors()
     # The reference's region has no score scale, so the fixture draws q at 1/sqrt(E) (unit-variance
     # scores) and its dq is exactly 8x the dq of the same program spelled with a 1/sqrt(E) scale on
-    # unit-variance q.  The bf16 bar (2e-2) is on that unit-scale gradient, i.e. on dq / 8 here; the
+    # unit-variance q: max |dq| is ~14 here, where bf16 values are 2^-4 apart, so rounding the
+    # output alone can miss by 0.031 and no bf16 result meets 2e-2 flat (measured on B200: 0.061).
+    # The bf16 bar (2e-2) is on that unit-scale gradient, i.e. on dq / 8 here; the
     # scaled-region tests (test_gpu_grad.py, test_bwd_shapes_vs_oracle) apply it to dq flat.
     qs = 1.0 / 8.0
     assert_bf16(_np(gq) * qs, dq * qs, what="dq (unit-scale program)")
