@@ -25,12 +25,7 @@
 // the running max used for the exponent only moves when a tile's max exceeds
 // it by more than 8 (a factor 256), so most tiles need no O correction; the
 // true max is tracked on the side for the m / den / lse outputs.
-#include <algorithm>
 #include <cfloat>
-#include <functional>
-#include <queue>
-#include <utility>
-#include <vector>
 
 #include "common.cuh"
 #include "tma.h"
@@ -43,8 +38,6 @@ constexpr int BN = 128;          // keys per tile
 constexpr int kThreads = 384;    // 3 warpgroups
 constexpr int kBoxBytes = 64 * 128 * 2;  // one TMA box: 128 rows x 64 bf16 (128 B, swizzled)
 constexpr float kRescaleThreshold = 8.0f;
-constexpr int kMaxLptCtas = 160;    // >= the SM count of the part
-constexpr int kMaxLptTiles = 1200;  // >= 8 x SMs: the small-job schedule's largest tile count
 
 struct __align__(8) Barriers {
   uint64_t q_full, q_empty;
@@ -71,15 +64,11 @@ struct FwdParams {
   const int32_t* key_lo;  // per-row key intervals (general closed masks) or null
   const int32_t* key_hi;
   int mask_monotone;
-  int lpt;          // 0: head-major pairs; 1: heaviest-first snake; 2: the host's LPT table below
+  int lpt;          // heaviest-first snake schedule (else head-major pairs)
   int DV;           // the value / output head dim (<= the kernel's D; the TMA maps zero-fill the rest)
   int num_mblocks;  // 256-row blocks per head
   float scale_log2;  // scale * log2(e)
   int* err;
-  // lpt == 2: CTA c walks tiles lpt_tile[lpt_start[c] .. lpt_start[c + 1]) (tile ids of the
-  // snake numbering), dealt by the host longest-processing-time first with exact tile costs
-  uint16_t lpt_start[kMaxLptCtas + 1];
-  uint16_t lpt_tile[kMaxLptTiles];
 };
 
 template <int D>
@@ -157,18 +146,9 @@ __device__ __forceinline__ void exp_chunk(const uint32_t* sr, uint64_t c2, uint6
 //   to the first, and CTA c takes ordinals c, 2G-1-c, 2G+c, ... (G CTAs), the
 //   longest-processing-time-first rule dealt in a boustrophedon.  The K/V of
 //   all heads of such a job fit in L2, so the head-major order buys nothing.
-// * LPT table (small causal jobs): the snake's greedy is approximate (its busiest
-//   CTA carries ~5 % above the mean at 32 heads x 16 row blocks); the host deals
-//   the tiles by true longest-processing-time first on their key-tile counts and
-//   passes each CTA's list in the kernel parameters.
-template <class P>
-__device__ __forceinline__ int kth_tile(int k, int num_tiles, const P& p) {
-  const int lpt = p.lpt;
+__device__ __forceinline__ int kth_tile(int k, int num_tiles, int lpt) {
   int t;
-  if (lpt == 2) {
-    const int i = (int)p.lpt_start[blockIdx.x] + k;
-    return i < (int)p.lpt_start[blockIdx.x + 1] ? (int)p.lpt_tile[i] : -1;
-  } else if (lpt) {
+  if (lpt) {
     const int G = gridDim.x;
     t = k * G + ((k & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
   } else {
@@ -225,7 +205,7 @@ template <int D, bool kKeyMask>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                           const __grid_constant__ FwdParams p) {
+                           const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using L = Smem<D>;
@@ -275,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tm_k);
       prefetch_tensormap(&tm_v);
       uint32_t g = 0, tt = 0;  // K/V tiles loaded, tiles started
-      for (int k = 0, tile = kth_tile(0, num_tiles, p); tile >= 0; tile = kth_tile(++k, num_tiles, p), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info(tile, p);
         if (!mbar_wait(&bar->q_empty, (tt & 1) ^ 1, abort, p.err)) break;
         mbar_expect_tx(&bar->q_full, 2 * L::kTileBytes);
@@ -306,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
       uint32_t g = 0, tt = 0, cs[2] = {0, 0};  // K/V tiles consumed, tiles, P tiles consumed per x
       bool ok = true;
-      for (int k = 0, tile = kth_tile(0, num_tiles, p); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info(tile, p);
         if (!(ok = mbar_wait(&bar->q_full, tt & 1, abort, p.err))) break;
         if (!(ok = mbar_wait(&bar->k_full[g & 1], (g >> 1) & 1, abort, p.err))) break;
@@ -368,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c = p.scale_log2;
     uint32_t cs = 0, tt = 0;
     bool ok = true;
-    for (int k = 0, tile = kth_tile(0, num_tiles, p); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p), ++tt) {
+    for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
       const TileInfo ti = tile_info(tile, p);
       const int t = ti.t0 + x * BM + row;  // query row
       const int n = x ? ti.nB : ti.nA;
@@ -548,7 +528,7 @@ struct __align__(8) BarriersD64 {
 template <bool kKeyMask>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_d64_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ FwdParams p) {
+                         const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
   constexpr int D = 64;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -595,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tm_k);
       uint32_t gk = 0, tt = 0;
       bool ok = true;
-      for (int k = 0, tile = kth_tile(0, num_tiles, p); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info(tile, p);
         if (!(ok = mbar_wait(&bar->q_empty, (tt & 1) ^ 1, abort, p.err))) break;
         mbar_expect_tx(&bar->q_full, 2 * L::kTileBytes);
@@ -613,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tm_v);
       uint32_t gv = 0;
       bool ok = true;
-      for (int k = 0, tile = kth_tile(0, num_tiles, p); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p)) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt)) {
         const TileInfo ti = tile_info(tile, p);
         for (int j = 0; j < ti.nB; ++j, ++gv) {
           const int st = gv & 1;
@@ -636,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++nqk[x];
         return true;
       };
-      for (int k = 0, tile = kth_tile(0, num_tiles, p); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info(tile, p);
         if (!(ok = mbar_wait(&bar->q_full, tt & 1, abort, p.err))) break;
         for (int j = 0; ok && j < ti.nB; ++j) {
@@ -654,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tP[2] = {tmem + 384, tmem + 448};
       uint32_t gv = 0, tt = 0, npf[2] = {0, 0};
       bool ok = true;
-      for (int k = 0, tile = kth_tile(0, num_tiles, p); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info(tile, p);
         for (int j = 0; ok && j < ti.nB; ++j) {
           const int st = gv & 1;
@@ -688,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c = p.scale_log2;
     uint32_t cs = 0, tt = 0, pw = 0;  // S tiles read, work tiles, P tiles written
     bool ok = true;
-    for (int k = 0, tile = kth_tile(0, num_tiles, p); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p), ++tt) {
+    for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0; tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
       const TileInfo ti = tile_info(tile, p);
       const int t = ti.t0 + x * BM + row;
       const int n = x ? ti.nB : ti.nA;
@@ -814,66 +794,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Longest-processing-time-first deal of the small causal job's tiles over `grid`
-// CTAs: tiles sorted by cost (key tiles of rows A and B, plus one step of
-// per-tile overhead), each to the CTA with the least work so far; ties go to
-// the lower tile id / CTA.  The tile ids and costs follow tile_info's snake
-// numbering (bh = tile % (H B), row block = num_mblocks - 1 - tile / (H B)).
-// The deal depends only on the shape, so the last one is reused.
-void lpt_table(FwdParams& p, int grid) {
-  struct Key {
-    int nbh, nmb, T, S, q_start, grid;
-    bool operator==(const Key& o) const {
-      return nbh == o.nbh && nmb == o.nmb && T == o.T && S == o.S && q_start == o.q_start && grid == o.grid;
-    }
-  };
-  static thread_local Key last{-1, -1, -1, -1, -1, -1};
-  static thread_local std::vector<uint16_t> start, tiles;
-  const Key key{p.H * p.B, p.num_mblocks, p.T, p.S, p.q_start, grid};
-  if (!(key == last)) {
-    const int nbh = key.nbh, ntile = nbh * p.num_mblocks, n_kv = (p.S + BN - 1) / BN;
-    auto cost_of_block = [&](int mblk) {
-      int n[2];
-      for (int x = 0; x < 2; ++x) {
-        int last_row = mblk * 2 * BM + x * BM + BM - 1;
-        if (last_row > p.T - 1) last_row = p.T - 1;
-        int c = (last_row + p.q_start) / BN + 1;
-        c = c < n_kv ? c : n_kv;
-        n[x] = c > 1 ? c : 1;
-      }
-      return n[0] + (n[1] < n[0] ? n[0] : n[1]) + 2;
-    };
-    // tile ids in descending cost: the snake numbering already runs heaviest block first
-    std::vector<int> order(ntile);
-    for (int t = 0; t < ntile; ++t) order[t] = t;
-    std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
-      return cost_of_block(p.num_mblocks - 1 - a / nbh) > cost_of_block(p.num_mblocks - 1 - b / nbh);
-    });
-    using Load = std::pair<int64_t, int>;
-    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
-    for (int c = 0; c < grid; ++c) heap.push({0, c});
-    std::vector<std::vector<uint16_t>> per(grid);
-    for (int t : order) {
-      Load l = heap.top();
-      heap.pop();
-      per[l.second].push_back((uint16_t)t);
-      l.first += cost_of_block(p.num_mblocks - 1 - t / nbh);
-      heap.push(l);
-    }
-    start.assign(grid + 1, 0);
-    tiles.clear();
-    for (int c = 0; c < grid; ++c) {
-      start[c] = (uint16_t)tiles.size();
-      tiles.insert(tiles.end(), per[c].begin(), per[c].end());
-    }
-    start[grid] = (uint16_t)tiles.size();
-    last = key;
-  }
-  std::copy(start.begin(), start.end(), p.lpt_start);
-  std::copy(tiles.begin(), tiles.end(), p.lpt_tile);
-  p.lpt = 2;
-}
-
 template <int D>
 int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   CUtensorMap tq, tk, tv;
@@ -928,7 +848,6 @@ int launch(const pdb_flash_desc& d, cudaStream_t stream) {
   p.lpt = pairs < 4 * (int64_t)sms ? 1 : 0;
   const int64_t units = p.lpt ? nblk : pairs;
   const int64_t grid = units < sms ? units : sms;  // persistent: one CTA per SM
-  if (p.lpt && p.causal && !p.key_lo && nblk <= kMaxLptTiles && grid <= kMaxLptCtas) lpt_table(p, (int)grid);
   const int smem = Smem<D>::kTotal;
   if constexpr (D == 64) {  // P in its own TMEM columns (656 vs 610 TFLOP/s at B8 H32 S4096 causal)
     auto kern = p.key_lo ? flash_fwd_d64_kernel<true> : flash_fwd_d64_kernel<false>;
@@ -1021,7 +940,7 @@ __device__ __forceinline__ TileInfo tile_info128(int tile, const FwdParams& p) {
 template <bool kKeyMask>
 __global__ void __launch_bounds__(kThreads256, 1)
     flash_fwd_d256_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ FwdParams p) {
+                          const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
   constexpr int D = 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1076,8 +995,8 @@ __global__ void __launch_bounds__(kThreads256, 1)
         return true;
       };
       bool ok = true;
-      for (int k = 0, tile = kth_tile(0, num_tiles, p); ok && tile >= 0;
-           tile = kth_tile(++k, num_tiles, p), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0;
+           tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info128(tile, p);
         if (!(ok = mbar_wait(&bar->q_empty, (tt & 1) ^ 1, abort, p.err))) break;
         mbar_expect_tx(&bar->q_full, 4 * kBoxBytes);
@@ -1139,8 +1058,8 @@ __global__ void __launch_bounds__(kThreads256, 1)
         return true;
       };
       bool ok = true;
-      for (int k = 0, tile = kth_tile(0, num_tiles, p); ok && tile >= 0;
-           tile = kth_tile(++k, num_tiles, p), ++tt) {
+      for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0;
+           tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
         const TileInfo ti = tile_info128(tile, p);
         const int n = ti.nA;
         if (!(ok = mbar_wait(&bar->q_full, tt & 1, abort, p.err))) break;
@@ -1171,8 +1090,8 @@ __global__ void __launch_bounds__(kThreads256, 1)
     const float c = p.scale_log2;
     uint32_t gs = 0, tt = 0;  // score tiles read, work tiles
     bool ok = true;
-    for (int k = 0, tile = kth_tile(0, num_tiles, p); ok && tile >= 0;
-         tile = kth_tile(++k, num_tiles, p), ++tt) {
+    for (int k = 0, tile = kth_tile(0, num_tiles, p.lpt); ok && tile >= 0;
+         tile = kth_tile(++k, num_tiles, p.lpt), ++tt) {
       const TileInfo ti = tile_info128(tile, p);
       const int t = ti.t0 + row;
       const int n = ti.nA;
