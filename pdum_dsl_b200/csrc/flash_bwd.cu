@@ -162,8 +162,10 @@ __device__ __forceinline__ int take_unit(UnitQueue* uq, uint32_t n, volatile int
 // next item, and writes dS^T = P^T (dP^T - D) to shared memory (K-major,
 // 128-byte swizzle), the A operand of dK += dS^T Q.  Per item the MMA issuer
 // sends
-//   S^T(g+1) [once dP^T(g) is in registers], dK(g) [after dS^T(g)],
-//   dV(g) [after P^T(g)], dP^T(g+1) [into the slot dV(g) read, behind it]
+//   dV(g) [after P^T(g)], S^T(g+1) [once dP^T(g) is in registers],
+//   dK(g) [after dS^T(g)], dP^T(g+1) [into the slot dV(g) read, behind it]
+// dV(g) keeps the tensor core busy while the compute warps take dP^T(g) into
+// registers, the hand-off the next score MMA waits for.
 // so the next item's scores are formed while this item's gradients are.
 // Q / dO (and the per-query nlse2 / D) pass through two stages each; Q is
 // released by dK, dO by dV.
@@ -338,25 +340,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int it = 0; ok && it < n_items; ++it) {
           const uint32_t g = gi + it;
           const int st = g & 1;
-          if (it + 1 < n_items && !(ok = issue_st(it + 1))) break;
-          if (!(ok = mbar_wait(&bar->ds_full[st], (g >> 1) & 1, abort, p.err))) break;
+          // dV(g) first: it needs only phase 1, so it runs while the compute warps take dP^T(g)
+          // into registers and the next score MMA waits for that slot
+          if (!(ok = mbar_wait(&bar->pt_full[st], (g >> 1) & 1, abort, p.err))) break;
           if (it == 0 && nkv > 0 && !(ok = mbar_wait(&bar->acc_free, (nkv - 1) & 1, abort, p.err))) break;
           tc_fence_after();
           const uint32_t bq = smem_u32(sQ + st * kT), bdo = smem_u32(sDO + st * kT), ads = smem_u32(sDS);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
-            mma_ss(tmem + kDK, sdesc_sw128(ads + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024),
-                   sdesc_sw128(bq + kk * 2048, kBox, 1024), idG, (it > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(&bar->q_empty[st]);
-          tc_commit(&bar->ds_free);
-          if (!(ok = mbar_wait(&bar->pt_full[st], (g >> 1) & 1, abort, p.err))) break;
-          tc_fence_after();
           const uint32_t a = tmem + st * 128;  // P^T of queries [0, 64) in columns [0, 32), [64, 128) in [64, 96)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO
             mma_ts(tmem + kDV, a + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_sw128(bdo + kk * 2048, kBox, 1024), idG,
                    (it > 0 || kk > 0) ? 1u : 0u);
           tc_commit(&bar->do_empty[st]);
+          if (it + 1 < n_items && !(ok = issue_st(it + 1))) break;
+          if (!(ok = mbar_wait(&bar->ds_full[st], (g >> 1) & 1, abort, p.err))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
+            mma_ss(tmem + kDK, sdesc_sw128(ads + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024),
+                   sdesc_sw128(bq + kk * 2048, kBox, 1024), idG, (it > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&bar->q_empty[st]);
+          tc_commit(&bar->ds_free);
           if (it + 1 < n_items && !(ok = issue_dpt(it + 1))) break;
         }
         if (!ok) break;
