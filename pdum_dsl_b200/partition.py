@@ -248,3 +248,70 @@ def gather_overlapped(attend, slabs_in, slabs_out, *, group=None, comm_stream=No
     if comm_stream is not None:
         cur.wait_stream(comm_stream)
     return blocks
+
+
+class PeerGather:
+    """The final gather by copy engines over NVLink, without NCCL kernels.
+
+    The global output lives in symmetric memory (``torch.distributed._symmetric_memory``):
+    every rank's buffer is mapped into every other rank's address space. When a
+    block of rows of the output is final on this rank, ``push(lo, hi)`` copies it
+    into the same rows of every peer's buffer, one ``cudaMemcpyAsync`` per peer on
+    its own side stream (copy engines: no SMs taken from the forward, which
+    keeps all of them); ``finish()`` joins the side streams and runs a one-word
+    NCCL all-reduce on the current stream, which completes on a rank only once
+    every rank has reached it, i.e. once every push into this rank's buffer has
+    completed. The all-gather is the one of ``placement.traffic`` (each rank
+    receives (p-1)/p of the output); only the transport differs from
+    ``all_gather_into_tensor``. Loads of peer memory: none (the copies write to
+    the peers); no multicast.
+    """
+
+    def __init__(self, shape, dtype, device, group=None):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        grp = group if group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(grp)
+        self.world = dist.get_world_size(grp)
+        self.group = grp
+        self.full = symm_mem.empty(tuple(shape), dtype=dtype, device=device)
+        self._hdl = symm_mem.rendezvous(self.full, grp.group_name)
+        self.peers = [self._hdl.get_buffer(p, tuple(shape), dtype) for p in range(self.world) if p != self.rank]
+        self.streams = [torch.cuda.Stream(device) for _ in self.peers]
+        self._flag = torch.zeros(1, device=device)
+
+    def push(self, lo: int, hi: int) -> None:
+        """Copy rows [lo, hi) of this rank's buffer to every peer, after the work
+        already queued on the current stream."""
+        import torch
+
+        cur = torch.cuda.current_stream(self.full.device)
+        src = self.full[lo:hi]
+        for s, peer in zip(self.streams, self.peers):
+            s.wait_stream(cur)
+            with torch.cuda.stream(s):
+                peer[lo:hi].copy_(src, non_blocking=True)
+
+    def finish(self) -> None:
+        """Every rank's pushes into every buffer are complete once this returns on
+        the current stream (stream-ordered; the host does not wait)."""
+        import torch
+        import torch.distributed as dist
+
+        cur = torch.cuda.current_stream(self.full.device)
+        for s in self.streams:
+            cur.wait_stream(s)
+        dist.all_reduce(self._flag, group=self.group)
+
+
+def peer_gather_overlapped(attend, slabs_in, slab_rows, pg: PeerGather):
+    """For each slab: ``attend(*slabs_in[c], out)`` writes this rank's block of the
+    slab straight into ``pg.full[slab_rows[c]]``, then ``pg.push`` sends it to
+    every peer while the next slab computes; ``pg.finish`` closes the step."""
+    for ins, (lo, hi) in zip(slabs_in, slab_rows):
+        attend(*ins, pg.full[lo:hi])
+        pg.push(lo, hi)
+    pg.finish()
+    return pg.full
