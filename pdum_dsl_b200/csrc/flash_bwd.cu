@@ -18,8 +18,8 @@
 //   bwd_dkdv128  per (batch, KV head, 128-key block): for every 128-row query
 //                tile of every query head of the group it forms S^T = K Q^T
 //                and dP^T = V dO^T in TMEM, P^T = exp2(S^T c + nlse2) (bf16,
-//                back to TMEM), dS^T = P^T (dP^T - D) (bf16, to shared
-//                memory; one thread per key row) and accumulates dV += P^T dO,
+//                back to TMEM), dS^T = P^T (dP^T - D) (bf16, beside P^T in
+//                TMEM; one thread per key row) and accumulates dV += P^T dO,
 //                dK += dS^T Q in TMEM; GQA sums over the group in place.
 //   bwd_dq128    per (batch, head, 128-row block): S = Q K^T, dP = dO V^T,
 //                dS = P (dP - D), dQ += dS K over 128-key tiles.
@@ -159,14 +159,15 @@ __device__ __forceinline__ int take_unit(UnitQueue* uq, uint32_t n, volatile int
 // [64x, 64x+64)).  Phase 1 forms P^T = exp2(S^T c + nlse2) and writes it
 // (bf16 pairs) into its own first 32 columns of the S^T slot, the A operand of
 // dV += P^T dO; phase 2 reads dP^T, whose slot is then free for S^T of the
-// next item, and writes dS^T = P^T (dP^T - D) to shared memory (K-major,
-// 128-byte swizzle), the A operand of dK += dS^T Q.  Per item the MMA issuer
-// sends
+// next item, and writes dS^T = P^T (dP^T - D) (bf16 pairs) into its other 32
+// columns of the S^T slot, the A operand of dK += dS^T Q (both gradient MMAs
+// take A from TMEM; dS^T in shared memory instead measured 0.5-1 % slower).
+// Per item the MMA issuer sends
 //   dV(g) [after P^T(g)], S^T(g+1) [once dP^T(g) is in registers],
 //   dK(g) [after dS^T(g)], dP^T(g+1) [into the slot dV(g) read, behind it]
 // dV(g) keeps the tensor core busy while the compute warps take dP^T(g) into
-// registers, the hand-off the next score MMA waits for.
-// so the next item's scores are formed while this item's gradients are.
+// registers, the hand-off the next score MMA waits for, and the next item's
+// scores are formed while this item's gradients are.
 // Q / dO (and the per-query nlse2 / D) pass through two stages each; Q is
 // released by dK, dO by dV.
 struct __align__(8) BarsK {
@@ -176,15 +177,14 @@ struct __align__(8) BarsK {
   uint64_t st_full[2], dpt_full[2];  // S^T(g), dP^T(g) complete
   uint64_t dp_free[2];               // dP^T(g) in registers (its slot may take S^T(g+1))
   uint64_t pt_full[2];               // P^T(g) written to TMEM
-  uint64_t ds_full[2];               // dS^T(g) written to shared memory
-  uint64_t ds_free;                  // dK(g) complete: the dS^T buffer may be rewritten
+  uint64_t ds_full[2];               // dS^T(g) written to TMEM
   uint64_t o_full, acc_free;
   UnitQueue uq;
   uint32_t tmem_base;
   int abort;
 };
 
-constexpr int kKv128Tiles = 32768 * 7;                    // K, V, Q x 2, dO x 2, dS^T
+constexpr int kKv128Tiles = 32768 * 6;                    // K, V, Q x 2, dO x 2
 constexpr int kKv128Smem = kKv128Tiles + 2 * 256 * 4 + (int)sizeof(BarsK);  // + nlse2 / D per stage + barriers
 constexpr int kMaxDynSmem = 227 * 1024;
 
@@ -207,7 +207,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + kT;
   uint8_t* sQ = smem + 2 * kT;   // 2 stages
   uint8_t* sDO = smem + 4 * kT;  // 2 stages
-  uint8_t* sDS = smem + 6 * kT;
   float* sVec = reinterpret_cast<float*>(smem + kKv128Tiles);  // per stage: nlse2[128], dsum[128]
   BarsK* bar = reinterpret_cast<BarsK*>(smem + kKv128Tiles + 2 * 256 * 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -244,7 +243,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->uq.full[i], 1);
       mbar_init(&bar->uq.empty[i], 9);  // the MMA thread + 8 compute warps
     }
-    mbar_init(&bar->ds_free, 1);
     mbar_init(&bar->o_full, 1);
     mbar_init(&bar->acc_free, 8);
     bar->abort = 0;
@@ -345,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = mbar_wait(&bar->pt_full[st], (g >> 1) & 1, abort, p.err))) break;
           if (it == 0 && nkv > 0 && !(ok = mbar_wait(&bar->acc_free, (nkv - 1) & 1, abort, p.err))) break;
           tc_fence_after();
-          const uint32_t bq = smem_u32(sQ + st * kT), bdo = smem_u32(sDO + st * kT), ads = smem_u32(sDS);
+          const uint32_t bq = smem_u32(sQ + st * kT), bdo = smem_u32(sDO + st * kT);
           const uint32_t a = tmem + st * 128;  // P^T of queries [0, 64) in columns [0, 32), [64, 128) in [64, 96)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO
@@ -356,11 +354,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = mbar_wait(&bar->ds_full[st], (g >> 1) & 1, abort, p.err))) break;
           tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
-            mma_ss(tmem + kDK, sdesc_sw128(ads + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024),
-                   sdesc_sw128(bq + kk * 2048, kBox, 1024), idG, (it > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q, dS^T beside P^T in the slot
+            mma_ts(tmem + kDK, a + (kk >> 2) * 64 + 32 + (kk & 3) * 8, sdesc_sw128(bq + kk * 2048, kBox, 1024), idG,
+                   (it > 0 || kk > 0) ? 1u : 0u);
           tc_commit(&bar->q_empty[st]);
-          tc_commit(&bar->ds_free);
           if (it + 1 < n_items && !(ok = issue_dpt(it + 1))) break;
         }
         if (!ok) break;
@@ -376,7 +373,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q4 * 32 + lane;  // key row within the block (TMEM lane)
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
-    const uint32_t ds_row = smem_u32(sDS + x * kBox + row * 128);
     uint32_t gi = 0, nu = 0, nkv = 0;
     bool ok = true;
     for (;; ++nu) {
@@ -429,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
           warp_arrive_after_tc(&bar->pt_full[st]);
         }
-        // phase 2: dS^T = P^T (dP^T - D) to shared memory
+        // phase 2: dS^T = P^T (dP^T - D) to TMEM
         if (!(ok = mbar_wait(&bar->dpt_full[st], ph, abort, p.err))) break;
         tc_fence_after();
         uint32_t dr[64];
@@ -455,13 +451,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             dd[2 * q + h2] = pack_bf16(g0, g1);
           }
         }
-        if (g > 0 && !(ok = mbar_wait(&bar->ds_free, (g - 1) & 1, abort, p.err))) break;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch)  // 128-byte swizzled row of 64 queries for key `row`
-          sts128(ds_row + ((ch ^ (row & 7)) << 4), dd[4 * ch], dd[4 * ch + 1], dd[4 * ch + 2], dd[4 * ch + 3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar->ds_full[st]);
+        tmem_st32(tmem + lane_off + st * 128 + x * 64 + 32, dd);  // its other 32 columns of the S^T slot
+        tmem_wait_st();
+        warp_arrive_after_tc(&bar->ds_full[st]);
       }
       if (!ok) break;
       const bool store = s < p.S;
