@@ -669,6 +669,22 @@ def _bwd(out, kernels, dev, stream, g, peaks=None, cpu=True):
             if peaks:
                 out[name]["roofline"] = {"bound": "tensor", "frac": tf / peaks["bf16_tflops"],
                                          "peak": peaks["bf16_tflops"], "peak_source": peaks["source"] + " (burst)"}
+            try:  # the same backward through torch's SDPA (its fused backward kernels), as a labelled bar
+                import math
+
+                import torch.nn.functional as F
+
+                qg, kg, vg = (x.detach().requires_grad_() for x in (q, k, v))
+                og = F.scaled_dot_product_attention(qg, kg, vg, is_causal=True, scale=1 / math.sqrt(Db))
+                _, per_b = _timed(lambda: torch.autograd.grad(og, (qg, kg, vg), do, retain_graph=True), 20, 3,
+                                  stream, 1)
+                tf_b = fl / (sum(per_b) / len(per_b) * 1e-3) / 1e12
+                out[name]["bar_torch_sdpa_bwd"] = {
+                    "TFLOP/s": tf_b, "ours_over_bar": tf / tf_b,
+                    "call": "torch.autograd.grad of F.scaled_dot_product_attention(is_causal=True), bf16"}
+                del qg, kg, vg, og
+            except Exception as e:
+                out[name]["bar_torch_sdpa_bwd"] = {"error": str(e)[:200]}
             if cpu and Db == 64:
                 from oracle import attention as OA
 
